@@ -1,0 +1,353 @@
+// abi.cu — the extern "C" surface declared in include/obn.h.
+//
+// Host-side BitLinear: validation, the one-time repack of I2_S weights into the
+// T256 device layout (layout.cuh), workspace partitioning and kernel dispatch.
+// Error handling follows the reference's C ABI: a status return plus a
+// thread-local message (packages/rust/crates/oxbitnet-ffi/src/lib.rs:31-46).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/obn.h"
+#include "gemm.h"
+#include "kernels.h"
+#include "layout.cuh"
+
+struct obn_bitlinear {
+  int device = 0;
+  int in_dim = 0;   // K
+  int out_dim = 0;  // M
+  int m_pad = 0;
+  float eps = 1e-5f;
+  uint8_t* w = nullptr;     // T256 layout, m_pad * K / 4 bytes
+  float* s_w = nullptr;     // [m_pad]
+  float* norm = nullptr;    // [K] or null
+};
+
+namespace {
+
+thread_local std::string g_error;
+thread_local bool g_has_error = false;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  g_has_error = true;
+  return code;
+}
+
+void clear_error() { g_has_error = false; }
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(OBN_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+int check_device(int dev) {
+  int count = 0;
+  cudaError_t e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0)
+    return fail(OBN_ERR_NO_DEVICE, "no CUDA device available (%s)",
+                e == cudaSuccess ? "count 0" : cudaGetErrorString(e));
+  if (dev < 0 || dev >= count) return fail(OBN_ERR_INVALID_ARGUMENT, "device %d out of range", dev);
+  int major = 0;
+  e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  if (major != 10)
+    return fail(OBN_ERR_NO_DEVICE, "device %d is sm_%d x; libobn is built for sm_100a only", dev,
+                major);
+  return OBN_OK;
+}
+
+int check_dims(int in_dim, int out_dim) {
+  if (in_dim <= 0 || out_dim <= 0)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "in_dim and out_dim must be positive (got %d, %d)",
+                in_dim, out_dim);
+  if (in_dim % obn::kBlockK != 0)
+    return fail(OBN_ERR_UNSUPPORTED,
+                "in_dim %d is not a multiple of 128 (the I2_S block interleave needs whole blocks)",
+                in_dim);
+  return OBN_OK;
+}
+
+obn::WeightView view(const obn_bitlinear* L) {
+  return obn::WeightView{L->w, L->s_w, L->in_dim, L->out_dim, L->m_pad};
+}
+
+void free_layer(obn_bitlinear* L) {
+  if (!L) return;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(L->device);
+  cudaFree(L->w);
+  cudaFree(L->s_w);
+  cudaFree(L->norm);
+  cudaSetDevice(prev);
+  delete L;
+}
+
+// Allocates the layer on the current device and fills its scale table
+// (scales_dev: device [out_dim] or null with host_scale used for every row).
+int alloc_layer(int in_dim, int out_dim, float eps, obn_bitlinear** out) {
+  auto* L = new obn_bitlinear;
+  cudaGetDevice(&L->device);
+  L->in_dim = in_dim;
+  L->out_dim = out_dim;
+  L->m_pad = obn::round_up(out_dim, obn::kPanelRows);
+  L->eps = eps;
+  const size_t wbytes = static_cast<size_t>(L->m_pad) * in_dim / 4;
+  cudaError_t e = cudaMalloc(&L->w, wbytes);
+  if (e == cudaSuccess) e = cudaMalloc(&L->s_w, sizeof(float) * L->m_pad);
+  if (e != cudaSuccess) {
+    free_layer(L);
+    cudaGetLastError();
+    return fail(OBN_ERR_OUT_OF_MEMORY, "cudaMalloc of %zu weight bytes failed", wbytes);
+  }
+  *out = L;
+  return OBN_OK;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+int check_layer(const obn_bitlinear* L) {
+  if (!L) return fail(OBN_ERR_INVALID_ARGUMENT, "layer is NULL");
+  return OBN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int obn_version(void) { return 100; }
+
+const char* obn_error_message(void) { return g_has_error ? g_error.c_str() : nullptr; }
+
+int obn_bitlinear_load_i2s(const uint8_t* i2s_tensor, size_t nbytes, int in_dim, int out_dim,
+                           const float* norm_weight, float eps, int device,
+                           obn_bitlinear** out_layer) {
+  clear_error();
+  if (!i2s_tensor || !out_layer) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  *out_layer = nullptr;
+  if (int rc = check_dims(in_dim, out_dim)) return rc;
+  const size_t packed = static_cast<size_t>(out_dim) * in_dim / 4;
+  if (nbytes < packed + 32)  // loader.rs:109-110: ceil(n/4) + 32 bytes
+    return fail(OBN_ERR_INVALID_ARGUMENT,
+                "I2_S tensor of %dx%d needs %zu bytes (packed + 32-byte scale), got %zu", out_dim,
+                in_dim, packed + 32, nbytes);
+  if (int rc = check_device(device)) return rc;
+  DeviceGuard g(device);
+  float scale;  // loader.rs:129-131: first f32 of the trailing 32 bytes
+  std::memcpy(&scale, i2s_tensor + packed, sizeof(float));
+
+  obn_bitlinear* L = nullptr;
+  if (int rc = alloc_layer(in_dim, out_dim, eps, &L)) return rc;
+  uint8_t* staging = nullptr;
+  cudaError_t e = cudaMalloc(&staging, packed);
+  if (e != cudaSuccess) {
+    free_layer(L);
+    cudaGetLastError();
+    return fail(OBN_ERR_OUT_OF_MEMORY, "cudaMalloc of %zu staging bytes failed", packed);
+  }
+  std::vector<float> table(L->m_pad, 0.0f);
+  for (int m = 0; m < out_dim; ++m) table[m] = scale;  // loader.rs:132-136 replication
+  e = cudaMemcpy(staging, i2s_tensor, packed, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = obn::launch_repack_i2s(staging, L->w, out_dim, in_dim, L->m_pad, 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(L->s_w, table.data(), sizeof(float) * L->m_pad, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && norm_weight) {
+    e = cudaMalloc(&L->norm, sizeof(float) * in_dim);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(L->norm, norm_weight, sizeof(float) * in_dim, cudaMemcpyHostToDevice);
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(staging);
+  if (e != cudaSuccess) {
+    free_layer(L);
+    return cuda_fail(e, "loading I2_S tensor");
+  }
+  *out_layer = L;
+  return OBN_OK;
+}
+
+int obn_bitlinear_create(const void* packed_dev, const float* scales_dev, const float* norm_dev,
+                         float eps, int in_dim, int out_dim, void* stream,
+                         obn_bitlinear** out_layer) {
+  clear_error();
+  if (!packed_dev || !scales_dev || !out_layer)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  *out_layer = nullptr;
+  if (int rc = check_dims(in_dim, out_dim)) return rc;
+  if (!aligned(packed_dev, 16))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "packed weights must be 16-byte aligned");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (int rc = check_device(dev)) return rc;
+  auto s = static_cast<cudaStream_t>(stream);
+  obn_bitlinear* L = nullptr;
+  if (int rc = alloc_layer(in_dim, out_dim, eps, &L)) return rc;
+  cudaError_t e = obn::launch_repack_i2s(static_cast<const uint8_t*>(packed_dev), L->w, out_dim,
+                                         in_dim, L->m_pad, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(L->s_w, 0, sizeof(float) * L->m_pad, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(L->s_w, scales_dev, sizeof(float) * out_dim, cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess && norm_dev) {
+    e = cudaMalloc(&L->norm, sizeof(float) * in_dim);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(L->norm, norm_dev, sizeof(float) * in_dim, cudaMemcpyDeviceToDevice, s);
+  }
+  if (e != cudaSuccess) {
+    free_layer(L);
+    return cuda_fail(e, "creating BitLinear");
+  }
+  *out_layer = L;
+  return OBN_OK;
+}
+
+void obn_bitlinear_free(obn_bitlinear* layer) { free_layer(layer); }
+
+int obn_bitlinear_in_dim(const obn_bitlinear* layer) { return layer ? layer->in_dim : 0; }
+int obn_bitlinear_out_dim(const obn_bitlinear* layer) { return layer ? layer->out_dim : 0; }
+
+size_t obn_bitlinear_workspace_bytes(const obn_bitlinear* layer, int n) {
+  if (!layer || n <= 0) return 0;
+  return align256(static_cast<size_t>(n) * layer->in_dim) + 2 * align256(sizeof(float) * n);
+}
+
+int obn_ternary_matmul(const obn_bitlinear* layer, const int8_t* q, const float* scales,
+                       const int32_t* qsum, int n, float* y, void* stream) {
+  clear_error();
+  if (int rc = check_layer(layer)) return rc;
+  if (!q || !scales || !qsum || !y) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (n <= 0) return fail(OBN_ERR_INVALID_ARGUMENT, "n must be positive (got %d)", n);
+  if (!aligned(q, 16)) return fail(OBN_ERR_INVALID_ARGUMENT, "q must be 16-byte aligned");
+  const int order = n == 1 ? obn::kOrderGemv : obn::kOrderGemm;
+  cudaError_t e;
+  if (obn::gemm_supported(view(layer), n))
+    e = obn::launch_gemm(view(layer), q, scales, qsum, n, y, nullptr, order,
+                         static_cast<cudaStream_t>(stream));
+  else if (layer->in_dim <= obn::kGemvMaxK)
+    e = obn::launch_gemv(view(layer), q, scales, qsum, n, y, nullptr, order,
+                         static_cast<cudaStream_t>(stream));
+  else
+    return fail(OBN_ERR_UNSUPPORTED, "in_dim %d exceeds the kernels' limit", layer->in_dim);
+  if (e != cudaSuccess) return cuda_fail(e, "ternary matmul launch");
+  return OBN_OK;
+}
+
+int obn_ternary_acc(const obn_bitlinear* layer, const int8_t* q, const int32_t* qsum, int n,
+                    int32_t* acc, void* stream) {
+  clear_error();
+  if (int rc = check_layer(layer)) return rc;
+  if (!q || !qsum || !acc) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (n <= 0) return fail(OBN_ERR_INVALID_ARGUMENT, "n must be positive (got %d)", n);
+  if (!aligned(q, 16)) return fail(OBN_ERR_INVALID_ARGUMENT, "q must be 16-byte aligned");
+  cudaError_t e;
+  if (obn::gemm_supported(view(layer), n))
+    e = obn::launch_gemm(view(layer), q, nullptr, qsum, n, nullptr, acc, obn::kOrderGemm,
+                         static_cast<cudaStream_t>(stream));
+  else if (layer->in_dim <= obn::kGemvMaxK)
+    e = obn::launch_gemv(view(layer), q, nullptr, qsum, n, nullptr, acc, obn::kOrderGemm,
+                         static_cast<cudaStream_t>(stream));
+  else
+    return fail(OBN_ERR_UNSUPPORTED, "in_dim %d exceeds the kernels' limit", layer->in_dim);
+  if (e != cudaSuccess) return cuda_fail(e, "ternary acc launch");
+  return OBN_OK;
+}
+
+int obn_rmsnorm_quantize(const float* x, const float* norm_weight, float eps, int n, int d,
+                         int8_t* q, float* scales, int32_t* qsum, void* stream) {
+  clear_error();
+  if (!x || !q || !scales) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (n <= 0 || d <= 0 || d % 4 != 0)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "need n > 0 and d > 0 with d %% 4 == 0 (got %d, %d)", n,
+                d);
+  if (!aligned(x, 16) || !aligned(q, 4) || (norm_weight && !aligned(norm_weight, 16)))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "x / norm_weight must be 16-byte and q 4-byte aligned");
+  cudaError_t e = obn::launch_rmsnorm_quant(x, norm_weight, eps, n, d, q, scales, qsum,
+                                            static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
+  return OBN_OK;
+}
+
+int obn_rmsnorm(const float* x, const float* w, float eps, int n, int d, float* y, void* stream) {
+  clear_error();
+  if (!x || !w || !y) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (n <= 0 || d <= 0) return fail(OBN_ERR_INVALID_ARGUMENT, "need n > 0 and d > 0");
+  cudaError_t e = obn::launch_rmsnorm(x, w, eps, n, d, y, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+  return OBN_OK;
+}
+
+int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, int n, float* y,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (int rc = check_layer(layer)) return rc;
+  if (!x || !y || !workspace) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (n <= 0) return fail(OBN_ERR_INVALID_ARGUMENT, "n must be positive (got %d)", n);
+  const size_t need = obn_bitlinear_workspace_bytes(layer, n);
+  if (workspace_bytes < need)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than the %zu needed",
+                workspace_bytes, need);
+  if (!aligned(workspace, 256) || !aligned(x, 16))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "workspace must be 256-byte and x 16-byte aligned");
+  auto* base = static_cast<uint8_t*>(workspace);
+  auto* q = reinterpret_cast<int8_t*>(base);
+  auto* sc = reinterpret_cast<float*>(base + align256(static_cast<size_t>(n) * layer->in_dim));
+  auto* qs = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(sc) + align256(sizeof(float) * n));
+  auto s = static_cast<cudaStream_t>(stream);
+  cudaError_t e =
+      obn::launch_rmsnorm_quant(x, layer->norm, layer->eps, n, layer->in_dim, q, sc, qs, s);
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
+  const int order = n == 1 ? obn::kOrderGemv : obn::kOrderGemm;  // bitlinear.rs:90-94
+  if (obn::gemm_supported(view(layer), n))
+    e = obn::launch_gemm(view(layer), q, sc, qs, n, y, nullptr, order, s);
+  else if (layer->in_dim <= obn::kGemvMaxK)
+    e = obn::launch_gemv(view(layer), q, sc, qs, n, y, nullptr, order, s);
+  else
+    return fail(OBN_ERR_UNSUPPORTED, "in_dim %d exceeds the kernels' limit", layer->in_dim);
+  if (e != cudaSuccess) return cuda_fail(e, "ternary matmul launch");
+  return OBN_OK;
+}
+
+int obn_bitlinear_export_i2s(const obn_bitlinear* layer, uint8_t* dst_dev, void* stream) {
+  clear_error();
+  if (int rc = check_layer(layer)) return rc;
+  if (!dst_dev || !aligned(dst_dev, 16))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "destination must be non-null and 16-byte aligned");
+  cudaError_t e = obn::launch_export_i2s(layer->w, dst_dev, layer->out_dim, layer->in_dim,
+                                         static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "export launch");
+  return OBN_OK;
+}
+
+int obn_check_device_errors(void) {
+  clear_error();
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  uint32_t word = 0;
+  e = obn::read_and_clear_dev_error(&word);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  if (word != 0)
+    return fail(OBN_ERR_DEVICE_TIMEOUT, "a bounded device-side wait gave up (code %u)", word);
+  return OBN_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,456 @@
+// kernels.cu — repack, fused RMSNorm+quantize and the dp4a decode GEMV (sm_100a).
+//
+// Bit-exactness contract (against the reference shaders):
+//  * RMSNorm sums squares as 256 strided lane partials followed by the halving
+//    tree of rmsnorm.wgsl:41-55, with explicitly rounded __fmul_rn/__fadd_rn so
+//    nvcc cannot contract them into FMAs; rms = 1 / sqrt(mean + eps) with IEEE
+//    sqrt and division; y = (x * rms) * w (rmsnorm.wgsl:57-61).
+//  * Quantization: absmax (order-free), scale/inv with IEEE division and the
+//    absmax == 0 selects of quantize.wgsl:122,131, q = clamp(rint(y * inv))
+//    with round-half-even (WGSL round(), quantize.wgsl:134).
+//  * The matmul is integer: sum_k c[m,k] q[t,k] - sum_k q[t,k] with codes
+//    c = w + 1 in {0,1,2}, which equals sum_k w[m,k] q[t,k] exactly (any order).
+//  * The epilogue rounds in the order of the shader the reference would have
+//    dispatched (kernels.h: EpilogueOrder).
+#include "kernels.h"
+#include "layout.cuh"
+#include "obn_common.cuh"
+
+namespace obn {
+
+namespace {
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// ---------------------------------------------------------------------------
+// Repack / export
+// ---------------------------------------------------------------------------
+// One thread per 16-byte half, enumerated in destination order so the T256
+// writes are contiguous: i = ((((panel*KB + b)*16 + s)*2 + h)*16 + r).
+__global__ void k_repack(const uint8_t* __restrict__ rows, uint8_t* __restrict__ t, int M, int K,
+                         int m_pad) {
+  const int KB = K / kBlockK;
+  const size_t total = static_cast<size_t>(m_pad) * KB * 2;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i % 16);
+    size_t j = i / 16;
+    const int h = static_cast<int>(j % 2);
+    j /= 2;
+    const int s = static_cast<int>(j % 16);
+    j /= 16;
+    const int b = static_cast<int>(j % KB);
+    const int panel = static_cast<int>(j / KB);
+    const int m = panel * kPanelRows + s * kSubRows + r;
+    uint4 v = make_uint4(0x55555555u, 0x55555555u, 0x55555555u, 0x55555555u);
+    if (m < M)
+      v = *reinterpret_cast<const uint4*>(rows + static_cast<size_t>(m) * (K / 4) + b * 32 + h * 16);
+    *reinterpret_cast<uint4*>(t + i * 16) = v;
+  }
+}
+
+// One thread per 16-byte half of the I2_S rows, in row order.
+__global__ void k_export(const uint8_t* __restrict__ t, uint8_t* __restrict__ rows, int M, int K) {
+  const int KB = K / kBlockK;
+  const size_t total = static_cast<size_t>(M) * KB * 2;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int h = static_cast<int>(i % 2);
+    const int b = static_cast<int>((i / 2) % KB);
+    const int m = static_cast<int>(i / (2 * static_cast<size_t>(KB)));
+    *reinterpret_cast<uint4*>(rows + i * 16) =
+        *reinterpret_cast<const uint4*>(t + half_offset(m, b, h, KB));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Block reductions for 256 threads
+// ---------------------------------------------------------------------------
+// The exact tree of rmsnorm.wgsl:47-55: partial[tid] += partial[tid + stride]
+// for stride = 128 .. 1. Strides 128 and 64 go through shared memory, 32 .. 1
+// through shuffles (lane l adds lane l + stride: the same pairing).
+OBN_DEVINL float tree_sum_256(float v, float* sh) {
+  const int tid = threadIdx.x;
+  sh[tid] = v;
+  __syncthreads();
+  if (tid < 128) sh[tid] = __fadd_rn(sh[tid], sh[tid + 128]);
+  __syncthreads();
+  if (tid < 64) sh[tid] = __fadd_rn(sh[tid], sh[tid + 64]);
+  __syncthreads();
+  if (tid < 32) {
+    float a = __fadd_rn(sh[tid], sh[tid + 32]);
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, s));
+    if (tid == 0) sh[0] = a;
+  }
+  __syncthreads();
+  const float r = sh[0];
+  __syncthreads();
+  return r;
+}
+
+// Max is order-independent: any reduction order gives the shader's result.
+OBN_DEVINL float block_max_256(float v, float* sh) {
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, s));
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = sh[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) r = fmaxf(r, sh[w]);
+  __syncthreads();
+  return r;
+}
+
+OBN_DEVINL int block_sum_int_256(int v, int* sh) {
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  int r = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) r += sh[w];
+  __syncthreads();
+  return r;
+}
+
+OBN_DEVINL float norm_mul(float x, float rms, float g) { return __fmul_rn(__fmul_rn(x, rms), g); }
+
+OBN_DEVINL uint32_t quant4(float4 y, float inv, int& sum) {
+  int a = min(127, max(-127, __float2int_rn(__fmul_rn(y.x, inv))));
+  int b = min(127, max(-127, __float2int_rn(__fmul_rn(y.y, inv))));
+  int c = min(127, max(-127, __float2int_rn(__fmul_rn(y.z, inv))));
+  int d = min(127, max(-127, __float2int_rn(__fmul_rn(y.w, inv))));
+  sum += a + b + c + d;
+  return (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
+         ((static_cast<uint32_t>(c) & 0xffu) << 16) | ((static_cast<uint32_t>(d) & 0xffu) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// Fused RMSNorm + quantize: one 256-thread CTA per token (the shaders' shape).
+// ---------------------------------------------------------------------------
+template <bool NORM>
+__global__ __launch_bounds__(256) void k_rmsnorm_quant(const float* __restrict__ x,
+                                                       const float* __restrict__ w, float eps,
+                                                       int d, int8_t* __restrict__ q,
+                                                       float* __restrict__ scales,
+                                                       int32_t* __restrict__ qsum) {
+  __shared__ float shf[256];
+  __shared__ int shi[8];
+  pdl_launch_dependents();
+  pdl_wait();  // x may be the previous kernel's output
+  const int tid = threadIdx.x;
+  const size_t row = blockIdx.x;
+  const float* xr = x + row * d;
+  float rms = 1.0f;
+  if (NORM) {
+    float part = 0.0f;  // rmsnorm.wgsl:41-45, lane tid owns columns tid + 256 j
+    for (int col = tid; col < d; col += 256) {
+      const float v = xr[col];
+      part = __fadd_rn(part, __fmul_rn(v, v));
+    }
+    const float total = tree_sum_256(part, shf);
+    rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(d)), eps)));
+  }
+  const float4* x4 = reinterpret_cast<const float4*>(xr);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const int d4 = d / 4;
+  float lmax = 0.0f;
+  for (int c = tid; c < d4; c += 256) {
+    float4 v = x4[c];
+    if (NORM) {
+      const float4 g = w4[c];
+      v = make_float4(norm_mul(v.x, rms, g.x), norm_mul(v.y, rms, g.y), norm_mul(v.z, rms, g.z),
+                      norm_mul(v.w, rms, g.w));
+    }
+    lmax = fmaxf(lmax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+  const float absmax = block_max_256(lmax, shf);
+  const float scale = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
+  const float inv = absmax == 0.0f ? 0.0f : __fdiv_rn(127.0f, absmax);
+  uint32_t* q4 = reinterpret_cast<uint32_t*>(q + row * d);
+  int lsum = 0;
+  for (int c = tid; c < d4; c += 256) {
+    float4 v = x4[c];
+    if (NORM) {
+      const float4 g = w4[c];
+      v = make_float4(norm_mul(v.x, rms, g.x), norm_mul(v.y, rms, g.y), norm_mul(v.z, rms, g.z),
+                      norm_mul(v.w, rms, g.w));
+    }
+    q4[c] = quant4(v, inv, lsum);
+  }
+  const int total_q = block_sum_int_256(lsum, shi);
+  if (tid == 0) {
+    scales[row] = scale;
+    if (qsum) qsum[row] = total_q;
+  }
+}
+
+// rmsnorm.wgsl alone.
+__global__ __launch_bounds__(256) void k_rmsnorm(const float* __restrict__ x,
+                                                 const float* __restrict__ w, float eps, int d,
+                                                 float* __restrict__ y) {
+  __shared__ float shf[256];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tid = threadIdx.x;
+  const size_t row = blockIdx.x;
+  const float* xr = x + row * d;
+  float part = 0.0f;
+  for (int col = tid; col < d; col += 256) {
+    const float v = xr[col];
+    part = __fadd_rn(part, __fmul_rn(v, v));
+  }
+  const float total = tree_sum_256(part, shf);
+  const float rms =
+      __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(d)), eps)));
+  float* yr = y + row * d;
+  for (int col = tid; col < d; col += 256) yr[col] = norm_mul(xr[col], rms, w[col]);
+}
+
+// ---------------------------------------------------------------------------
+// Decode GEMV on CUDA cores.
+//
+// CTA = one 16-row subtile x NT tokens, 4 warps. Before waiting on the
+// previous kernel (PDL), warp 0 bulk-copies the subtile's KB x 512 bytes of
+// packed weights into shared memory: the weights never depend on earlier
+// kernels, so their HBM stream overlaps the tail of the producer of q. Lane
+// (h = lane/16, r = lane%16) owns row r's half h of every block; warps split
+// the blocks. Per 16 bytes of weights and per token: 4 broadcast 16-byte
+// activation loads and 16 dp4a.
+// ---------------------------------------------------------------------------
+template <int NT, bool ACC>
+__global__ __launch_bounds__(128) void k_gemv(const uint8_t* __restrict__ W,
+                                              const float* __restrict__ s_w,
+                                              const int8_t* __restrict__ q,
+                                              const float* __restrict__ s_x,
+                                              const int32_t* __restrict__ qsum,
+                                              float* __restrict__ y, int32_t* __restrict__ acc_out,
+                                              int M, int K, int n, int order) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int red[4][NT][16];
+  __shared__ float sx_s[NT];
+  __shared__ int qs_s[NT];
+
+  const int KB = K / kBlockK;
+  const int S = blockIdx.x;
+  const int t0 = blockIdx.y * NT;
+  const int nt = min(NT, n - t0);
+  uint8_t* w_s = smem;
+  uint8_t* q_s = smem + KB * kSubtileBytes;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) mbar_arrive_expect_tx(&bar, static_cast<uint32_t>(KB) * kSubtileBytes);
+    __syncwarp();
+    const uint64_t pol = policy_evict_first();
+    for (int b = lane; b < KB; b += 32)
+      bulk_g2s_hint(w_s + b * kSubtileBytes, W + subtile_offset(S, b, KB), kSubtileBytes, &bar,
+                    pol);
+  }
+  pdl_launch_dependents();
+  pdl_wait();  // q / s_x / qsum come from the quantize kernel
+
+  const int kc = K / 16;  // 16-byte chunks per token
+  for (int i = tid; i < NT * kc; i += 128) {
+    const int t = i / kc, c = i - t * kc;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (t < nt) v = reinterpret_cast<const uint4*>(q + static_cast<size_t>(t0 + t) * K)[c];
+    reinterpret_cast<uint4*>(q_s)[i] = v;
+  }
+  if (tid < NT) {
+    sx_s[tid] = (!ACC && tid < nt) ? s_x[t0 + tid] : 0.0f;  // s_x is null in ACC mode
+    qs_s[tid] = tid < nt ? qsum[t0 + tid] : 0;
+  }
+  __syncthreads();
+
+  const bool ok = mbar_wait(&bar, 0);
+  if (!ok) mbar_wait(&bar, 0);  // copies may still be in flight: wait once more, bounded
+  int acc[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t] = 0;
+  if (ok) {
+    const uint32_t wbase = smem_u32(w_s) + lane * 16;
+    const uint32_t qbase = smem_u32(q_s) + (lane >> 4) * 16;
+#pragma unroll 2
+    for (int b = warp; b < KB; b += 4) {
+      const uint4 wv = lds128(wbase + b * kSubtileBytes);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int sh = 6 - 2 * g;
+        const uint32_t c0 = (wv.x >> sh) & 0x03030303u;
+        const uint32_t c1 = (wv.y >> sh) & 0x03030303u;
+        const uint32_t c2 = (wv.z >> sh) & 0x03030303u;
+        const uint32_t c3 = (wv.w >> sh) & 0x03030303u;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const uint4 xa = lds128(qbase + t * K + b * kBlockK + 32 * g);
+          int a = acc[t];
+          a = dp4a_us(c0, xa.x, a);
+          a = dp4a_us(c1, xa.y, a);
+          a = dp4a_us(c2, xa.z, a);
+          a = dp4a_us(c3, xa.w, a);
+          acc[t] = a;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], 16);
+  if (lane < 16) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) red[warp][t][lane] = acc[t];
+  }
+  __syncthreads();
+  if (tid < 16 * NT) {
+    const int t = tid >> 4, r = tid & 15;
+    const int m = S * kSubRows + r;
+    if (ok && t < nt && m < M) {
+      const int a = red[0][t][r] + red[1][t][r] + red[2][t][r] + red[3][t][r] - qs_s[t];
+      const size_t o = static_cast<size_t>(t0 + t) * M + m;
+      if (ACC) {
+        acc_out[o] = a;
+      } else {
+        const float fa = static_cast<float>(a);
+        const float sw = s_w[m], sx = sx_s[t];
+        y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fa, sw), sx) : __fmul_rn(fa, __fmul_rn(sw, sx));
+      }
+    }
+  }
+}
+
+// Raises a kernel's dynamic shared memory limit once per (kernel, device) to the
+// largest size requested so far.
+struct SmemCfg {
+  const void* fn;
+  int dev;
+  size_t bytes;
+};
+cudaError_t ensure_smem(const void* fn, size_t bytes) {
+  static SmemCfg table[256];
+  static int used = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  for (int i = 0; i < used; ++i)
+    if (table[i].fn == fn && table[i].dev == dev) {
+      if (table[i].bytes >= bytes) return cudaSuccess;
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+      if (e == cudaSuccess) table[i].bytes = bytes;
+      return e;
+    }
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess && used < 256) table[used++] = SmemCfg{fn, dev, bytes};
+  return e;
+}
+
+template <int NT, bool ACC>
+cudaError_t gemv_nt(const WeightView& W, const int8_t* q, const float* s_x, const int32_t* qsum,
+                    int n, float* y, int32_t* acc, int order, cudaStream_t s) {
+  const int K = W.in_dim;
+  const size_t smem = static_cast<size_t>(K / kBlockK) * kSubtileBytes + static_cast<size_t>(NT) * K;
+  auto kern = k_gemv<NT, ACC>;
+  cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kern), smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((W.out_dim + kSubRows - 1) / kSubRows, (n + NT - 1) / NT);
+  return launch_pdl(kern, grid, dim3(128), smem, s, W.w, W.s_w, q, s_x, qsum, y, acc, W.out_dim,
+                    K, n, order);
+}
+
+template <bool ACC>
+cudaError_t gemv_dispatch(const WeightView& W, const int8_t* q, const float* s_x,
+                          const int32_t* qsum, int n, float* y, int32_t* acc, int order,
+                          cudaStream_t s) {
+  switch (n) {
+    case 1: return gemv_nt<1, ACC>(W, q, s_x, qsum, n, y, acc, order, s);
+    case 2: return gemv_nt<2, ACC>(W, q, s_x, qsum, n, y, acc, order, s);
+    case 3: return gemv_nt<3, ACC>(W, q, s_x, qsum, n, y, acc, order, s);
+    case 4: return gemv_nt<4, ACC>(W, q, s_x, qsum, n, y, acc, order, s);
+    case 5: return gemv_nt<5, ACC>(W, q, s_x, qsum, n, y, acc, order, s);
+    case 6: return gemv_nt<6, ACC>(W, q, s_x, qsum, n, y, acc, order, s);
+    case 7: return gemv_nt<7, ACC>(W, q, s_x, qsum, n, y, acc, order, s);
+    default: return gemv_nt<8, ACC>(W, q, s_x, qsum, n, y, acc, order, s);
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+static int grid_for(size_t work, int block) {
+  size_t g = (work + block - 1) / block;
+  if (g > 148 * 32) g = 148 * 32;
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+cudaError_t launch_repack_i2s(const uint8_t* rows, uint8_t* t256, int M, int K, int m_pad,
+                              cudaStream_t s) {
+  const size_t work = static_cast<size_t>(m_pad) * (K / kBlockK) * 2;
+  k_repack<<<grid_for(work, 256), 256, 0, s>>>(rows, t256, M, K, m_pad);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_export_i2s(const uint8_t* t256, uint8_t* rows, int M, int K, cudaStream_t s) {
+  const size_t work = static_cast<size_t>(M) * (K / kBlockK) * 2;
+  k_export<<<grid_for(work, 256), 256, 0, s>>>(t256, rows, M, K);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps, int n, int d,
+                                 int8_t* q, float* scales, int32_t* qsum, cudaStream_t s) {
+  if (norm_w)
+    return launch_pdl(k_rmsnorm_quant<true>, dim3(n), dim3(256), 0, s, x, norm_w, eps, d, q,
+                      scales, qsum);
+  return launch_pdl(k_rmsnorm_quant<false>, dim3(n), dim3(256), 0, s, x, norm_w, eps, d, q, scales,
+                    qsum);
+}
+
+cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int d, float* y,
+                           cudaStream_t s) {
+  return launch_pdl(k_rmsnorm, dim3(n), dim3(256), 0, s, x, w, eps, d, y);
+}
+
+cudaError_t launch_gemv(const WeightView& W, const int8_t* q, const float* s_x,
+                        const int32_t* qsum, int n, float* y, int32_t* acc, int order,
+                        cudaStream_t s) {
+  if (acc) return gemv_dispatch<true>(W, q, s_x, qsum, n, nullptr, acc, order, s);
+  return gemv_dispatch<false>(W, q, s_x, qsum, n, y, nullptr, order, s);
+}
+
+cudaError_t read_and_clear_dev_error_kernels(uint32_t* out) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_dev_error, sizeof(uint32_t));
+  if (e != cudaSuccess) return e;
+  const uint32_t zero = 0;
+  return cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(uint32_t));
+}
+
+cudaError_t read_and_clear_dev_error(uint32_t* out) {
+  uint32_t a = 0, b = 0;
+  cudaError_t e = read_and_clear_dev_error_kernels(&a);
+  if (e == cudaSuccess) e = read_and_clear_dev_error_gemm(&b);
+  *out = a ? a : b;
+  return e;
+}
+
+}  // namespace obn

@@ -1,0 +1,49 @@
+// kernels.h — internal C++ launchers for the sm_100a kernels (not part of the C ABI).
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace obn {
+
+// Epilogue rounding order, as the two reference shaders write it.
+enum EpilogueOrder : int {
+  kOrderGemv = 0,  // (f32(acc) * s_w[m]) * s_x[t]      ternary_gemv.wgsl:232
+  kOrderGemm = 1,  // f32(acc) * (s_w[m] * s_x[t])      ternary_gemm.wgsl:132-133
+};
+
+struct WeightView {
+  const uint8_t* w;   // T256 layout (layout.cuh)
+  const float* s_w;   // [m_pad] per-row scales
+  int in_dim;         // K
+  int out_dim;        // M
+  int m_pad;          // M rounded up to 256
+};
+
+// I2_S rows [M][K/4] -> T256 (rows >= M filled with code 1).
+cudaError_t launch_repack_i2s(const uint8_t* rows, uint8_t* t256, int M, int K, int m_pad,
+                              cudaStream_t s);
+// T256 -> I2_S rows [M][K/4].
+cudaError_t launch_export_i2s(const uint8_t* t256, uint8_t* rows, int M, int K, cudaStream_t s);
+
+// Fused RMSNorm (norm_w may be null) + absmax int8 quantize; qsum nullable.
+cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps, int n, int d,
+                                 int8_t* q, float* scales, int32_t* qsum, cudaStream_t s);
+cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int d, float* y,
+                           cudaStream_t s);
+
+// Decode-path matmul on CUDA cores (dp4a) for any n (tokens in groups of 8).
+// Writes y (float, `order` rounding) or, when acc != nullptr, exact int32 sums.
+cudaError_t launch_gemv(const WeightView& W, const int8_t* q, const float* s_x,
+                        const int32_t* qsum, int n, float* y, int32_t* acc, int order,
+                        cudaStream_t s);
+// Largest K the GEMV kernel accepts.
+constexpr int kGemvMaxK = 16384;
+
+// Device error words (one per translation unit): read and reset.
+cudaError_t read_and_clear_dev_error_kernels(uint32_t* out);
+cudaError_t read_and_clear_dev_error_gemm(uint32_t* out);
+cudaError_t read_and_clear_dev_error(uint32_t* out);
+
+}  // namespace obn

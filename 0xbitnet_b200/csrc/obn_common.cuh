@@ -1,0 +1,143 @@
+// obn_common.cuh — shared device helpers for the sm_100a ternary BitLinear kernels.
+//
+// Inline PTX wrappers for mbarriers, bulk (TMA) copies, programmatic dependent
+// launch (PDL) and bounded waits. Every wait in this library is bounded: when
+// the bound is hit the kernel records OBN_DEVERR_* in obn_dev_error and moves on
+// without touching the data the wait guarded; the host reads the word with
+// obn_check_device_errors().
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#define OBN_DEVINL __device__ __forceinline__
+
+namespace obn {
+
+// Device-side error word (one per device context): 0 = ok, else the first
+// failure code recorded by a bounded wait.
+enum : uint32_t {
+  DEVERR_NONE = 0,
+  DEVERR_MBAR_TIMEOUT = 1,
+};
+// Internal linkage: every translation unit (built without -rdc) owns its own
+// copy and exposes it through a host reader (kernels.h).
+static __device__ uint32_t g_dev_error = 0;
+
+// Spin bound for mbarrier waits. try_wait suspends the thread for a
+// hardware-chosen interval per attempt, so this bounds the wait at well under
+// a second for any sane data movement while still ending a stuck kernel.
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+OBN_DEVINL uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+OBN_DEVINL void record_error(uint32_t code) { atomicCAS(&g_dev_error, 0u, code); }
+
+// ---- mbarrier ---------------------------------------------------------------
+OBN_DEVINL void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+OBN_DEVINL void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+OBN_DEVINL void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+OBN_DEVINL void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+OBN_DEVINL void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+OBN_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on phase `parity`. Returns false (and records the error) when
+// the bound is reached.
+OBN_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  record_error(DEVERR_MBAR_TIMEOUT);
+  return false;
+}
+
+// ---- bulk copies (non-tensor TMA) -------------------------------------------
+// Global -> shared, completion signalled on `bar` as transaction bytes.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+OBN_DEVINL void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Same, with an L2 eviction-priority hint (createpolicy result).
+OBN_DEVINL void bulk_g2s_hint(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
+                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], "
+      "%2, [%3], %4;" ::"r"(smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+OBN_DEVINL uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+OBN_DEVINL uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ---- programmatic dependent launch ------------------------------------------
+// Lets the next kernel in the stream (launched with the PDL attribute) start
+// its prologue; it still waits for this grid's completion in pdl_wait().
+OBN_DEVINL void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// Blocks until every prerequisite grid has completed and its writes are visible.
+OBN_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---- integer dot product ------------------------------------------------------
+// acc + sum_{b<4} a.byte[b] * b.byte[b], a unsigned codes, b signed int8.
+OBN_DEVINL int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+OBN_DEVINL uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+}  // namespace obn

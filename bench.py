@@ -1,0 +1,463 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 ternary BitLinear path (decode GEMV sweep, config 1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Step: the BitLinear forwards of a BitNet-b1.58-2B decoder for every batch size
+of the sweep: for B in {1, 8, 32, 64}, 30 layers x 5 projections (fused QKV
+3840x2560, o 2560x2560, gate 6912x2560, up 6912x2560, down 2560x6912), each a
+fused RMSNorm + per-token int8 quantize + ternary matmul through the C ABI.
+The 150 weight matrices (521 MB packed) exceed L2, so every pass streams them
+from HBM. Each B is one CUDA graph of the 150 forwards (captured through the
+public API), replayed per step.
+
+value  = algorithmic bytes of the step / device time (GB/s, summed over ranks);
+         bytes per forward = M*K/4 + B*K*4 + K*4 + B*M*4 + 4.
+e2e    = the same through host buffers: per step one H2D copy of all inputs
+         from pinned memory and one D2H copy of all outputs, timed with the
+         graph replays.
+Multi-GPU (torchrun): independent decode sequences per GPU, full weight
+replicas, no collective on the data path (weak scaling); the max over ranks
+of the device time is reported.
+
+--impl reference times the reference algorithm's CPU restatement (oracle/,
+OpenMP over all host threads) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "ternary decode GEMV GB/s"
+BATCHES = (1, 8, 32, 64)
+LAYERS = 30
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--layers", type=int, default=LAYERS)
+    p.add_argument("--batches", type=str, default=",".join(map(str, BATCHES)))
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def shapes():
+    synth = importlib.import_module("0xbitnet_b200.synthetic")
+    return list(synth.SHAPES_2B.items())
+
+
+def fwd_bytes(M: int, K: int, B: int) -> int:
+    return M * K // 4 + B * K * 4 + K * 4 + B * M * 4 + 4
+
+
+def gemv_kernel_bytes(M: int, K: int, B: int) -> int:
+    # matmul kernel alone: packed weights + int8 activations + per-token scale
+    # and code sum + per-row scales + f32 output
+    return M * K // 4 + B * K + 8 * B + 4 * M + 4 * B * M
+
+
+def config(args, world):
+    return {
+        "workload": "cfg1 decode GEMV sweep: B in {%s} x %d layers x 5 BitNet-2B BitLinear shapes "
+                    "(qkv 3840x2560, o 2560x2560, gate 6912x2560, up 6912x2560, down 2560x6912); "
+                    "fused RMSNorm + int8 absmax quantize + ternary matmul per forward"
+                    % (args.batches, args.layers),
+        "batches": [int(b) for b in args.batches.split(",")],
+        "layers": args.layers,
+        "weights_bytes_per_pass": sum(M * K // 4 for _, (M, K) in shapes()) * args.layers,
+        "l2": "inputs larger than L2: each batch pass streams 521 MB of packed weights",
+        "parallelism": f"dp{world} (independent decode sequences per GPU, no collective)",
+    }
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i - 1] for r in rows for i in range(1, 5)
+                          if r[3][i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in rows),
+                "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows),
+                "samples": len(rows), "reasons": reasons}
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_sample(args, min_seconds=10.0, max_reps=50):
+    """Times the oracle (OpenMP, all host threads) on 1 layer x 5 shapes x every B."""
+    import numpy as np
+    import oracle as orc
+    synth = importlib.import_module("0xbitnet_b200.synthetic")
+    batches = [int(b) for b in args.batches.split(",")]
+    data = []
+    for i, (name, (M, K)) in enumerate(shapes()):
+        L = synth.layer(900 + i, M, K)
+        xs = {B: synth.activations(950 + i * 10 + B, B, K) for B in batches}
+        data.append((M, K, L, xs))
+    threads = orc.max_threads()
+    bytes_per_rep = sum(fwd_bytes(M, K, B) for M, K, _, _ in data for B in batches)
+
+    def rep():
+        for M, K, L, xs in data:
+            for B in batches:
+                orc.bitlinear_omp(xs[B], L.packed, L.row_scales(), M, K, norm_w=L.gamma,
+                                  threads=threads)
+    rep()  # warm
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        rep()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or reps >= max_reps:
+            break
+    return {"value": bytes_per_rep * reps / el / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"1 layer x 5 shapes x B in {{{args.batches}}} ({reps} reps, "
+                      f"{el:.1f} s): the oracle's C restatement of the WGSL kernels"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import oracle as orc
+    import numpy as np
+    synth = importlib.import_module("0xbitnet_b200.synthetic")
+    batches = [int(b) for b in args.batches.split(",")]
+    data = []
+    for i, (name, (M, K)) in enumerate(shapes()):
+        L = synth.layer(900 + i, M, K)
+        xs = {B: synth.activations(950 + i * 10 + B, B, K) for B in batches}
+        data.append((M, K, L, xs))
+    threads = orc.max_threads()
+    step_bytes = sum(fwd_bytes(M, K, B) for M, K, _, _ in data for B in batches)
+
+    def step():
+        for M, K, L, xs in data:
+            for B in batches:
+                orc.bitlinear_omp(xs[B], L.packed, L.row_scales(), M, K, norm_w=L.gamma,
+                                  threads=threads)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    value = step_bytes * args.steps / el / 1e9
+    sample = (f"each step: 1 of the {args.layers} layers (5 shapes) x B in {{{args.batches}}}, "
+              f"{step_bytes} algorithmic bytes; oracle C restatement, OpenMP")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded)",
+        "config": config(args, world),
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ----------------------------------------------------------------------------- ours
+def load_profile_traffic():
+    path = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+    try:
+        return json.load(open(path))
+    except (OSError, ValueError):
+        return None
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and "WORLD_SIZE" in os.environ:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    obn = importlib.import_module("0xbitnet_b200")
+    synth = importlib.import_module("0xbitnet_b200.synthetic")
+    batches = [int(b) for b in args.batches.split(",")]
+    shp = shapes()
+
+    # Weights: one replica per GPU (independent decode sequences need no exchange).
+    layers = []
+    for l in range(args.layers):
+        row = []
+        for i, (name, (M, K)) in enumerate(shp):
+            packed, s_w, gamma = synth.layer_device(10_000 + 10 * l + i, M, K, dev)
+            row.append(obn.BitLinear(packed, s_w, gamma, K, M))
+            del packed
+        layers.append(row)
+    torch.cuda.synchronize()
+
+    # Activations: flat device buffers so the e2e copies are one H2D + one D2H per step.
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    x_total = sum(B * K for B in batches for _, (M, K) in shp)
+    y_total = sum(B * M for B in batches for _, (M, K) in shp)
+    x_flat = torch.randn(x_total, generator=gen, device=dev)
+    y_flat = torch.empty(y_total, device=dev)
+    xs, ys = {}, {}
+    xo = yo = 0
+    for B in batches:
+        for i, (name, (M, K)) in enumerate(shp):
+            xs[B, i] = x_flat[xo:xo + B * K].view(B, K)
+            ys[B, i] = y_flat[yo:yo + B * M].view(B, M)
+            xo += B * K
+            yo += B * M
+
+    stream = torch.cuda.Stream(device=dev)
+    graphs = {}
+    with torch.cuda.stream(stream):
+        for B in batches:  # eager warm-up allocates every layer's workspace
+            for row in layers:
+                for i, L in enumerate(row):
+                    L.forward(xs[B, i], out=ys[B, i])
+        stream.synchronize()
+        for B in batches:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for row in layers:
+                    for i, L in enumerate(row):
+                        L.forward(xs[B, i], out=ys[B, i])
+            graphs[B] = g
+    torch.cuda.synchronize()
+    obn.check_device_errors()
+
+    step_bytes = {B: args.layers * sum(fwd_bytes(M, K, B) for _, (M, K) in shp) for B in batches}
+    launches_per_step = 2 * args.layers * len(shp) * len(batches)
+
+    def step(evs=None):
+        for j, B in enumerate(batches):
+            if evs is not None:
+                evs[j][0].record(stream)
+            graphs[B].replay()
+            if evs is not None:
+                evs[j][1].record(stream)
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+        stream.synchronize()
+        barrier()
+        per_b_ms = {B: 0.0 for B in batches}
+        evs_all = []
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t_start.record(stream)
+        for _ in range(args.steps):
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in batches]
+            step(evs)
+            evs_all.append(evs)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    clock_info = clocks.stop()
+    total_ms = t_start.elapsed_time(t_end)
+    for evs in evs_all:
+        for j, B in enumerate(batches):
+            per_b_ms[B] += evs[j][0].elapsed_time(evs[j][1])
+    total_ms_max = max_over_ranks(total_ms)
+    bytes_all = world * args.steps * sum(step_bytes.values())
+    value = bytes_all / (total_ms_max / 1e3) / 1e9
+
+    # e2e: pinned host inputs -> device, graphs, device -> pinned host outputs, every step.
+    x_host = torch.empty(x_total, dtype=torch.float32, pin_memory=True)
+    x_host.copy_(x_flat.cpu())
+    y_host = torch.empty(y_total, dtype=torch.float32, pin_memory=True)
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            x_flat.copy_(x_host, non_blocking=True)
+            step()
+            y_host.copy_(y_flat, non_blocking=True)
+        stream.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            x_flat.copy_(x_host, non_blocking=True)
+            step()
+            y_host.copy_(y_flat, non_blocking=True)
+        e1.record(stream)
+        stream.synchronize()
+        barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = bytes_all / (e2e_ms / 1e3) / 1e9
+
+    # Dominant kernel: the B=1 matmul alone over all 150 weights (pre-quantized q).
+    q_ms = None
+    k_bytes = args.layers * sum(gemv_kernel_bytes(M, K, 1) for _, (M, K) in shp)
+    with torch.cuda.stream(stream):
+        qin = {}
+        for i, (name, (M, K)) in enumerate(shp):
+            qin[i] = obn.rmsnorm_quantize(xs[1, i].contiguous())
+        torch.cuda.synchronize()
+        gk = torch.cuda.CUDAGraph()
+        outs = {i: torch.empty((1, M), device=dev) for i, (_, (M, K)) in enumerate(shp)}
+        with torch.cuda.graph(gk, stream=stream):
+            for row in layers:
+                for i, L in enumerate(row):
+                    q, s, qs = qin[i]
+                    obn._lib.check(obn.lib().obn_ternary_matmul(
+                        L.handle, q.data_ptr(), s.data_ptr(), qs.data_ptr(), 1,
+                        outs[i].data_ptr(), stream.cuda_stream))
+        for _ in range(3):
+            gk.replay()
+        stream.synchronize()
+        k0 = torch.cuda.Event(enable_timing=True)
+        k1 = torch.cuda.Event(enable_timing=True)
+        reps = max(10, args.steps)
+        k0.record(stream)
+        for _ in range(reps):
+            gk.replay()
+        k1.record(stream)
+        stream.synchronize()
+        q_ms = k0.elapsed_time(k1) / reps
+    torch.cuda.synchronize()
+    obn.check_device_errors()
+
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("hbm_gbs")
+    peak_note = "measured" if peak else "fallback"
+    peak = peak or 6650.0
+    launches_k = args.layers * len(shp)
+    achieved = k_bytes / (q_ms / 1e3) / 1e9
+    traffic = load_profile_traffic()
+    roofline = {
+        "kernel": "k_gemv<1> (B=1 ternary matmul, dp4a)",
+        "bound": "hbm", "achieved": achieved, "peak": peak, "peak_source": peak_note,
+        "unit": "GB/s", "frac": achieved / peak,
+        "avg_launch_us": q_ms * 1e3 / launches_k,
+        "bytes_per_launch_avg": k_bytes / launches_k,
+        "traffic": traffic.get("bytes_per_launch_avg") if traffic else None,
+    }
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_sample(args)
+
+    if rank == 0:
+        # per-batch figures are rank 0's own device time (ranks run identical work)
+        per_b = {str(B): step_bytes[B] * args.steps * world / (per_b_ms[B] / 1e3) / 1e9
+                 for B in batches}
+        tok_s = {str(B): B * world * args.steps / (per_b_ms[B] / 1e3) for B in batches}
+        out = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms_max / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (seeded): N(0,1) activations, RMSNorm gamma N(1,0.1), i.i.d. "
+                    "ternary weights P(-1)=P(+1)=0.3, per-tensor scale U(0.5,2)",
+            "config": config(args, world),
+            "per_batch_gbs": per_b,
+            "bitlinear_stack_tok_s": tok_s,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clock_info,
+            "e2e": {"value": e2e_value, "unit": "GB/s",
+                    "h2d_bytes_per_step": x_total * 4, "d2h_bytes_per_step": y_total * 4},
+            "gpu_launches": launches_per_step * args.steps,
+        }
+        print(json.dumps(out), flush=True)
+    for g in graphs.values():
+        del g
+    graphs.clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

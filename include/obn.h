@@ -1,0 +1,146 @@
+/*
+ * obn.h — C ABI of the B200-native ternary BitLinear path (libobn.so).
+ *
+ * Replaces the wgpu dispatches of 0xBitNet's BitLinear layer:
+ *   BitLinear::new / BitLinear::forward
+ *     packages/rust/crates/oxbitnet/src/nn/bitlinear.rs:31-97
+ *     packages/core/src/nn/bitlinear.ts:47-169 (exported via packages/core/src/internals.ts:33)
+ *   the I2_S upload + per-row scale extraction
+ *     packages/rust/crates/oxbitnet/src/model/loader.rs:105-137
+ *   and the four shaders they dispatch
+ *     packages/core/src/shaders/{rmsnorm,quantize,ternary_gemv,ternary_gemm}.wgsl
+ *
+ * Conventions (those of the reference's C ABI, packages/rust/crates/oxbitnet-ffi):
+ *   - every entry point returns OBN_OK (0) or a negative status; the message of
+ *     the last failure on the calling thread is returned by obn_error_message()
+ *     (thread-local, library-owned, valid until the next obn_* call on that
+ *     thread; cf. oxbitnet-ffi/src/lib.rs:31-46, 528-541);
+ *   - device pointers are caller-owned CUDA device memory; `stream` is a
+ *     cudaStream_t passed as void* (NULL = the legacy default stream);
+ *   - every compute entry point is stream-ordered and does not synchronise.
+ *
+ * Data formats:
+ *   - activations x: float32 [n, in_dim], row-major;
+ *   - quantized activations q: int8 [n, in_dim] (the reference stores the same
+ *     values as i32, quantize.wgsl:74); per-token scales float32 [n];
+ *     per-token code sums int32 [n] (sum_k q[t,k], used by the kernels to turn
+ *     2-bit codes c in {0,1,2} into weights c-1 exactly);
+ *   - weights: I2_S rows of in_dim/4 bytes (128-element blocks of 32 bytes,
+ *     byte gp holding elements gp, 32+gp, 64+gp, 96+gp in bits 7:6..1:0, code
+ *     c meaning weight c-1), in_dim % 128 == 0;
+ *   - outputs y: float32 [n, out_dim], token-major (ternary_gemm.wgsl:133).
+ */
+#ifndef OBN_H
+#define OBN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define OBN_API __attribute__((visibility("default")))
+#else
+#define OBN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OBN_OK 0
+#define OBN_ERR_INVALID_ARGUMENT -1  /* null pointer, bad size, misaligned buffer */
+#define OBN_ERR_UNSUPPORTED -2       /* shape outside what the kernels handle */
+#define OBN_ERR_CUDA -3              /* a CUDA runtime call failed */
+#define OBN_ERR_OUT_OF_MEMORY -4
+#define OBN_ERR_DEVICE_TIMEOUT -5    /* a bounded device-side wait gave up */
+#define OBN_ERR_NO_DEVICE -6         /* no CUDA device, or not sm_100 */
+
+typedef struct obn_bitlinear obn_bitlinear;
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+OBN_API int obn_version(void);
+
+/* Last error on this thread, or NULL. Mirrors oxbitnet_error_message
+ * (oxbitnet-ffi/oxbitnet.h:218-224). */
+OBN_API const char* obn_error_message(void);
+
+/* ---- layer lifecycle ------------------------------------------------------ */
+
+/* Loads one GGUF I2_S tensor from host memory: `i2s_tensor` holds
+ * out_dim*in_dim/4 packed bytes followed by 32 bytes whose first float32 is the
+ * per-tensor scale (loader.rs:105-137; GGUF ne[0]=in_dim, ne[1]=out_dim).
+ * The scale is replicated into a per-row [out_dim] table as the reference does
+ * (loader.rs:129-137). `norm_weight` (host, nullable) is the optional [in_dim]
+ * RMSNorm gamma applied before quantization (bitlinear.rs:61-71), `eps` its
+ * epsilon (the reference hard-codes 1e-5, bitlinear.rs:112). The weights are
+ * repacked into the device layout on `device`. */
+OBN_API int obn_bitlinear_load_i2s(const uint8_t* i2s_tensor, size_t nbytes, int in_dim, int out_dim,
+                           const float* norm_weight, float eps, int device,
+                           obn_bitlinear** out_layer);
+
+/* BitLinear::new(device, packed_weights, weight_scales, norm_weight, in_dim,
+ * out_dim) (bitlinear.rs:31-49) over buffers already on the device in the
+ * reference's layout: packed [out_dim, in_dim/16] u32, per-row scales
+ * [out_dim] f32, norm [in_dim] f32 or NULL. The data is copied (repacked) into
+ * library-owned memory on the current device, ordered on `stream`. */
+OBN_API int obn_bitlinear_create(const void* packed_dev, const float* scales_dev, const float* norm_dev,
+                         float eps, int in_dim, int out_dim, void* stream,
+                         obn_bitlinear** out_layer);
+
+/* Frees a layer; NULL is a no-op (oxbitnet-ffi/src/lib.rs:367-376). */
+OBN_API void obn_bitlinear_free(obn_bitlinear* layer);
+
+/* Shape queries. */
+OBN_API int obn_bitlinear_in_dim(const obn_bitlinear* layer);
+OBN_API int obn_bitlinear_out_dim(const obn_bitlinear* layer);
+
+/* Device scratch that obn_bitlinear_forward needs for n tokens (bytes). */
+OBN_API size_t obn_bitlinear_workspace_bytes(const obn_bitlinear* layer, int n);
+
+/* BitLinear::forward(input, n) (bitlinear.rs:52-97; bitlinear.ts:117-169):
+ * optional RMSNorm -> per-token absmax int8 quantize -> ternary GEMV (n == 1)
+ * or GEMM (n > 1) -> y[n, out_dim]. `workspace` (device, 256-byte aligned) must
+ * hold obn_bitlinear_workspace_bytes(layer, n) bytes and must not be used by
+ * other work in flight. The epilogue rounds like the reference: n == 1 gives
+ * (f32(acc) * s_w) * s_x (ternary_gemv.wgsl:232), n > 1 gives
+ * f32(acc) * (s_w * s_x) (ternary_gemm.wgsl:132-133). */
+OBN_API int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, int n, float* y,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- kernel-level entry points (one per reference shader) ------------------ */
+
+/* Fused rmsnorm.wgsl + quantize.wgsl: per token, optional RMSNorm with gamma
+ * `norm_weight` (NULL: none), then absmax int8 quantization. Writes q [n, d],
+ * scales [n] and code sums qsum [n] (nullable). d % 4 == 0. */
+OBN_API int obn_rmsnorm_quantize(const float* x, const float* norm_weight, float eps, int n, int d,
+                         int8_t* q, float* scales, int32_t* qsum, void* stream);
+
+/* rmsnorm.wgsl alone: y[n, d] = (x * rms) * w. */
+OBN_API int obn_rmsnorm(const float* x, const float* w, float eps, int n, int d, float* y,
+                void* stream);
+
+/* ternary_gemv.wgsl / ternary_gemm.wgsl on already-quantized activations,
+ * with the layer's weights: y[t, m] for t < n. `qsum` as written by
+ * obn_rmsnorm_quantize. n == 1 rounds like the GEMV shader, n > 1 like the
+ * GEMM shader. */
+OBN_API int obn_ternary_matmul(const obn_bitlinear* layer, const int8_t* q, const float* scales,
+                       const int32_t* qsum, int n, float* y, void* stream);
+
+/* The exact int32 accumulators acc[t, m] = sum_k w[m,k] * q[t,k] (no scaling),
+ * for bit-exact checks of the integer core. */
+OBN_API int obn_ternary_acc(const obn_bitlinear* layer, const int8_t* q, const int32_t* qsum, int n,
+                    int32_t* acc, void* stream);
+
+/* Copies the layer's device weights back out in the reference's I2_S row
+ * layout [out_dim, in_dim/4] bytes (device destination), for round-trip
+ * checks of the repack. */
+OBN_API int obn_bitlinear_export_i2s(const obn_bitlinear* layer, uint8_t* dst_dev, void* stream);
+
+/* Reads (and clears) the device error word that bounded in-kernel waits set
+ * when they give up; returns OBN_OK or OBN_ERR_DEVICE_TIMEOUT. Synchronises
+ * the current device. */
+OBN_API int obn_check_device_errors(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OBN_H */
