@@ -313,8 +313,13 @@ int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, int n, flo
   auto* sc = reinterpret_cast<float*>(base + align256(static_cast<size_t>(n) * layer->in_dim));
   auto* qs = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(sc) + align256(sizeof(float) * n));
   auto s = static_cast<cudaStream_t>(stream);
-  cudaError_t e =
-      obn::launch_rmsnorm_quant(x, layer->norm, layer->eps, n, layer->in_dim, q, sc, qs, s);
+  cudaError_t e;
+  if (n == 1 && layer->in_dim <= obn::kGemvMaxK) {  // whole BitLinear in one kernel
+    e = obn::launch_bitlinear_n1(view(layer), layer->norm, layer->eps, x, y, s);
+    if (e != cudaSuccess) return cuda_fail(e, "bitlinear (n=1) launch");
+    return OBN_OK;
+  }
+  e = obn::launch_rmsnorm_quant(x, layer->norm, layer->eps, n, layer->in_dim, q, sc, qs, s);
   if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
   const int order = n == 1 ? obn::kOrderGemv : obn::kOrderGemm;  // bitlinear.rs:90-94
   if (obn::gemm_supported(view(layer), n))

@@ -5,6 +5,9 @@
 
 namespace obn {
 
+// Smallest token count routed to the tensor-core GEMM.
+constexpr int kGemmMinTokens = 16;
+
 // True when launch_gemm handles this shape (otherwise the dp4a path runs).
 bool gemm_supported(const WeightView& W, int n);
 

@@ -225,25 +225,73 @@ __global__ __launch_bounds__(256) void k_rmsnorm(const float* __restrict__ x,
 // ---------------------------------------------------------------------------
 // Decode GEMV on CUDA cores.
 //
-// CTA = one 16-row subtile x NT tokens, 4 warps. Before waiting on the
-// previous kernel (PDL), warp 0 bulk-copies the subtile's KB x 512 bytes of
-// packed weights into shared memory: the weights never depend on earlier
+// CTA = one 16-row subtile x NT tokens, kGemvWarps warps. Before waiting on
+// the previous kernel (PDL), warp 0 bulk-copies the subtile's KB x 512 bytes
+// of packed weights into shared memory: the weights never depend on earlier
 // kernels, so their HBM stream overlaps the tail of the producer of q. Lane
 // (h = lane/16, r = lane%16) owns row r's half h of every block; warps split
 // the blocks. Per 16 bytes of weights and per token: 4 broadcast 16-byte
-// activation loads and 16 dp4a.
+// activation loads and 16 dp4a, in two independent accumulation chains.
 // ---------------------------------------------------------------------------
+constexpr int kGemvWarps = 8;
+
+// Accumulates sum_k c[r,k] q[t,k] for this lane's row r = lane%16 and half
+// h = lane/16 over blocks first, first + stride, ... (codes c = w + 1).
+//
+// Group g of a packed byte sits at bits (6-2g); instead of shifting it down,
+// the word is only masked (one LOP3) and fed to dp4a as unsigned bytes
+// c_g << (6-2g). Each group keeps its own accumulator, an exact multiple of
+// 4^(3-g), and the shifts are applied once at the end (exact; |acc| stays
+// below 3*64*127*16384 < 2^31 for K <= 16384).
+template <int NT>
+OBN_DEVINL void subtile_dot(uint32_t w_s, uint32_t q_s, int ldq, int KB, int first, int stride,
+                            int lane, int (&acc)[NT]) {
+  int a[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int g = 0; g < 4; ++g) a[t][g] = 0;
+  const uint32_t wbase = w_s + lane * 16;
+  const uint32_t qbase = q_s + (lane >> 4) * 16;
+#pragma unroll 2
+  for (int b = first; b < KB; b += stride) {
+    const uint4 wv = lds128(wbase + b * kSubtileBytes);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint32_t mask = 0xC0C0C0C0u >> (2 * g);
+      const uint32_t c0 = wv.x & mask, c1 = wv.y & mask, c2 = wv.z & mask, c3 = wv.w & mask;
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+        const uint4 xa = lds128(qbase + t * ldq + b * kBlockK + 32 * g);
+        a[t][g] = dp4a_us(c3, xa.w, dp4a_us(c2, xa.z, dp4a_us(c1, xa.y, dp4a_us(c0, xa.x, a[t][g]))));
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+    acc[t] += (a[t][0] >> 6) + (a[t][1] >> 4) + (a[t][2] >> 2) + a[t][3];
+}
+
+// Issues the bulk copies of subtile S's KB blocks (warp 0) on `bar`, with
+// `extra` more expected bytes announced for copies the caller adds.
+OBN_DEVINL void prefetch_subtile(uint8_t* w_s, const uint8_t* W, int S, int KB, uint64_t* bar,
+                                 uint32_t extra_bytes, int lane) {
+  if (lane == 0)
+    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(KB) * kSubtileBytes + extra_bytes);
+  __syncwarp();
+  const uint64_t pol = policy_evict_first();
+  for (int b = lane; b < KB; b += 32)
+    bulk_g2s_hint(w_s + b * kSubtileBytes, W + subtile_offset(S, b, KB), kSubtileBytes, bar, pol);
+}
+
 template <int NT, bool ACC>
-__global__ __launch_bounds__(128) void k_gemv(const uint8_t* __restrict__ W,
-                                              const float* __restrict__ s_w,
-                                              const int8_t* __restrict__ q,
-                                              const float* __restrict__ s_x,
-                                              const int32_t* __restrict__ qsum,
-                                              float* __restrict__ y, int32_t* __restrict__ acc_out,
-                                              int M, int K, int n, int order) {
+__global__ __launch_bounds__(kGemvWarps * 32) void k_gemv(
+    const uint8_t* __restrict__ W, const float* __restrict__ s_w, const int8_t* __restrict__ q,
+    const float* __restrict__ s_x, const int32_t* __restrict__ qsum, float* __restrict__ y,
+    int32_t* __restrict__ acc_out, int M, int K, int n, int order) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
-  __shared__ int red[4][NT][16];
+  __shared__ int red[kGemvWarps][NT][16];
   __shared__ float sx_s[NT];
   __shared__ int qs_s[NT];
 
@@ -260,19 +308,12 @@ __global__ __launch_bounds__(128) void k_gemv(const uint8_t* __restrict__ W,
     fence_mbar_init();
   }
   __syncthreads();
-  if (warp == 0) {
-    if (lane == 0) mbar_arrive_expect_tx(&bar, static_cast<uint32_t>(KB) * kSubtileBytes);
-    __syncwarp();
-    const uint64_t pol = policy_evict_first();
-    for (int b = lane; b < KB; b += 32)
-      bulk_g2s_hint(w_s + b * kSubtileBytes, W + subtile_offset(S, b, KB), kSubtileBytes, &bar,
-                    pol);
-  }
+  if (warp == 0) prefetch_subtile(w_s, W, S, KB, &bar, 0, lane);
   pdl_launch_dependents();
   pdl_wait();  // q / s_x / qsum come from the quantize kernel
 
   const int kc = K / 16;  // 16-byte chunks per token
-  for (int i = tid; i < NT * kc; i += 128) {
+  for (int i = tid; i < NT * kc; i += kGemvWarps * 32) {
     const int t = i / kc, c = i - t * kc;
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
     if (t < nt) v = reinterpret_cast<const uint4*>(q + static_cast<size_t>(t0 + t) * K)[c];
@@ -289,32 +330,7 @@ __global__ __launch_bounds__(128) void k_gemv(const uint8_t* __restrict__ W,
   int acc[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc[t] = 0;
-  if (ok) {
-    const uint32_t wbase = smem_u32(w_s) + lane * 16;
-    const uint32_t qbase = smem_u32(q_s) + (lane >> 4) * 16;
-#pragma unroll 2
-    for (int b = warp; b < KB; b += 4) {
-      const uint4 wv = lds128(wbase + b * kSubtileBytes);
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const int sh = 6 - 2 * g;
-        const uint32_t c0 = (wv.x >> sh) & 0x03030303u;
-        const uint32_t c1 = (wv.y >> sh) & 0x03030303u;
-        const uint32_t c2 = (wv.z >> sh) & 0x03030303u;
-        const uint32_t c3 = (wv.w >> sh) & 0x03030303u;
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const uint4 xa = lds128(qbase + t * K + b * kBlockK + 32 * g);
-          int a = acc[t];
-          a = dp4a_us(c0, xa.x, a);
-          a = dp4a_us(c1, xa.y, a);
-          a = dp4a_us(c2, xa.z, a);
-          a = dp4a_us(c3, xa.w, a);
-          acc[t] = a;
-        }
-      }
-    }
-  }
+  if (ok) subtile_dot<NT>(smem_u32(w_s), smem_u32(q_s), K, KB, warp, kGemvWarps, lane, acc);
 #pragma unroll
   for (int t = 0; t < NT; ++t) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], 16);
   if (lane < 16) {
@@ -326,7 +342,9 @@ __global__ __launch_bounds__(128) void k_gemv(const uint8_t* __restrict__ W,
     const int t = tid >> 4, r = tid & 15;
     const int m = S * kSubRows + r;
     if (ok && t < nt && m < M) {
-      const int a = red[0][t][r] + red[1][t][r] + red[2][t][r] + red[3][t][r] - qs_s[t];
+      int a = -qs_s[t];
+#pragma unroll
+      for (int w = 0; w < kGemvWarps; ++w) a += red[w][t][r];
       const size_t o = static_cast<size_t>(t0 + t) * M + m;
       if (ACC) {
         acc_out[o] = a;
@@ -336,6 +354,146 @@ __global__ __launch_bounds__(128) void k_gemv(const uint8_t* __restrict__ W,
         y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fa, sw), sx) : __fmul_rn(fa, __fmul_rn(sw, sx));
       }
     }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Single-token BitLinear in one kernel: RMSNorm + quantize + GEMV.
+//
+// One decode token leaves no work to share, so every CTA (two 16-row
+// subtiles, 256 threads) normalises and quantizes the token itself; that keeps
+// the whole BitLinear to one launch and one dependent round trip. Before the
+// PDL wait the CTA prefetches everything that does not depend on earlier
+// kernels: its packed weights and the RMSNorm gamma (bulk copies into shared
+// memory) and its row scales. After the wait, thread t loads x[t + 256 j] —
+// exactly the columns lane t of rmsnorm.wgsl / quantize.wgsl owns — so the sum
+// of squares is reduced in the shaders' order (tree_sum_256) and q matches
+// bit for bit. The scalar divisions run once (thread 0) and are broadcast.
+// ---------------------------------------------------------------------------
+constexpr int kN1Rows = 32;  // rows per CTA (two subtiles)
+
+template <int EPT>
+__global__ __launch_bounds__(256) void k_bitlinear_n1(
+    const uint8_t* __restrict__ W, const float* __restrict__ s_w,
+    const float* __restrict__ gamma, float eps, const float* __restrict__ x,
+    float* __restrict__ y, int M, int K) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float shf[256];
+  __shared__ float scal[4];  // rms, scale, inv
+  __shared__ int red[8][16];
+  __shared__ int red_q[8];
+  __shared__ int ok_s;
+
+  const int KB = K / kBlockK;
+  const int S0 = blockIdx.x * 2;                  // first subtile
+  const int nsub = min(2, (M + kSubRows - 1) / kSubRows - S0);
+  if (nsub <= 0) return;  // uniform per CTA; the launcher never makes such CTAs
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint8_t* w_s = smem;                                                   // nsub * KB * 512
+  float* g_s = reinterpret_cast<float*>(smem + 2 * KB * kSubtileBytes);  // K floats
+  int8_t* q_s = reinterpret_cast<int8_t*>(g_s + K);                      // K bytes
+
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t gbytes = gamma ? static_cast<uint32_t>(K) * 4u : 0u;
+    if (lane == 0)
+      mbar_arrive_expect_tx(&bar, static_cast<uint32_t>(nsub * KB) * kSubtileBytes + gbytes);
+    __syncwarp();
+    const uint64_t pol = policy_evict_first();
+    for (int i = lane; i < nsub * KB; i += 32) {
+      const int sub = i / KB, b = i - sub * KB;
+      bulk_g2s_hint(w_s + i * kSubtileBytes, W + subtile_offset(S0 + sub, b, KB), kSubtileBytes,
+                    &bar, pol);
+    }
+    if (gamma && lane == 0) bulk_g2s(g_s, gamma, gbytes, &bar);
+  }
+  const int row = S0 * kSubRows + tid;
+  const float sw = (tid < kN1Rows && row < M) ? s_w[row] : 0.0f;
+  pdl_launch_dependents();
+  pdl_wait();  // x may be the previous kernel's output
+
+  float xv[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int col = tid + 256 * j;
+    xv[j] = col < K ? x[col] : 0.0f;
+  }
+  if (tid == 0) {
+    bool ok = mbar_wait(&bar, 0);  // weights + gamma (normally landed long ago)
+    if (!ok) mbar_wait(&bar, 0);
+    ok_s = ok;
+  }
+  __syncthreads();
+  float rms = 1.0f;
+  if (gamma) {
+    float part = 0.0f;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j)
+      if (tid + 256 * j < K) part = __fadd_rn(part, __fmul_rn(xv[j], xv[j]));
+    const float total = tree_sum_256(part, shf);
+    if (tid == 0)
+      scal[0] =
+          __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), eps)));
+    __syncthreads();
+    rms = scal[0];
+  }
+  float lmax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int col = tid + 256 * j;
+    if (gamma && col < K) xv[j] = norm_mul(xv[j], rms, g_s[col]);
+    lmax = fmaxf(lmax, fabsf(xv[j]));
+  }
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, s));
+  if (lane == 0) shf[warp] = lmax;
+  __syncthreads();
+  if (tid == 0) {
+    float absmax = shf[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) absmax = fmaxf(absmax, shf[w]);
+    scal[1] = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
+    scal[2] = absmax == 0.0f ? 0.0f : __fdiv_rn(127.0f, absmax);
+  }
+  __syncthreads();
+  const float inv = scal[2];
+  int qpart = 0;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int col = tid + 256 * j;
+    if (col < K) {
+      const int qi = min(127, max(-127, __float2int_rn(__fmul_rn(xv[j], inv))));
+      q_s[col] = static_cast<int8_t>(qi);
+      qpart += qi;
+    }
+  }
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) qpart += __shfl_xor_sync(0xffffffffu, qpart, s);
+  if (lane == 0) red_q[warp] = qpart;
+  __syncthreads();
+
+  const int sub = warp >> 2;  // warps 0-3: subtile 0, warps 4-7: subtile 1
+  int acc[1] = {0};
+  if (ok_s && sub < nsub)
+    subtile_dot<1>(smem_u32(w_s) + sub * KB * kSubtileBytes, smem_u32(q_s), K, KB, warp & 3,
+                   4, lane, acc);
+  acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 16);
+  if (lane < 16) red[warp][lane] = acc[0];
+  __syncthreads();
+  if (tid < kN1Rows && row < M && ok_s) {
+    const int sb = tid >> 4, r = tid & 15;
+    int a = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) a -= red_q[w];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) a += red[sb * 4 + w][r];
+    // ternary_gemv.wgsl:232 order: (f32(acc) * s_w) * s_x
+    y[row] = __fmul_rn(__fmul_rn(static_cast<float>(a), sw), scal[1]);
   }
 }
 
@@ -373,8 +531,21 @@ cudaError_t gemv_nt(const WeightView& W, const int8_t* q, const float* s_x, cons
   cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return e;
   dim3 grid((W.out_dim + kSubRows - 1) / kSubRows, (n + NT - 1) / NT);
-  return launch_pdl(kern, grid, dim3(128), smem, s, W.w, W.s_w, q, s_x, qsum, y, acc, W.out_dim,
-                    K, n, order);
+  return launch_pdl(kern, grid, dim3(kGemvWarps * 32), smem, s, W.w, W.s_w, q, s_x, qsum, y, acc,
+                    W.out_dim, K, n, order);
+}
+
+template <int EPT>
+cudaError_t bitlinear_n1_ept(const WeightView& W, const float* gamma, float eps, const float* x,
+                             float* y, cudaStream_t s) {
+  const int K = W.in_dim;
+  const size_t smem =
+      2 * static_cast<size_t>(K / kBlockK) * kSubtileBytes + static_cast<size_t>(K) * 5;
+  auto kern = k_bitlinear_n1<EPT>;
+  cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kern), smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((W.out_dim + kN1Rows - 1) / kN1Rows);
+  return launch_pdl(kern, grid, dim3(256), smem, s, W.w, W.s_w, gamma, eps, x, y, W.out_dim, K);
 }
 
 template <bool ACC>
@@ -429,6 +600,26 @@ cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps,
 cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int d, float* y,
                            cudaStream_t s) {
   return launch_pdl(k_rmsnorm, dim3(n), dim3(256), 0, s, x, w, eps, d, y);
+}
+
+cudaError_t launch_bitlinear_n1(const WeightView& W, const float* gamma, float eps,
+                                const float* x, float* y, cudaStream_t s) {
+  const int ept = (W.in_dim + 255) / 256;
+  if (ept <= 1) return bitlinear_n1_ept<1>(W, gamma, eps, x, y, s);
+  if (ept <= 2) return bitlinear_n1_ept<2>(W, gamma, eps, x, y, s);
+  if (ept <= 4) return bitlinear_n1_ept<4>(W, gamma, eps, x, y, s);
+  if (ept <= 8) return bitlinear_n1_ept<8>(W, gamma, eps, x, y, s);
+  if (ept <= 12) return bitlinear_n1_ept<12>(W, gamma, eps, x, y, s);
+  if (ept <= 16) return bitlinear_n1_ept<16>(W, gamma, eps, x, y, s);
+  if (ept <= 20) return bitlinear_n1_ept<20>(W, gamma, eps, x, y, s);
+  if (ept <= 24) return bitlinear_n1_ept<24>(W, gamma, eps, x, y, s);
+  if (ept <= 28) return bitlinear_n1_ept<28>(W, gamma, eps, x, y, s);
+  if (ept <= 32) return bitlinear_n1_ept<32>(W, gamma, eps, x, y, s);
+  if (ept <= 40) return bitlinear_n1_ept<40>(W, gamma, eps, x, y, s);
+  if (ept <= 48) return bitlinear_n1_ept<48>(W, gamma, eps, x, y, s);
+  if (ept <= 56) return bitlinear_n1_ept<56>(W, gamma, eps, x, y, s);
+  if (ept <= 64) return bitlinear_n1_ept<64>(W, gamma, eps, x, y, s);
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_gemv(const WeightView& W, const int8_t* q, const float* s_x,

@@ -38,7 +38,12 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int
 cudaError_t launch_gemv(const WeightView& W, const int8_t* q, const float* s_x,
                         const int32_t* qsum, int n, float* y, int32_t* acc, int order,
                         cudaStream_t s);
-// Largest K the GEMV kernel accepts.
+// One-token BitLinear forward in a single kernel (RMSNorm when gamma != null,
+// quantize, GEMV with ternary_gemv.wgsl's epilogue order). K <= kGemvMaxK.
+cudaError_t launch_bitlinear_n1(const WeightView& W, const float* gamma, float eps,
+                                const float* x, float* y, cudaStream_t s);
+
+// Largest K the GEMV kernels accept.
 constexpr int kGemvMaxK = 16384;
 
 // Device error words (one per translation unit): read and reset.

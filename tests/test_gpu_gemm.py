@@ -1,0 +1,65 @@
+"""GPU parity of the tensor-core (tcgen05 kind::i8) ternary GEMM path.
+
+Token counts >= 16 run on the tensor cores. Shapes cover partial tiles in both
+the weight-row (128) and token (32/64/128/256) dimensions, single and many K
+blocks, one and several tiles per persistent CTA.
+"""
+import numpy as np
+import pytest
+
+import oracle as orc
+from _util import need_cuda, obn, synth
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch():
+    return need_cuda()
+
+
+def run_acc(torch, M, K, n, seed):
+    L = synth().layer(seed, M, K)
+    layer = obn().BitLinear.from_i2s(L.blob(), K, M)
+    q_np = np.random.default_rng(seed + 1).integers(-127, 128, (n, K), dtype=np.int8)
+    q = torch.from_numpy(q_np).cuda()
+    qs = torch.from_numpy(q_np.astype(np.int64).sum(1).astype(np.int32)).cuda()
+    acc = layer.acc(q, qs).cpu().numpy()
+    return acc, orc.ternary_acc(L.packed, q_np, M, K)
+
+
+@pytest.mark.parametrize("M,K,n", [(128, 128, 16), (128, 256, 32), (256, 384, 64)])
+def test_gemm_small_exact(torch, M, K, n):
+    got, want = run_acc(torch, M, K, n, M + K + n)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("M,K,n", [(1, 128, 16), (100, 256, 17), (129, 128, 33), (300, 384, 100),
+                                   (513, 640, 129), (1000, 256, 257), (2560, 2560, 64),
+                                   (6912, 2560, 32), (2560, 6912, 64), (3840, 2560, 300)])
+def test_gemm_acc_bitexact(torch, M, K, n):
+    got, want = run_acc(torch, M, K, n, M * 3 + K + n)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("n", [16, 32, 64, 512])
+def test_gemm_forward_matches_oracle(torch, n):
+    M, K = 2560, 2560
+    L = synth().layer(700 + n, M, K)
+    x = synth().activations(701 + n, n, K)
+    layer = obn().BitLinear.from_i2s(L.blob(), K, M, norm_weight=L.gamma)
+    y = layer.forward(torch.from_numpy(x).cuda()).cpu().numpy()
+    y_ref, _, _ = orc.bitlinear(x, L.packed, L.row_scales(), M, K, norm_w=L.gamma)
+    assert np.array_equal(y, y_ref)
+
+
+def test_gemm_many_tiles_per_cta(torch):
+    # 54 row tiles x 8 token tiles = 432 tiles over <= 148 persistent CTAs.
+    M, K, n = 6912, 256, 2048
+    got, want = run_acc(torch, M, K, n, 9)
+    assert np.array_equal(got, want)
+
+
+def test_gemm_device_errors_clean(torch):
+    torch.cuda.synchronize()
+    obn().check_device_errors()
