@@ -134,6 +134,12 @@ int check_layer(const obn_bitlinear* L) {
 
 }  // namespace
 
+namespace obn {
+// Lets other translation units of the library report through the same
+// thread-local error slot as the entry points in this file.
+int report_error(int code, const char* message) { return fail(code, "%s", message); }
+}  // namespace obn
+
 extern "C" {
 
 int obn_version(void) { return 100; }

@@ -106,6 +106,22 @@ OBN_API size_t obn_bitlinear_workspace_bytes(const obn_bitlinear* layer, int n);
 OBN_API int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, int n, float* y,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference. obn_bitlinear_forward for callers that cannot
+ * allocate device memory: hosts whose device memory is reserved up front by
+ * another allocator, and latency-critical threads that must not call
+ * cudaMalloc/cudaFree (they can block and synchronise the device). The scratch
+ * obn_bitlinear_forward takes as `workspace` lives instead in one fixed device
+ * array of 1 MiB + 32 KiB that every device loading the library holds until the
+ * process exits; the call allocates nothing. Limits: n * in_dim <= 1048576 and
+ * n <= 4096, otherwise OBN_ERR_UNSUPPORTED with a message naming the sizes.
+ * The first call on a device looks the array's device address up (once per
+ * device, with that device current); make that first call before any stream
+ * capture. All calls on a device share the array and it keeps the previous
+ * call's contents (nothing in it needs to start at zero: every byte read is
+ * first written by the same call); calls that overlap on the GPU race on it. */
+OBN_API int obn_bitlinear_forward_noalloc(const obn_bitlinear* layer, const float* x, int n,
+                                          float* y, void* stream);
+
 /* ---- kernel-level entry points (one per reference shader) ------------------ */
 
 /* Fused rmsnorm.wgsl + quantize.wgsl: per token, optional RMSNorm with gamma
