@@ -1,7 +1,7 @@
 // abi.cu — the extern "C" surface declared in include/obn.h.
 //
 // Host-side BitLinear: validation, the one-time repack of I2_S weights into the
-// T256 device layout (layout.cuh), workspace partitioning and kernel dispatch.
+// T16 device layout (layout.cuh), workspace partitioning and kernel dispatch.
 // Error handling follows the reference's C ABI: a status return plus a
 // thread-local message (packages/rust/crates/oxbitnet-ffi/src/lib.rs:31-46).
 #include <cstdarg>
@@ -21,7 +21,7 @@ struct obn_bitlinear {
   int out_dim = 0;  // M
   int m_pad = 0;
   float eps = 1e-5f;
-  uint8_t* w = nullptr;     // T256 layout, m_pad * K / 4 bytes
+  uint8_t* w = nullptr;     // T16 layout, m_pad * K / 4 bytes
   float* s_w = nullptr;     // [m_pad]
   float* norm = nullptr;    // [K] or null
 };
@@ -102,7 +102,7 @@ int alloc_layer(int in_dim, int out_dim, float eps, obn_bitlinear** out) {
   cudaGetDevice(&L->device);
   L->in_dim = in_dim;
   L->out_dim = out_dim;
-  L->m_pad = obn::round_up(out_dim, obn::kPanelRows);
+  L->m_pad = obn::round_up(out_dim, obn::kTileRows);
   L->eps = eps;
   const size_t wbytes = static_cast<size_t>(L->m_pad) * in_dim / 4;
   cudaError_t e = cudaMalloc(&L->w, wbytes);

@@ -6,13 +6,16 @@
 // dimension BN tokens, so D[m, n] lives in TMEM with one weight row per lane and
 // the epilogue's stores of Out[n, m] are 128-byte coalesced runs over m.
 //
-// Per 128-element K block (one I2_S block) a pipeline stage holds:
-//   P: the 128 rows' packed 2-bit weights, 4 KB, one contiguous bulk copy
-//      (T256 layout: a half panel of one block is contiguous);
-//   B: BN tokens x 128 int8 activations, TMA 2D tile, 128-byte swizzle;
-//   A: P expanded to unsigned 8-bit codes c = w + 1 in the UMMA K-major
-//      128-byte-swizzle layout (row r at (r/8)*1024 + (r%8)*128, 16-byte chunk
-//      j stored at chunk j ^ (r%8)).
+// A pipeline stage covers KSTG 128-element K blocks (one block = one I2_S block):
+//   P: the 128 rows' packed 2-bit weights, KSTG x 4 KB, one 3D TMA copy from the
+//      T16 layout (box: 512 bytes x KSTG blocks x 8 subtiles);
+//   B: BN tokens x KSTG*128 int8 activations, one 3D TMA copy with 128-byte
+//      swizzle landing as KSTG K-major [BN][128] tiles;
+//   A: P expanded to unsigned 8-bit codes c = w + 1, either in tensor memory
+//      (A_TMEM: one TMEM lane per weight row, 32 columns of 4 codes, written
+//      with tcgen05.st — keeps the 16 KB tile off the shared-memory port the MMA
+//      reads B through) or in shared memory in the UMMA K-major 128-byte-swizzle
+//      layout (row r at (r/8)*1024 + (r%8)*128, 16-byte chunk j at chunk j ^ (r%8)).
 // The MMA accumulates sum_k c q = sum_k w q + sum_k q; the epilogue subtracts
 // the per-token code sum qsum[n] (exact, integer).
 //
@@ -35,9 +38,9 @@ namespace obn {
 namespace {
 
 constexpr int kBM = 128;           // weight rows per tile (MMA M)
-constexpr int kBK = 128;           // K elements per stage (one I2_S block)
+constexpr int kBK = 128;           // K elements per block (one I2_S block)
 constexpr int kThreads = 384;
-constexpr int kPackedStage = kBM * 32;  // 4096 bytes of packed weights per stage
+constexpr int kPackedBlock = kBM * 32;  // 4096 bytes of packed weights per block
 
 struct GemmSmem {
   uint64_t full_tma[8];
@@ -79,6 +82,29 @@ OBN_DEVINL void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t
       : "memory");
 }
 
+OBN_DEVINL void mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+OBN_DEVINL void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+      "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]),
+      "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]),
+      "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+OBN_DEVINL void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Arrives on `bar` once every tcgen05 operation issued so far by this thread
 // has completed.
 OBN_DEVINL void mma_commit(uint64_t* bar) {
@@ -99,14 +125,25 @@ OBN_DEVINL void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
       : "r"(taddr)
       : "memory");
 }
+OBN_DEVINL void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
 OBN_DEVINL void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// 2D tiled TMA load (no multicast) completing on `bar`.
-OBN_DEVINL void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+// 3D tiled TMA load (no multicast) completing on `bar`.
+OBN_DEVINL void tma_load_3d(void* smem_dst, const CUtensorMap* map, int x, int y, int z,
+                            uint64_t* bar) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
-      "{%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3, %4}], [%5];" ::"r"(smem_u32(smem_dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -141,40 +178,48 @@ OBN_DEVINL bool wait_or_abort(GemmSmem* sm, uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KSTG, bool A_TMEM>
 __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CUtensorMap tmap_q,
-                                                      const uint8_t* __restrict__ W,
+                                                      const __grid_constant__ CUtensorMap tmap_w,
                                                       const float* __restrict__ s_w,
                                                       const float* __restrict__ s_x,
                                                       const int32_t* __restrict__ qsum,
                                                       float* __restrict__ y,
                                                       int32_t* __restrict__ acc_out, int M, int N,
                                                       int K, int order) {
+  constexpr int kAStage = KSTG * kBM * kBK;      // expanded A bytes per stage (smem variant)
+  constexpr int kBStage = KSTG * BN * kBK;       // activation bytes per stage
+  constexpr int kPStage = KSTG * kPackedBlock;   // packed weight bytes per stage
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* sA = base;                                   // STAGES x 16 KB
-  uint8_t* sB = sA + STAGES * kBM * kBK;                // STAGES x BN*128
-  uint8_t* sP = sB + STAGES * BN * kBK;                 // STAGES x 4 KB
-  GemmSmem* sm = reinterpret_cast<GemmSmem*>(sP + STAGES * kPackedStage);
+  uint8_t* sA = base;                                  // STAGES x kAStage (A in shared memory)
+  uint8_t* sB = sA + (A_TMEM ? 0 : STAGES * kAStage);  // STAGES x kBStage
+  uint8_t* sP = sB + STAGES * kBStage;                 // STAGES x kPStage
+  GemmSmem* sm = reinterpret_cast<GemmSmem*>(sP + STAGES * kPStage);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int KB = K / kBK;
+  const int n_stages = (KB + KSTG - 1) / KSTG;  // a missing last block is zero-filled by TMA
   const int num_m = (M + kBM - 1) / kBM;
   const int num_n = (N + BN - 1) / BN;
   const int tiles = num_m * num_n;
-  constexpr uint32_t kTmemCols = (2 * BN < 32) ? 32 : 2 * BN;
+  // TMEM columns: two BN-wide accumulators, then (A_TMEM) 32 columns per block per stage.
+  constexpr uint32_t kTmemNeed = 2 * BN + (A_TMEM ? 32 * KSTG * STAGES : 0);
+  constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
+                                 : kTmemNeed <= 256 ? 256 : 512;
+  static_assert(kTmemNeed <= 512, "TMEM budget");
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&sm->full_tma[s], 1);
-      mbar_init(&sm->full_a[s], 128);
+      mbar_init(&sm->full_a[s], 4);  // one arrival per expansion warp
       mbar_init(&sm->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&sm->accf[a], 1);
-      mbar_init(&sm->acce[a], 128);
+      mbar_init(&sm->acce[a], 4);  // one arrival per epilogue warp
     }
     mbar_init(&sm->drain, 1);
     sm->abort_flag = 0;
@@ -192,106 +237,160 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // The whole warp runs the loop (converged); one lane issues the copies.
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_q) : "memory");
-      const uint64_t pol = policy_evict_last();  // weights are re-read by every token tile
-      int it = 0;
-      bool waited = false;
-      for (int t = blockIdx.x; t < tiles && !sm->abort_flag; t += gridDim.x) {
-        const int mt = t % num_m, nt = t / num_m;
-        const uint8_t* wsrc = W + (static_cast<size_t>(mt >> 1) * KB * 16 + (mt & 1) * 8) *
-                                      kSubtileBytes;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1u;
-          if (!wait_or_abort(sm, &sm->empty[s], ph ^ 1u)) break;
-          mbar_arrive_expect_tx(&sm->full_tma[s], BN * kBK + kPackedStage);
-          bulk_g2s_hint(sP + s * kPackedStage, wsrc + static_cast<size_t>(kb) * 16 * kSubtileBytes,
-                        kPackedStage, &sm->full_tma[s], pol);
-          if (!waited) {  // q comes from the previous kernel; the weights do not
-            pdl_wait();
-            waited = true;
-          }
-          tma_load_2d(sB + s * BN * kBK, &tmap_q, kb * kBK, nt * BN, &sm->full_tma[s]);
-        }
-      }
-      if (!waited) pdl_wait();
-      // Drain: wait (bounded) for every copy this thread issued before exiting.
-      const int last = it;
-      for (int j = (last > STAGES ? last - STAGES : 0); j < last; ++j)
-        mbar_wait(&sm->full_tma[j % STAGES], (j / STAGES) & 1u);
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_w) : "memory");
     }
+    int it = 0;
+    bool waited = false;
+    for (int t = blockIdx.x; t < tiles && !sm->abort_flag; t += gridDim.x) {
+      const int mt = t % num_m, nt = t / num_m;
+      bool ok = true;
+      for (int st = 0; st < n_stages; ++st, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1u;
+        if (!wait_or_abort(sm, &sm->empty[s], ph ^ 1u)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&sm->full_tma[s], kBStage + kPStage);
+          tma_load_3d(sP + s * kPStage, &tmap_w, 0, st * KSTG, mt * (kBM / kSubRows),
+                      &sm->full_tma[s]);
+        }
+        if (!waited) {  // q comes from the previous kernel; the weights do not
+          pdl_wait();
+          waited = true;
+        }
+        if (lane == 0)
+          tma_load_3d(sB + s * kBStage, &tmap_q, 0, nt * BN, st * KSTG, &sm->full_tma[s]);
+        __syncwarp();
+      }
+      if (!ok) break;
+    }
+    if (!waited) pdl_wait();
+    // Drain: wait (bounded) for every copy this warp issued before exiting.
+    const int last = it;
+    for (int j = (last > STAGES ? last - STAGES : 0); j < last; ++j)
+      mbar_wait(&sm->full_tma[j % STAGES], (j / STAGES) & 1u);
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Converged warp; one lane issues the MMAs and commits.
     pdl_wait();
-    if (lane == 0) {
-      int it = 0, ti = 0;
-      constexpr uint32_t idesc = idesc_i8<BN>();
-      for (int t = blockIdx.x; t < tiles && !sm->abort_flag; t += gridDim.x, ++ti) {
-        const int a = ti & 1;
-        const uint32_t aph = (ti >> 1) & 1u;
-        if (!wait_or_abort(sm, &sm->acce[a], aph ^ 1u)) break;
+    int it = 0, ti = 0;
+    constexpr uint32_t idesc = idesc_i8<BN>();
+    for (int t = blockIdx.x; t < tiles && !sm->abort_flag; t += gridDim.x, ++ti) {
+      const int a = ti & 1;
+      const uint32_t aph = (ti >> 1) & 1u;
+      if (!wait_or_abort(sm, &sm->acce[a], aph ^ 1u)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem + a * BN;
+      bool ok = true;
+      for (int st = 0; st < n_stages; ++st, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1u;
+        if (!wait_or_abort(sm, &sm->full_tma[s], ph) || !wait_or_abort(sm, &sm->full_a[s], ph)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t d_tmem = tmem + a * BN;
-        bool ok = true;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1u;
-          if (!wait_or_abort(sm, &sm->full_tma[s], ph) || !wait_or_abort(sm, &sm->full_a[s], ph)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + s * kBM * kBK);
-          const uint32_t b_addr = smem_u32(sB + s * BN * kBK);
+        if (lane == 0) {
 #pragma unroll
-          for (int kk = 0; kk < kBK / 32; ++kk)
-            mma_i8(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
-                   (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int bb = 0; bb < KSTG; ++bb) {
+            const uint32_t b_addr = smem_u32(sB + s * kBStage + bb * BN * kBK);
+            if (A_TMEM) {
+              const uint32_t a_tmem = tmem + 2 * BN + (s * KSTG + bb) * 32;
+#pragma unroll
+              for (int kk = 0; kk < kBK / 32; ++kk)
+                mma_i8_ts(d_tmem, a_tmem + kk * 8, sw128_desc(b_addr + kk * 32), idesc,
+                          (st > 0 || bb > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              const uint32_t a_addr = smem_u32(sA + s * kAStage + bb * kBM * kBK);
+#pragma unroll
+              for (int kk = 0; kk < kBK / 32; ++kk)
+                mma_i8(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
+                       (st > 0 || bb > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
           mma_commit(&sm->empty[s]);
         }
-        if (!ok) break;
-        mma_commit(&sm->accf[a]);
+        __syncwarp();
       }
-      // Every MMA issued by this thread must finish before TMEM is released.
-      mma_commit(&sm->drain);
-      mbar_wait(&sm->drain, 0);
+      if (!ok) break;
+      if (lane == 0) mma_commit(&sm->accf[a]);
+      __syncwarp();
     }
+    // Every MMA issued by this warp must finish before TMEM is released.
+    if (lane == 0) mma_commit(&sm->drain);
+    __syncwarp();
+    mbar_wait(&sm->drain, 0);
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ expansion
     pdl_wait();
-    const int r = tid - 128;  // weight row within the tile
+    const int r = tid - 128;  // weight row within the tile = TMEM lane
     const int sub = r >> 4, rr = r & 15;
-    const uint32_t swz = static_cast<uint32_t>(r & 7);
     int it = 0;
     for (int t = blockIdx.x; t < tiles && !sm->abort_flag; t += gridDim.x) {
       bool ok = true;
-      for (int kb = 0; kb < KB; ++kb, ++it) {
+      for (int st = 0; st < n_stages; ++st, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1u;
         if (!wait_or_abort(sm, &sm->full_tma[s], ph)) {
           ok = false;
           break;
         }
-        const uint8_t* p = sP + s * kPackedStage + sub * kSubtileBytes + rr * 16;
-        uint8_t* arow = sA + s * kBM * kBK + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint4 w = *reinterpret_cast<const uint4*>(p + h * 256);
+        for (int bb = 0; bb < KSTG; ++bb) {
+          // P stage layout [8 subtiles][KSTG blocks][512 B]
+          const uint8_t* p = sP + s * kPStage + (sub * KSTG + bb) * kSubtileBytes + rr * 16;
+          if (A_TMEM) {
+            // Row r's 128 codes as 32 words, word j = codes of k = 4j .. 4j+3; the
+            // 16-k chunk c = 2g + h is words 4c .. 4c+3.
+            uint32_t v[32];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int sh = 6 - 2 * g;
-            uint4 c;
-            c.x = (w.x >> sh) & 0x03030303u;
-            c.y = (w.y >> sh) & 0x03030303u;
-            c.z = (w.z >> sh) & 0x03030303u;
-            c.w = (w.w >> sh) & 0x03030303u;
-            const uint32_t chunk = static_cast<uint32_t>(2 * g + h) ^ swz;
-            *reinterpret_cast<uint4*>(arow + chunk * 16) = c;
+            for (int h = 0; h < 2; ++h) {
+              const uint4 w = *reinterpret_cast<const uint4*>(p + h * 256);
+#pragma unroll
+              for (int g = 0; g < 4; ++g) {
+                const int sh = 6 - 2 * g, c = 2 * g + h;
+                v[4 * c + 0] = (w.x >> sh) & 0x03030303u;
+                v[4 * c + 1] = (w.y >> sh) & 0x03030303u;
+                v[4 * c + 2] = (w.z >> sh) & 0x03030303u;
+                v[4 * c + 3] = (w.w >> sh) & 0x03030303u;
+              }
+            }
+            tmem_st32(tmem + (static_cast<uint32_t>(r & ~31) << 16) + 2 * BN + (s * KSTG + bb) * 32,
+                      v);
+          } else {
+            uint8_t* arow = sA + s * kAStage + bb * kBM * kBK + (r >> 3) * 1024 + (r & 7) * 128;
+            const uint32_t swz = static_cast<uint32_t>(r & 7);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint4 w = *reinterpret_cast<const uint4*>(p + h * 256);
+#pragma unroll
+              for (int g = 0; g < 4; ++g) {
+                const int sh = 6 - 2 * g;
+                uint4 c;
+                c.x = (w.x >> sh) & 0x03030303u;
+                c.y = (w.y >> sh) & 0x03030303u;
+                c.z = (w.z >> sh) & 0x03030303u;
+                c.w = (w.w >> sh) & 0x03030303u;
+                const uint32_t chunk = static_cast<uint32_t>(2 * g + h) ^ swz;
+                *reinterpret_cast<uint4*>(arow + chunk * 16) = c;
+              }
+            }
           }
         }
-        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
-        mbar_arrive(&sm->full_a[s]);
+        if (A_TMEM) {
+          tmem_st_wait();
+          tc_fence_before();
+        } else {
+          fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm->full_a[s]);
       }
       if (!ok) break;
     }
@@ -310,30 +409,36 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
       const float sw = (m < M && !acc_out) ? s_w[m] : 0.0f;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
 #pragma unroll 1
-      for (int j0 = 0; j0 < BN; j0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(taddr + j0, v);
+      for (int j0 = 0; j0 < BN; j0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(taddr + j0, v);
         tmem_ld_wait();
         const int n0 = nt * BN + j0;
+        // Column j's code sum and scale, fetched once per warp and broadcast.
+        const int nl = n0 + (lane & 15);
+        const int qs_l = nl < N ? qsum[nl] : 0;
+        const float sx_l = (nl < N && !acc_out) ? s_x[nl] : 0.0f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < 16; ++j) {
           const int n = n0 + j;
+          const int qs_j = __shfl_sync(0xffffffffu, qs_l, j);
+          const float sx_j = __shfl_sync(0xffffffffu, sx_l, j);
           if (n < N && m < M) {
-            const int d = static_cast<int>(v[j]) - qsum[n];
+            const int d = static_cast<int>(v[j]) - qs_j;
             const size_t o = static_cast<size_t>(n) * M + m;
             if (acc_out) {
               acc_out[o] = d;
             } else {
               const float fd = static_cast<float>(d);
-              const float sx = s_x[n];
-              y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx)
-                                         : __fmul_rn(fd, __fmul_rn(sw, sx));
+              y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx_j)
+                                         : __fmul_rn(fd, __fmul_rn(sw, sx_j));
             }
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(&sm->acce[a]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm->acce[a]);
     }
   }
 
@@ -362,9 +467,11 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KSTG, bool A_TMEM>
 size_t gemm_smem_bytes() {
-  return 1024 + static_cast<size_t>(STAGES) * (kBM * kBK + BN * kBK + kPackedStage) +
+  return 1024 +
+         static_cast<size_t>(STAGES) *
+             ((A_TMEM ? 0 : KSTG * kBM * kBK) + KSTG * BN * kBK + KSTG * kPackedBlock) +
          sizeof(GemmSmem);
 }
 
@@ -377,22 +484,49 @@ int num_sms() {
   return sms[dev] ? sms[dev] : 148;
 }
 
-template <int BN, int STAGES>
+// Activations q [n][K] int8 viewed as 3D {128 bytes of a block, n tokens, KB blocks}
+// so one box brings KSTG K-major [BN][128] tiles; 128-byte swizzle for the MMA.
+bool make_q_map(CUtensorMap* map, const int8_t* q, int n, int K, int BN, int KSTG) {
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kBK), static_cast<cuuint64_t>(n),
+                              static_cast<cuuint64_t>(K / kBK)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(kBK)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(BN),
+                             static_cast<cuuint32_t>(KSTG)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(q), dims, strides,
+                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// T16 weights viewed as 3D u32 {128 words of a subtile block, KB blocks, m_pad/16
+// subtiles}; one box = KSTG blocks of 8 subtiles (a 128-row tile), no swizzle.
+bool make_w_map(CUtensorMap* map, const WeightView& W, int KSTG) {
+  const int KB = W.in_dim / kBK;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kSubtileBytes / 4),
+                              static_cast<cuuint64_t>(KB),
+                              static_cast<cuuint64_t>(W.m_pad / kSubRows)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(kSubtileBytes),
+                                 static_cast<cuuint64_t>(KB) * kSubtileBytes};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kSubtileBytes / 4),
+                             static_cast<cuuint32_t>(KSTG),
+                             static_cast<cuuint32_t>(kBM / kSubRows)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<uint8_t*>(W.w), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES, int KSTG, bool A_TMEM>
 cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, const int32_t* qsum,
                     int n, float* y, int32_t* acc, int order, cudaStream_t s) {
-  EncodeTiledFn enc = encode_fn();
-  if (!enc) return cudaErrorNotSupported;
-  CUtensorMap map;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(W.in_dim), static_cast<cuuint64_t>(n)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(W.in_dim)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(BN)};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(q), dims, strides,
-                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  const size_t smem = gemm_smem_bytes<BN, STAGES>();
-  auto kern = k_gemm<BN, STAGES>;
+  if (!encode_fn()) return cudaErrorNotSupported;
+  CUtensorMap qmap, wmap;
+  if (!make_q_map(&qmap, q, n, W.in_dim, BN, KSTG) || !make_w_map(&wmap, W, KSTG))
+    return cudaErrorInvalidValue;
+  const size_t smem = gemm_smem_bytes<BN, STAGES, KSTG, A_TMEM>();
+  auto kern = k_gemm<BN, STAGES, KSTG, A_TMEM>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -414,23 +548,24 @@ cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, cons
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, map, W.w, W.s_w, s_x, qsum, y, acc, W.out_dim, n,
+  return cudaLaunchKernelEx(&cfg, kern, qmap, wmap, W.s_w, s_x, qsum, y, acc, W.out_dim, n,
                             W.in_dim, order);
 }
 
 }  // namespace
 
 bool gemm_supported(const WeightView& W, int n) {
-  return n >= kGemmMinTokens && W.in_dim % kBK == 0 && encode_fn() != nullptr;
+  return n >= kGemmMinTokens && W.in_dim % kBK == 0 && W.m_pad % kBM == 0 && encode_fn() != nullptr;
 }
 
 cudaError_t launch_gemm(const WeightView& W, const int8_t* q, const float* s_x,
                         const int32_t* qsum, int n, float* y, int32_t* acc, int order,
                         cudaStream_t s) {
-  if (n <= 32) return gemm_bn<32, 8>(W, q, s_x, qsum, n, y, acc, order, s);
-  if (n <= 64) return gemm_bn<64, 6>(W, q, s_x, qsum, n, y, acc, order, s);
-  if (n <= 128) return gemm_bn<128, 5>(W, q, s_x, qsum, n, y, acc, order, s);
-  return gemm_bn<256, 4>(W, q, s_x, qsum, n, y, acc, order, s);
+  if (n <= 16) return gemm_bn<16, 6, 2, true>(W, q, s_x, qsum, n, y, acc, order, s);
+  if (n <= 32) return gemm_bn<32, 6, 2, true>(W, q, s_x, qsum, n, y, acc, order, s);
+  if (n <= 64) return gemm_bn<64, 5, 2, true>(W, q, s_x, qsum, n, y, acc, order, s);
+  if (n <= 128) return gemm_bn<128, 4, 2, true>(W, q, s_x, qsum, n, y, acc, order, s);
+  return gemm_bn<256, 4, 1, false>(W, q, s_x, qsum, n, y, acc, order, s);
 }
 
 cudaError_t read_and_clear_dev_error_gemm(uint32_t* out) {

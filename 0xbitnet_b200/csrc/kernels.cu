@@ -39,8 +39,8 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 // ---------------------------------------------------------------------------
 // Repack / export
 // ---------------------------------------------------------------------------
-// One thread per 16-byte half, enumerated in destination order so the T256
-// writes are contiguous: i = ((((panel*KB + b)*16 + s)*2 + h)*16 + r).
+// One thread per 16-byte half, enumerated in destination order so the T16
+// writes are contiguous: i = ((S*KB + b)*2 + h)*16 + r, row m = 16*S + r.
 __global__ void k_repack(const uint8_t* __restrict__ rows, uint8_t* __restrict__ t, int M, int K,
                          int m_pad) {
   const int KB = K / kBlockK;
@@ -51,11 +51,9 @@ __global__ void k_repack(const uint8_t* __restrict__ rows, uint8_t* __restrict__
     size_t j = i / 16;
     const int h = static_cast<int>(j % 2);
     j /= 2;
-    const int s = static_cast<int>(j % 16);
-    j /= 16;
     const int b = static_cast<int>(j % KB);
-    const int panel = static_cast<int>(j / KB);
-    const int m = panel * kPanelRows + s * kSubRows + r;
+    const int S = static_cast<int>(j / KB);
+    const int m = S * kSubRows + r;
     uint4 v = make_uint4(0x55555555u, 0x55555555u, 0x55555555u, 0x55555555u);
     if (m < M)
       v = *reinterpret_cast<const uint4*>(rows + static_cast<size_t>(m) * (K / 4) + b * 32 + h * 16);
@@ -272,16 +270,17 @@ OBN_DEVINL void subtile_dot(uint32_t w_s, uint32_t q_s, int ldq, int KB, int fir
     acc[t] += (a[t][0] >> 6) + (a[t][1] >> 4) + (a[t][2] >> 2) + a[t][3];
 }
 
-// Issues the bulk copies of subtile S's KB blocks (warp 0) on `bar`, with
-// `extra` more expected bytes announced for copies the caller adds.
+// Issues the bulk copy of subtile S's KB blocks (one contiguous KB*512-byte
+// run) on `bar` (lane 0 of the calling warp), announcing `extra_bytes` more for
+// copies the caller adds.
 OBN_DEVINL void prefetch_subtile(uint8_t* w_s, const uint8_t* W, int S, int KB, uint64_t* bar,
                                  uint32_t extra_bytes, int lane) {
-  if (lane == 0)
-    mbar_arrive_expect_tx(bar, static_cast<uint32_t>(KB) * kSubtileBytes + extra_bytes);
+  if (lane == 0) {
+    const uint32_t bytes = static_cast<uint32_t>(KB) * kSubtileBytes;
+    mbar_arrive_expect_tx(bar, bytes + extra_bytes);
+    bulk_g2s_hint(w_s, W + subtile_offset(S, 0, KB), bytes, bar, policy_evict_first());
+  }
   __syncwarp();
-  const uint64_t pol = policy_evict_first();
-  for (int b = lane; b < KB; b += 32)
-    bulk_g2s_hint(w_s + b * kSubtileBytes, W + subtile_offset(S, b, KB), kSubtileBytes, bar, pol);
 }
 
 template <int NT, bool ACC>
@@ -400,17 +399,14 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
   }
   __syncthreads();
   if (warp == 0) {
-    const uint32_t gbytes = gamma ? static_cast<uint32_t>(K) * 4u : 0u;
-    if (lane == 0)
-      mbar_arrive_expect_tx(&bar, static_cast<uint32_t>(nsub * KB) * kSubtileBytes + gbytes);
-    __syncwarp();
-    const uint64_t pol = policy_evict_first();
-    for (int i = lane; i < nsub * KB; i += 32) {
-      const int sub = i / KB, b = i - sub * KB;
-      bulk_g2s_hint(w_s + i * kSubtileBytes, W + subtile_offset(S0 + sub, b, KB), kSubtileBytes,
-                    &bar, pol);
+    if (lane == 0) {  // both subtiles are one contiguous run in the T16 layout
+      const uint32_t gbytes = gamma ? static_cast<uint32_t>(K) * 4u : 0u;
+      const uint32_t wbytes = static_cast<uint32_t>(nsub * KB) * kSubtileBytes;
+      mbar_arrive_expect_tx(&bar, wbytes + gbytes);
+      bulk_g2s_hint(w_s, W + subtile_offset(S0, 0, KB), wbytes, &bar, policy_evict_first());
+      if (gamma) bulk_g2s(g_s, gamma, gbytes, &bar);
     }
-    if (gamma && lane == 0) bulk_g2s(g_s, gamma, gbytes, &bar);
+    __syncwarp();
   }
   const int row = S0 * kSubRows + tid;
   const float sw = (tid < kN1Rows && row < M) ? s_w[row] : 0.0f;
@@ -423,10 +419,13 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
     const int col = tid + 256 * j;
     xv[j] = col < K ? x[col] : 0.0f;
   }
-  if (tid == 0) {
-    bool ok = mbar_wait(&bar, 0);  // weights + gamma (normally landed long ago)
-    if (!ok) mbar_wait(&bar, 0);
-    ok_s = ok;
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = mbar_wait(&bar, 0);  // weights + gamma (normally landed long ago)
+      if (!ok) mbar_wait(&bar, 0);
+      ok_s = ok;
+    }
+    __syncwarp();
   }
   __syncthreads();
   float rms = 1.0f;

@@ -14,17 +14,17 @@ enum EpilogueOrder : int {
 };
 
 struct WeightView {
-  const uint8_t* w;   // T256 layout (layout.cuh)
+  const uint8_t* w;   // T16 layout (layout.cuh)
   const float* s_w;   // [m_pad] per-row scales
   int in_dim;         // K
   int out_dim;        // M
-  int m_pad;          // M rounded up to 256
+  int m_pad;          // M rounded up to 128
 };
 
-// I2_S rows [M][K/4] -> T256 (rows >= M filled with code 1).
+// I2_S rows [M][K/4] -> T16 (rows >= M filled with code 1).
 cudaError_t launch_repack_i2s(const uint8_t* rows, uint8_t* t256, int M, int K, int m_pad,
                               cudaStream_t s);
-// T256 -> I2_S rows [M][K/4].
+// T16 -> I2_S rows [M][K/4].
 cudaError_t launch_export_i2s(const uint8_t* t256, uint8_t* rows, int M, int K, cudaStream_t s);
 
 // Fused RMSNorm (norm_w may be null) + absmax int8 quantize; qsum nullable.

@@ -1,4 +1,4 @@
-// layout.cuh — the device weight layout ("T256") and its index arithmetic.
+// layout.cuh — the device weight layout ("T16") and its index arithmetic.
 //
 // GGUF I2_S stores each output row m as in_dim/4 bytes: 128-element blocks of
 // 32 bytes, byte gp of a block holding elements gp, 32+gp, 64+gp, 96+gp in bits
@@ -10,33 +10,31 @@
 //
 // The repack keeps every 16-byte half intact and only moves it:
 //
-//   rows are padded to a multiple of 256 with code 1 (weight 0); then
+//   rows are padded to a multiple of 128 with code 1 (weight 0); then
 //   byte offset of (row m, block b, half h) =
-//       ((((m/256) * KB + b) * 16 + (m%256)/16) * 2 + h) * 256 + (m%16) * 16
-//   with KB = in_dim / 128.
+//       ((m/16) * KB + b) * 512 + h * 256 + (m%16) * 16,   KB = in_dim / 128.
 //
-// So a (256-row panel, block) pair is one contiguous 8 KB tile — one bulk copy
-// per pipeline stage for the tensor-core GEMM — and inside it each 16-row
-// subtile is 512 contiguous bytes ordered [half][row][16 B]: a warp reads a
-// subtile's block with one fully coalesced 512-byte access, lane = half*16+row.
+// A 16-row subtile is one contiguous KB * 512-byte run (a single bulk copy for a
+// GEMV CTA); inside it each block is 512 bytes ordered [half][row][16 B], so a
+// warp reads a subtile's block with one fully coalesced 512-byte access (lane =
+// half*16 + row). The tensor-core GEMM fetches a 128-row x 2-block stage with a
+// single 3D TMA copy (box: 512 bytes x 2 blocks x 8 subtiles).
 #pragma once
 
 #include <cstdint>
 
 namespace obn {
 
-constexpr int kPanelRows = 256;     // rows per contiguous panel
-constexpr int kSubRows = 16;        // rows per 512-byte subtile
+constexpr int kTileRows = 128;      // row padding (one GEMM weight tile)
+constexpr int kSubRows = 16;        // rows per subtile
 constexpr int kBlockK = 128;        // elements per I2_S block
-constexpr int kSubtileBytes = 512;  // 16 rows x 32 bytes
-constexpr int kPanelBlockBytes = kPanelRows * 32;  // 8192
+constexpr int kSubtileBytes = 512;  // one block of one subtile: 16 rows x 32 bytes
 
 __host__ __device__ inline int round_up(int a, int b) { return (a + b - 1) / b * b; }
 
-// Byte offset of the 512-byte subtile (global subtile index S = m/16, block b).
+// Byte offset of block b of subtile S (= m / 16).
 __host__ __device__ inline size_t subtile_offset(int S, int b, int KB) {
-  const int panel = S / 16, s = S % 16;
-  return ((static_cast<size_t>(panel) * KB + b) * 16 + s) * kSubtileBytes;
+  return (static_cast<size_t>(S) * KB + b) * kSubtileBytes;
 }
 
 // Byte offset of the 16-byte half (row m, block b, half h).
