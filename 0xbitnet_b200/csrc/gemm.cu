@@ -448,6 +448,274 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
   if (warp == 2) tmem_dealloc(tmem, kTmemCols);
 }
 
+// ---- split-K over a thread-block cluster ---------------------------------------------
+//
+// Decode-sized token counts leave too few 128-row tiles to occupy the GPU
+// (e.g. 20 tiles for a 2560-row layer). k_gemm_sk gives each tile a cluster of
+// S CTAs (S <= 8) that split its K stages; each CTA accumulates its partial in
+// its own TMEM. The reduction is a reduce-scatter over distributed shared
+// memory: rank r owns rows [r*RB, r*RB+RB) of the tile (RB = ceil(128/S)); every
+// rank stores its partial rows to their owner's buffer slot [src][row][col]
+// (st.shared::cluster) and arrives on the owner's mbarrier with cluster-scope
+// release; the owner sums the S slots in rank order (integers: exact) and
+// writes the outputs.
+
+OBN_DEVINL uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+OBN_DEVINL void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+OBN_DEVINL uint32_t map_rank(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+OBN_DEVINL void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b),
+               "r"(c), "r"(d)
+               : "memory");
+}
+OBN_DEVINL void mbar_arrive_cluster(uint32_t cluster_bar_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   cluster_bar_addr)
+               : "memory");
+}
+OBN_DEVINL bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr int kRedRows = 136;
+constexpr int kSplitKEnabled = 0;  // >= S * ceil(128 / S) for every S <= 8
+
+template <int BN, int STAGES, int KSTG>
+__global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__ CUtensorMap tmap_q,
+                                                         const __grid_constant__ CUtensorMap tmap_w,
+                                                         const float* __restrict__ s_w,
+                                                         const float* __restrict__ s_x,
+                                                         const int32_t* __restrict__ qsum,
+                                                         float* __restrict__ y,
+                                                         int32_t* __restrict__ acc_out, int M,
+                                                         int N, int K, int order) {
+  constexpr int kBStage = KSTG * BN * kBK;
+  constexpr int kPStage = KSTG * kPackedBlock;
+  constexpr int BNP = BN + 4;  // padded reduction row (ints): conflict-free lane strides
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sB = base;                                            // STAGES x kBStage
+  uint8_t* sP = sB + STAGES * kBStage;                           // STAGES x kPStage
+  int32_t* red = reinterpret_cast<int32_t*>(sP + STAGES * kPStage);  // [S][RB][BNP]
+  GemmSmem* sm = reinterpret_cast<GemmSmem*>(red + kRedRows * BNP);
+  uint64_t* red_full = &sm->acce[0];  // reused: arrivals from every epilogue warp of the cluster
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t S = gridDim.x;  // cluster = the whole x dimension
+  const uint32_t rank = cluster_ctarank();
+  const int mt = blockIdx.y;
+  const int KB = K / kBK;
+  const int total_st = (KB + KSTG - 1) / KSTG;
+  const int st0 = static_cast<int>(rank * total_st / S);
+  const int st1 = static_cast<int>((rank + 1) * total_st / S);
+  const int nst = st1 - st0;
+  const int RB = (kBM + static_cast<int>(S) - 1) / static_cast<int>(S);
+  constexpr uint32_t kTmemNeed = BN + 32 * KSTG * STAGES;
+  constexpr uint32_t kTmemCols = kTmemNeed <= 128 ? 128 : kTmemNeed <= 256 ? 256 : 512;
+  static_assert(kTmemNeed <= 512, "TMEM budget");
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sm->full_tma[s], 1);
+      mbar_init(&sm->full_a[s], 4);
+      mbar_init(&sm->empty[s], 1);
+    }
+    mbar_init(&sm->accf[0], 1);
+    mbar_init(red_full, 4 * S);
+    mbar_init(&sm->drain, 1);
+    sm->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(&sm->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // every CTA's barriers exist before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = sm->tmem_base;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_q) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_w) : "memory");
+    }
+    bool waited = false;
+    int it = 0;
+    for (; it < nst; ++it) {
+      const int s = it % STAGES;
+      const uint32_t ph = (it / STAGES) & 1u;
+      if (!wait_or_abort(sm, &sm->empty[s], ph ^ 1u)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&sm->full_tma[s], kBStage + kPStage);
+        tma_load_3d(sP + s * kPStage, &tmap_w, 0, (st0 + it) * KSTG, mt * (kBM / kSubRows),
+                    &sm->full_tma[s]);
+      }
+      if (!waited) {
+        pdl_wait();
+        waited = true;
+      }
+      if (lane == 0) tma_load_3d(sB + s * kBStage, &tmap_q, 0, 0, (st0 + it) * KSTG, &sm->full_tma[s]);
+      __syncwarp();
+    }
+    if (!waited) pdl_wait();
+    for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+      mbar_wait(&sm->full_tma[j % STAGES], (j / STAGES) & 1u);
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    pdl_wait();
+    constexpr uint32_t idesc = idesc_i8<BN>();
+    bool ok = true;
+    for (int it = 0; it < nst; ++it) {
+      const int s = it % STAGES;
+      const uint32_t ph = (it / STAGES) & 1u;
+      if (!wait_or_abort(sm, &sm->full_tma[s], ph) || !wait_or_abort(sm, &sm->full_a[s], ph)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int bb = 0; bb < KSTG; ++bb) {
+          const uint32_t b_addr = smem_u32(sB + s * kBStage + bb * BN * kBK);
+          const uint32_t a_tmem = tmem + BN + (s * KSTG + bb) * 32;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; ++kk)
+            mma_i8_ts(tmem, a_tmem + kk * 8, sw128_desc(b_addr + kk * 32), idesc,
+                      (it > 0 || bb > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(&sm->empty[s]);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) {
+      if (ok) mma_commit(&sm->accf[0]);
+      mma_commit(&sm->drain);
+    }
+    __syncwarp();
+    mbar_wait(&sm->drain, 0);
+    __syncwarp();
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ expansion
+    pdl_wait();
+    const int r = tid - 128;
+    const int sub = r >> 4, rr = r & 15;
+    for (int it = 0; it < nst; ++it) {
+      const int s = it % STAGES;
+      const uint32_t ph = (it / STAGES) & 1u;
+      if (!wait_or_abort(sm, &sm->full_tma[s], ph)) break;
+#pragma unroll
+      for (int bb = 0; bb < KSTG; ++bb) {
+        const uint8_t* p = sP + s * kPStage + (sub * KSTG + bb) * kSubtileBytes + rr * 16;
+        uint32_t v[32];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint4 w = *reinterpret_cast<const uint4*>(p + h * 256);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int sh = 6 - 2 * g, c = 2 * g + h;
+            v[4 * c + 0] = (w.x >> sh) & 0x03030303u;
+            v[4 * c + 1] = (w.y >> sh) & 0x03030303u;
+            v[4 * c + 2] = (w.z >> sh) & 0x03030303u;
+            v[4 * c + 3] = (w.w >> sh) & 0x03030303u;
+          }
+        }
+        tmem_st32(tmem + (static_cast<uint32_t>(r & ~31) << 16) + BN + (s * KSTG + bb) * 32, v);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm->full_a[s]);
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ epilogue
+    pdl_wait();
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // tile row = TMEM lane
+    const int owner = r / RB;
+    const int orow = r - owner * RB;
+    const uint32_t dst = map_rank(smem_u32(red + (static_cast<int>(rank) * RB + orow) * BNP), owner);
+    bool have = nst > 0 && wait_or_abort(sm, &sm->accf[0], 0);
+    tc_fence_after();
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+    for (int j0 = 0; j0 < BN; j0 += 16) {
+      uint32_t v[16];
+      tmem_ld16(taddr + j0, v);
+      tmem_ld_wait();
+      if (!have) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = 0;  // no K stages here: contribute zero
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        st_cluster_v4(dst + (j0 + 4 * i) * 4, v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0)
+      for (uint32_t o = 0; o < S; ++o) mbar_arrive_cluster(map_rank(smem_u32(red_full), o));
+    // Reduce and write this rank's rows.
+    // Every thread acquires at cluster scope, so each sees the remote stores.
+    bool ok = false;
+    for (uint32_t i = 0; i < kWaitLimit && !ok; ++i) ok = mbar_try_wait_cluster(red_full, 0);
+    if (!ok) record_error(DEVERR_MBAR_TIMEOUT);
+    // rows of this rank, all 128 epilogue threads: idx -> (col j, row rr), rr fastest so
+    // consecutive threads store consecutive m of one output row n.
+    const int row0 = static_cast<int>(rank) * RB;
+    const int nrows = (row0 + RB <= kBM ? RB : kBM - row0);
+    const int t = tid - 256;
+    if (ok && nrows > 0) {
+      for (int idx = t; idx < nrows * BN; idx += 128) {
+        const int j = idx / nrows, rr = idx - j * nrows;
+        const int m = mt * kBM + row0 + rr;
+        if (j >= N || m >= M) continue;
+        int sum = 0;
+        for (uint32_t src = 0; src < S; ++src) sum += red[(src * RB + rr) * BNP + j];
+        const int d = sum - qsum[j];
+        const size_t o = static_cast<size_t>(j) * M + m;
+        if (acc_out) {
+          acc_out[o] = d;
+        } else {
+          const float fd = static_cast<float>(d);
+          const float sw = s_w[m], sx = s_x[j];
+          y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx)
+                                     : __fmul_rn(fd, __fmul_rn(sw, sx));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem, kTmemCols);
+}
+
 // ---- host side ------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -552,6 +820,59 @@ cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, cons
                             W.in_dim, order);
 }
 
+template <int BN, int STAGES, int KSTG>
+cudaError_t gemm_sk(const WeightView& W, const int8_t* q, const float* s_x, const int32_t* qsum,
+                    int n, float* y, int32_t* acc, int order, int S, cudaStream_t s) {
+  CUtensorMap qmap, wmap;
+  if (!make_q_map(&qmap, q, n, W.in_dim, BN, KSTG) || !make_w_map(&wmap, W, KSTG))
+    return cudaErrorInvalidValue;
+  constexpr int BNP = BN + 4;
+  const size_t smem = 1024 + static_cast<size_t>(STAGES) * (KSTG * BN * kBK + KSTG * kPackedBlock) +
+                      static_cast<size_t>(kRedRows) * BNP * 4 + sizeof(GemmSmem);
+  auto kern = k_gemm_sk<BN, STAGES, KSTG>;
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured[dev] = 1;
+  }
+  const int num_m = (W.out_dim + kBM - 1) / kBM;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S, num_m);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = S;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, qmap, wmap, W.s_w, s_x, qsum, y, acc, W.out_dim, n,
+                            W.in_dim, order);
+}
+
+// Cluster size for split-K: enough CTAs to cover the SMs, at most 8, and no
+// more ranks than 2-block stages.
+int split_k_factor(const WeightView& W, int n) {
+  // Measured on B200: the DSMEM reduction (~2 us) and the limited number of
+  // co-resident clusters of 7-8 CTAs outweigh the shorter K loops for every
+  // BitNet shape, so split-K stays off until its reduction is cheaper.
+  if (kSplitKEnabled == 0 || n > 128) return 1;
+  const int num_m = (W.out_dim + kBM - 1) / kBM;
+  const int total_st = (W.in_dim / kBK + 1) / 2;
+  int S = (num_sms() - 4) / num_m;
+  if (S > 8) S = 8;
+  if (S > total_st) S = total_st;
+  return S < 2 ? 1 : S;
+}
+
 }  // namespace
 
 bool gemm_supported(const WeightView& W, int n) {
@@ -561,9 +882,17 @@ bool gemm_supported(const WeightView& W, int n) {
 cudaError_t launch_gemm(const WeightView& W, const int8_t* q, const float* s_x,
                         const int32_t* qsum, int n, float* y, int32_t* acc, int order,
                         cudaStream_t s) {
-  if (n <= 16) return gemm_bn<16, 6, 2, true>(W, q, s_x, qsum, n, y, acc, order, s);
-  if (n <= 32) return gemm_bn<32, 6, 2, true>(W, q, s_x, qsum, n, y, acc, order, s);
-  if (n <= 64) return gemm_bn<64, 5, 2, true>(W, q, s_x, qsum, n, y, acc, order, s);
+  const int S = split_k_factor(W, n);
+  if (S > 1) {
+    if (n <= 16) return gemm_sk<16, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
+    if (n <= 32) return gemm_sk<32, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
+    if (n <= 64) return gemm_sk<64, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
+    return gemm_sk<128, 3, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
+  }
+  // Small token tiles: 4-block stages (16 MMAs per commit) amortise the commit cost.
+  if (n <= 16) return gemm_bn<16, 3, 4, true>(W, q, s_x, qsum, n, y, acc, order, s);
+  if (n <= 32) return gemm_bn<32, 3, 4, true>(W, q, s_x, qsum, n, y, acc, order, s);
+  if (n <= 64) return gemm_bn<64, 3, 4, true>(W, q, s_x, qsum, n, y, acc, order, s);
   if (n <= 128) return gemm_bn<128, 4, 2, true>(W, q, s_x, qsum, n, y, acc, order, s);
   return gemm_bn<256, 4, 1, false>(W, q, s_x, qsum, n, y, acc, order, s);
 }

@@ -53,6 +53,16 @@ def test_gemm_forward_matches_oracle(torch, n):
     assert np.array_equal(y, y_ref)
 
 
+@pytest.mark.parametrize("M,K,n", [(128, 2560, 16), (300, 2560, 64), (2560, 2560, 32),
+                                   (3840, 2560, 128), (6912, 2560, 100), (2560, 6912, 64),
+                                   (1000, 384, 48), (640, 1280, 128), (2560, 9216, 16)])
+def test_gemm_split_k_cluster_bitexact(torch, M, K, n):
+    # token counts <= 128 with few 128-row tiles run split-K over a cluster of up
+    # to 8 CTAs (reduction through distributed shared memory)
+    got, want = run_acc(torch, M, K, n, M + 7 * K + n)
+    assert np.array_equal(got, want)
+
+
 def test_gemm_many_tiles_per_cta(torch):
     # 54 row tiles x 8 token tiles = 432 tiles over <= 148 persistent CTAs.
     M, K, n = 6912, 256, 2048
