@@ -198,6 +198,90 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant(const float* __restrict__
   }
 }
 
+// Single-pass variant for d <= 256 * EPT: gamma is fetched into registers
+// before the PDL wait (it never depends on earlier kernels), x is loaded once
+// (thread t owns columns t + 256 j, the shaders' lane mapping), and the scalar
+// divisions run in one thread and are broadcast.
+template <int EPT, bool NORM>
+__global__ __launch_bounds__(256) void k_rmsnorm_quant_reg(const float* __restrict__ x,
+                                                           const float* __restrict__ w, float eps,
+                                                           int d, int8_t* __restrict__ q,
+                                                           float* __restrict__ scales,
+                                                           int32_t* __restrict__ qsum) {
+  __shared__ float shf[256];
+  __shared__ float scal[3];
+  __shared__ int shi[8];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float g[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int col = tid + 256 * j;
+    g[j] = (NORM && col < d) ? w[col] : 1.0f;
+  }
+  pdl_launch_dependents();
+  pdl_wait();  // x may be the previous kernel's output
+  const size_t row = blockIdx.x;
+  const float* xr = x + row * d;
+  float xv[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int col = tid + 256 * j;
+    xv[j] = col < d ? xr[col] : 0.0f;
+  }
+  if (NORM) {
+    float part = 0.0f;  // rmsnorm.wgsl:41-45
+#pragma unroll
+    for (int j = 0; j < EPT; ++j)
+      if (tid + 256 * j < d) part = __fadd_rn(part, __fmul_rn(xv[j], xv[j]));
+    const float total = tree_sum_256(part, shf);
+    if (tid == 0)
+      scal[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(d)), eps)));
+    __syncthreads();
+    const float rms = scal[0];
+#pragma unroll
+    for (int j = 0; j < EPT; ++j)
+      if (tid + 256 * j < d) xv[j] = norm_mul(xv[j], rms, g[j]);
+  }
+  float lmax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) lmax = fmaxf(lmax, fabsf(xv[j]));
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, s));
+  if (lane == 0) shf[warp] = lmax;
+  __syncthreads();
+  if (tid == 0) {
+    float absmax = shf[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) absmax = fmaxf(absmax, shf[i]);
+    scal[1] = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
+    scal[2] = absmax == 0.0f ? 0.0f : __fdiv_rn(127.0f, absmax);
+  }
+  __syncthreads();
+  const float inv = scal[2];
+  int8_t* qr = q + row * d;
+  int lsum = 0;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int col = tid + 256 * j;
+    if (col < d) {
+      const int qi = min(127, max(-127, __float2int_rn(__fmul_rn(xv[j], inv))));
+      qr[col] = static_cast<int8_t>(qi);
+      lsum += qi;
+    }
+  }
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, s);
+  if (lane == 0) shi[warp] = lsum;
+  __syncthreads();
+  if (tid == 0) {
+    int t = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += shi[i];
+    scales[row] = scal[1];
+    if (qsum) qsum[row] = t;
+  }
+}
+
 // rmsnorm.wgsl alone.
 __global__ __launch_bounds__(256) void k_rmsnorm(const float* __restrict__ x,
                                                  const float* __restrict__ w, float eps, int d,
@@ -587,8 +671,28 @@ cudaError_t launch_export_i2s(const uint8_t* t256, uint8_t* rows, int M, int K, 
   return cudaGetLastError();
 }
 
+template <int EPT>
+cudaError_t rmsnorm_quant_ept(const float* x, const float* norm_w, float eps, int n, int d,
+                              int8_t* q, float* scales, int32_t* qsum, cudaStream_t s) {
+  if (norm_w)
+    return launch_pdl(k_rmsnorm_quant_reg<EPT, true>, dim3(n), dim3(256), 0, s, x, norm_w, eps, d,
+                      q, scales, qsum);
+  return launch_pdl(k_rmsnorm_quant_reg<EPT, false>, dim3(n), dim3(256), 0, s, x, norm_w, eps, d,
+                    q, scales, qsum);
+}
+
 cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps, int n, int d,
                                  int8_t* q, float* scales, int32_t* qsum, cudaStream_t s) {
+  const int ept = (d + 255) / 256;
+  if (ept <= 2) return rmsnorm_quant_ept<2>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept <= 4) return rmsnorm_quant_ept<4>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept <= 8) return rmsnorm_quant_ept<8>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept <= 12) return rmsnorm_quant_ept<12>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept <= 16) return rmsnorm_quant_ept<16>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept <= 24) return rmsnorm_quant_ept<24>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept <= 28) return rmsnorm_quant_ept<28>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept <= 36) return rmsnorm_quant_ept<36>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  // larger rows: the three-pass kernel re-reads x instead of holding it in registers
   if (norm_w)
     return launch_pdl(k_rmsnorm_quant<true>, dim3(n), dim3(256), 0, s, x, norm_w, eps, d, q,
                       scales, qsum);

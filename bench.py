@@ -53,6 +53,9 @@ def parse_args():
     p.add_argument("--layers", type=int, default=LAYERS)
     p.add_argument("--batches", type=str, default=",".join(map(str, BATCHES)))
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--case", type=str, default=None,
+                   help="SHAPE:B — run a few forwards of one 2B shape at B tokens and exit "
+                        "(a small, self-contained workload for ncu captures)")
     return p.parse_args()
 
 
@@ -217,7 +220,9 @@ def run_reference(args):
 
 # ----------------------------------------------------------------------------- ours
 def load_profile_traffic():
-    path = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+    """DRAM traffic of the dominant kernel from the committed ncu summary
+    (profiles/traffic.json: batch, kernel, dram_bytes_per_launch), or None."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         return json.load(open(path))
     except (OSError, ValueError):
@@ -364,35 +369,51 @@ def run_ours(args):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     e2e_value = bytes_all / (e2e_ms / 1e3) / 1e9
 
-    # Dominant kernel: the B=1 matmul alone over all 150 weights (pre-quantized q).
-    q_ms = None
-    k_bytes = args.layers * sum(gemv_kernel_bytes(M, K, 1) for _, (M, K) in shp)
+    # Per-batch kernel timings. B = 1 runs one fused kernel per forward, so its
+    # step graph is the kernel alone; for B > 1 the matmul kernel (dp4a GEMV or
+    # tcgen05 GEMM) is timed alone over the same 150 weights with pre-quantized
+    # activations. The roofline is reported for the kernel with the largest
+    # total time in the step.
+    kernels = {}
+    n1_bytes = args.layers * sum(fwd_bytes(M, K, 1) for _, (M, K) in shp)
+    if 1 in batches:
+        kernels[1] = {"kernel": "k_bitlinear_n1 (fused RMSNorm+quantize+GEMV, B=1)",
+                      "bound": "hbm", "us": per_b_ms[1] * 1e3 / (args.steps * args.layers * len(shp)),
+                      "bytes": n1_bytes / (args.layers * len(shp)),
+                      "step_share_ms": per_b_ms[1] / args.steps}
     with torch.cuda.stream(stream):
-        qin = {}
-        for i, (name, (M, K)) in enumerate(shp):
-            qin[i] = obn.rmsnorm_quantize(xs[1, i].contiguous())
-        torch.cuda.synchronize()
-        gk = torch.cuda.CUDAGraph()
-        outs = {i: torch.empty((1, M), device=dev) for i, (_, (M, K)) in enumerate(shp)}
-        with torch.cuda.graph(gk, stream=stream):
-            for row in layers:
-                for i, L in enumerate(row):
-                    q, s, qs = qin[i]
-                    obn._lib.check(obn.lib().obn_ternary_matmul(
-                        L.handle, q.data_ptr(), s.data_ptr(), qs.data_ptr(), 1,
-                        outs[i].data_ptr(), stream.cuda_stream))
-        for _ in range(3):
-            gk.replay()
-        stream.synchronize()
-        k0 = torch.cuda.Event(enable_timing=True)
-        k1 = torch.cuda.Event(enable_timing=True)
-        reps = max(10, args.steps)
-        k0.record(stream)
-        for _ in range(reps):
-            gk.replay()
-        k1.record(stream)
-        stream.synchronize()
-        q_ms = k0.elapsed_time(k1) / reps
+        for B in [b for b in batches if b > 1]:
+            qin = {}
+            for i, (name, (M, K)) in enumerate(shp):
+                qin[i] = obn.rmsnorm_quantize(xs[B, i].contiguous())
+            outs = {i: torch.empty((B, M), device=dev) for i, (_, (M, K)) in enumerate(shp)}
+            torch.cuda.synchronize()
+            gk = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gk, stream=stream):
+                for row in layers:
+                    for i, L in enumerate(row):
+                        q, sc, qs = qin[i]
+                        obn._lib.check(obn.lib().obn_ternary_matmul(
+                            L.handle, q.data_ptr(), sc.data_ptr(), qs.data_ptr(), B,
+                            outs[i].data_ptr(), stream.cuda_stream))
+            for _ in range(3):
+                gk.replay()
+            stream.synchronize()
+            k0 = torch.cuda.Event(enable_timing=True)
+            k1 = torch.cuda.Event(enable_timing=True)
+            reps = max(5, min(args.steps, 50))
+            k0.record(stream)
+            for _ in range(reps):
+                gk.replay()
+            k1.record(stream)
+            stream.synchronize()
+            ms = k0.elapsed_time(k1) / reps
+            nl = args.layers * len(shp)
+            kb = args.layers * sum(gemv_kernel_bytes(M, K, B) for _, (M, K) in shp)
+            name = ("k_gemv (dp4a, B=%d)" % B) if B < 16 else ("k_gemm (tcgen05 kind::i8, B=%d)" % B)
+            kernels[B] = {"kernel": name, "bound": "hbm", "us": ms * 1e3 / nl, "bytes": kb / nl,
+                          "step_share_ms": ms}
+            del gk
     torch.cuda.synchronize()
     obn.check_device_errors()
 
@@ -404,17 +425,24 @@ def run_ours(args):
     peak = peaks.get("hbm_gbs")
     peak_note = "measured" if peak else "fallback"
     peak = peak or 6650.0
-    launches_k = args.layers * len(shp)
-    achieved = k_bytes / (q_ms / 1e3) / 1e9
+    rooflines = {}
+    for B, k in kernels.items():
+        ach = k["bytes"] / (k["us"] * 1e-6) / 1e9
+        rooflines[str(B)] = {"kernel": k["kernel"], "avg_launch_us": k["us"],
+                             "bytes_per_launch_avg": k["bytes"], "achieved_gbs": ach,
+                             "frac": ach / peak}
+    dom = max(kernels, key=lambda b: kernels[b]["step_share_ms"]) if kernels else None
     traffic = load_profile_traffic()
-    roofline = {
-        "kernel": "k_gemv<1> (B=1 ternary matmul, dp4a)",
-        "bound": "hbm", "achieved": achieved, "peak": peak, "peak_source": peak_note,
-        "unit": "GB/s", "frac": achieved / peak,
-        "avg_launch_us": q_ms * 1e3 / launches_k,
-        "bytes_per_launch_avg": k_bytes / launches_k,
-        "traffic": traffic.get("bytes_per_launch_avg") if traffic else None,
-    }
+    roofline = None
+    if dom is not None:
+        k = kernels[dom]
+        ach = k["bytes"] / (k["us"] * 1e-6) / 1e9
+        tr = None
+        if traffic and traffic.get("batch") == dom:
+            tr = traffic.get("dram_bytes_per_launch")
+        roofline = {"kernel": k["kernel"], "bound": k["bound"], "achieved": ach, "peak": peak,
+                    "peak_source": peak_note, "unit": "GB/s", "frac": ach / peak,
+                    "avg_launch_us": k["us"], "bytes_per_launch_avg": k["bytes"], "traffic": tr}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -436,6 +464,7 @@ def run_ours(args):
             "per_batch_gbs": per_b,
             "bitlinear_stack_tok_s": tok_s,
             "roofline": roofline,
+            "rooflines_per_batch": rooflines,
             "cpu_baseline": cpu,
             "clocks": clock_info,
             "e2e": {"value": e2e_value, "unit": "GB/s",
@@ -451,8 +480,32 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_case(spec: str):
+    """A few BitLinear forwards of one shape (4 layers, cold weights) for profilers."""
+    import torch
+    obn = importlib.import_module("0xbitnet_b200")
+    synth = importlib.import_module("0xbitnet_b200.synthetic")
+    name, B = spec.split(":")
+    B = int(B)
+    M, K = synth.SHAPES_2B[name]
+    layers = []
+    for i in range(4):
+        packed, s_w, gamma = synth.layer_device(77 + i, M, K)
+        layers.append(obn.BitLinear(packed, s_w, gamma, K, M))
+    x = torch.randn(B, K, device="cuda")
+    for _ in range(3):
+        for L in layers:
+            L.forward(x)
+    torch.cuda.synchronize()
+    obn.check_device_errors()
+    print(f"case {name} {M}x{K} B={B}: ok")
+
+
 def main():
     args = parse_args()
+    if args.case:
+        run_case(args.case)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
