@@ -291,22 +291,28 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
       for (int st = 0; st < n_stages; ++st, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1u;
-        if (!wait_or_abort(sm, &sm->full_tma[s], ph) || !wait_or_abort(sm, &sm->full_a[s], ph)) {
+        // full_a implies full_tma: the expansion warps arrive only after waiting
+        // for this stage's TMA bytes (weights and activations share the barrier).
+        if (!wait_or_abort(sm, &sm->full_a[s], ph)) {
           ok = false;
           break;
         }
         tc_fence_after();
         if (lane == 0) {
+          // Straight-line MMA burst: descriptors are one base plus constant steps
+          // (start address in 16-byte units, no carry out of its 14-bit field).
+          const uint64_t bdesc0 = sw128_desc(smem_u32(sB + s * kBStage));
 #pragma unroll
           for (int bb = 0; bb < KSTG; ++bb) {
-            const uint32_t b_addr = smem_u32(sB + s * kBStage + bb * BN * kBK);
             if (A_TMEM) {
               const uint32_t a_tmem = tmem + 2 * BN + (s * KSTG + bb) * 32;
 #pragma unroll
               for (int kk = 0; kk < kBK / 32; ++kk)
-                mma_i8_ts(d_tmem, a_tmem + kk * 8, sw128_desc(b_addr + kk * 32), idesc,
+                mma_i8_ts(d_tmem, a_tmem + kk * 8,
+                          bdesc0 + static_cast<uint64_t>((bb * BN * kBK + kk * 32) >> 4), idesc,
                           (st > 0 || bb > 0 || kk > 0) ? 1u : 0u);
             } else {
+              const uint32_t b_addr = smem_u32(sB + s * kBStage + bb * BN * kBK);
               const uint32_t a_addr = smem_u32(sA + s * kAStage + bb * kBM * kBK);
 #pragma unroll
               for (int kk = 0; kk < kBK / 32; ++kk)
@@ -593,7 +599,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
     for (int it = 0; it < nst; ++it) {
       const int s = it % STAGES;
       const uint32_t ph = (it / STAGES) & 1u;
-      if (!wait_or_abort(sm, &sm->full_tma[s], ph) || !wait_or_abort(sm, &sm->full_a[s], ph)) {
+      if (!wait_or_abort(sm, &sm->full_a[s], ph)) {  // implies the TMA bytes landed
         ok = false;
         break;
       }

@@ -53,6 +53,8 @@ def parse_args():
     p.add_argument("--layers", type=int, default=LAYERS)
     p.add_argument("--batches", type=str, default=",".join(map(str, BATCHES)))
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--prefill", type=str, default="512,2048,8192",
+                   help="config-2 token counts for the prefill TOPS block ('' to skip)")
     p.add_argument("--case", type=str, default=None,
                    help="SHAPE:B — run a few forwards of one 2B shape at B tokens and exit "
                         "(a small, self-contained workload for ncu captures)")
@@ -140,6 +142,15 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU baseline
+def host_threads() -> int:
+    # torchrun exports OMP_NUM_THREADS=1; the CPU baseline is timed on every core
+    # this process may run on instead.
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_sample(args, min_seconds=10.0, max_reps=50):
     """Times the oracle (OpenMP, all host threads) on 1 layer x 5 shapes x every B."""
     import numpy as np
@@ -151,7 +162,7 @@ def cpu_sample(args, min_seconds=10.0, max_reps=50):
         L = synth.layer(900 + i, M, K)
         xs = {B: synth.activations(950 + i * 10 + B, B, K) for B in batches}
         data.append((M, K, L, xs))
-    threads = orc.max_threads()
+    threads = host_threads()
     bytes_per_rep = sum(fwd_bytes(M, K, B) for M, K, _, _ in data for B in batches)
 
     def rep():
@@ -188,7 +199,7 @@ def run_reference(args):
         L = synth.layer(900 + i, M, K)
         xs = {B: synth.activations(950 + i * 10 + B, B, K) for B in batches}
         data.append((M, K, L, xs))
-    threads = orc.max_threads()
+    threads = host_threads()
     step_bytes = sum(fwd_bytes(M, K, B) for M, K, _, _ in data for B in batches)
 
     def step():
@@ -227,6 +238,84 @@ def load_profile_traffic():
         return json.load(open(path))
     except (OSError, ValueError):
         return None
+
+
+def measure_int8_peak(dev) -> float:
+    """Dense int8 tensor throughput of this GPU: torch._int_mm 8192^3, best of 10."""
+    import torch
+    a = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = float("inf")
+    for _ in range(10):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return 2.0 * 8192 ** 3 / (best / 1e3) / 1e12
+
+
+def measure_prefill(args, obn, synth, dev, stream):
+    """Config 2: the 5 BitNet-2B shapes at M_tok prefill tokens (one layer's
+    weights each), timed as the tcgen05 GEMM alone and as the full BitLinear
+    forward (RMSNorm + quantize + GEMM), in TOPS = 2*M_tok*M*K / time."""
+    import torch
+    toks = [int(t) for t in args.prefill.split(",") if t]
+    peak = measure_int8_peak(dev)
+    shp = shapes()
+    layers = []
+    for i, (name, (M, K)) in enumerate(shp):
+        packed, s_w, gamma = synth.layer_device(20_000 + i, M, K, dev)
+        layers.append(obn.BitLinear(packed, s_w, gamma, K, M))
+    out = {"int8_peak_tops": peak, "int8_peak_how": "torch._int_mm 8192^3 best of 10 (cuBLASLt)",
+           "gemm_tops": {}, "forward_tops": {}}
+    for T in toks:
+        ops = sum(2.0 * T * M * K for _, (M, K) in shp)
+        xs = [torch.randn(T, K, device=dev) for _, (M, K) in shp]
+        ys = [torch.empty(T, M, device=dev) for _, (M, K) in shp]
+        with torch.cuda.stream(stream):
+            qin = [obn.rmsnorm_quantize(x) for x in xs]
+            for i, L in enumerate(layers):
+                L.forward(xs[i], out=ys[i])
+            stream.synchronize()
+            res = {}
+            for mode in ("gemm", "forward"):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for i, L in enumerate(layers):
+                        if mode == "gemm":
+                            q, sc, qs = qin[i]
+                            obn._lib.check(obn.lib().obn_ternary_matmul(
+                                L.handle, q.data_ptr(), sc.data_ptr(), qs.data_ptr(), T,
+                                ys[i].data_ptr(), stream.cuda_stream))
+                        else:
+                            L.forward(xs[i], out=ys[i])
+                for _ in range(2):
+                    g.replay()
+                stream.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                reps = 5
+                e0.record(stream)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(stream)
+                stream.synchronize()
+                res[mode] = ops / (e0.elapsed_time(e1) / reps / 1e3) / 1e12
+                del g
+        out["gemm_tops"][str(T)] = res["gemm"]
+        out["forward_tops"][str(T)] = res["forward"]
+        del xs, ys, qin
+    best = max(out["gemm_tops"].values()) if out["gemm_tops"] else 0.0
+    out["gemm_frac_of_int8_peak"] = best / peak if peak else None
+    for L in layers:
+        L.close()
+    torch.cuda.synchronize()
+    return out
 
 
 def run_ours(args):
@@ -444,6 +533,8 @@ def run_ours(args):
                     "peak_source": peak_note, "unit": "GB/s", "frac": ach / peak,
                     "avg_launch_us": k["us"], "bytes_per_launch_avg": k["bytes"], "traffic": tr}
 
+    prefill = measure_prefill(args, obn, synth, dev, stream) if args.prefill else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_sample(args)
@@ -465,6 +556,7 @@ def run_ours(args):
             "bitlinear_stack_tok_s": tok_s,
             "roofline": roofline,
             "rooflines_per_batch": rooflines,
+            "prefill": prefill,
             "cpu_baseline": cpu,
             "clocks": clock_info,
             "e2e": {"value": e2e_value, "unit": "GB/s",
