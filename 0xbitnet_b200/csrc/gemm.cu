@@ -30,6 +30,8 @@
 // and TMEM is freed before exit.
 #include <cuda.h>
 
+#include <cstdlib>
+
 #include "gemm.h"
 #include "layout.cuh"
 #include "obn_common.cuh"
@@ -189,6 +191,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                                                       int K, int order) {
   constexpr int kAStage = KSTG * kBM * kBK;      // expanded A bytes per stage (smem variant)
   constexpr int kBStage = KSTG * BN * kBK;       // activation bytes per stage
+  constexpr int kColWords = (BN + 31) / 32;     // column scalars held per lane
   constexpr int kPStage = KSTG * kPackedBlock;   // packed weight bytes per stage
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
@@ -409,28 +412,35 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
       const int mt = t % num_m, nt = t / num_m;
       const int a = ti & 1;
       const uint32_t aph = (ti >> 1) & 1u;
-      if (!wait_or_abort(sm, &sm->accf[a], aph)) break;
-      tc_fence_after();
+      // This tile's per-row and per-column scalars are fetched before the
+      // accumulator is ready, so no global load sits between accf and the stores.
       const int m = mt * kBM + quarter * 32 + lane;
       const float sw = (m < M && !acc_out) ? s_w[m] : 0.0f;
+      int qs_r[kColWords];
+      float sx_r[kColWords];
+#pragma unroll
+      for (int i = 0; i < kColWords; ++i) {
+        const int c = nt * BN + 32 * i + lane;
+        qs_r[i] = c < N ? qsum[c] : 0;
+        sx_r[i] = (c < N && !acc_out) ? s_x[c] : 0.0f;
+      }
+      if (!wait_or_abort(sm, &sm->accf[a], aph)) break;
+      tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
-#pragma unroll 1
+      uint32_t v[2][16];
+      tmem_ld16(taddr, v[0]);
+      tmem_ld_wait();
+#pragma unroll
       for (int j0 = 0; j0 < BN; j0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(taddr + j0, v);
-        tmem_ld_wait();
-        const int n0 = nt * BN + j0;
-        // Column j's code sum and scale, fetched once per warp and broadcast.
-        const int nl = n0 + (lane & 15);
-        const int qs_l = nl < N ? qsum[nl] : 0;
-        const float sx_l = (nl < N && !acc_out) ? s_x[nl] : 0.0f;
+        const int cur = (j0 / 16) & 1;
+        if (j0 + 16 < BN) tmem_ld16(taddr + j0 + 16, v[cur ^ 1]);  // overlaps the stores below
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int n = n0 + j;
-          const int qs_j = __shfl_sync(0xffffffffu, qs_l, j);
-          const float sx_j = __shfl_sync(0xffffffffu, sx_l, j);
+          const int cj = j0 + j, n = nt * BN + cj;
+          const int qs_j = __shfl_sync(0xffffffffu, qs_r[cj / 32], cj % 32);
+          const float sx_j = __shfl_sync(0xffffffffu, sx_r[cj / 32], cj % 32);
           if (n < N && m < M) {
-            const int d = static_cast<int>(v[j]) - qs_j;
+            const int d = static_cast<int>(v[cur][j]) - qs_j;
             const size_t o = static_cast<size_t>(n) * M + m;
             if (acc_out) {
               acc_out[o] = d;
@@ -441,6 +451,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
             }
           }
         }
+        tmem_ld_wait();
       }
       tc_fence_before();
       __syncwarp();
@@ -460,21 +471,26 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
 // (e.g. 20 tiles for a 2560-row layer). k_gemm_sk gives each tile a cluster of
 // S CTAs (S <= 8) that split its K stages; each CTA accumulates its partial in
 // its own TMEM. The reduction is a reduce-scatter over distributed shared
-// memory: rank r owns rows [r*RB, r*RB+RB) of the tile (RB = ceil(128/S)); every
-// rank stores its partial rows to their owner's buffer slot [src][row][col]
-// (st.shared::cluster) and arrives on the owner's mbarrier with cluster-scope
-// release; the owner sums the S slots in rank order (integers: exact) and
-// writes the outputs.
+// memory driven by the bulk-copy engine: each CTA stages its partial tile in
+// its own shared memory, then one thread sends every owner rank r the rows
+// [r*RB, r*RB+RB) (RB = ceil(128/S)) with one cp.async.bulk shared::cta ->
+// shared::cluster copy into slot [src] of the owner's buffer, completing as
+// transaction bytes on the owner's mbarrier; the owner sums its S slots in rank
+// order (integers: exact) and writes the outputs. Cluster barriers at entry and
+// exit keep every CTA's shared memory alive while peers copy into or out of it.
 
 OBN_DEVINL uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-OBN_DEVINL void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
+// Relaxed arrive: nothing is published through the cluster barrier itself
+// (barrier inits are released by fence.mbarrier_init, copied rows by their
+// mbarrier's transaction count), and a release arrive costs about a microsecond.
+OBN_DEVINL void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
+OBN_DEVINL void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 OBN_DEVINL uint32_t map_rank(uint32_t smem_addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
@@ -490,6 +506,17 @@ OBN_DEVINL void mbar_arrive_cluster(uint32_t cluster_bar_addr) {
                    cluster_bar_addr)
                : "memory");
 }
+// Shared memory of this CTA -> shared memory of a CTA in the cluster (mapa
+// addresses), completing `bytes` of transactions on that CTA's mbarrier.
+OBN_DEVINL void bulk_s2cluster(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                               uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+      "[%3];" ::"r"(dst_cluster),
+      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
+
 OBN_DEVINL bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -502,8 +529,8 @@ OBN_DEVINL bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-constexpr int kRedRows = 136;
-constexpr int kSplitKEnabled = 0;  // >= S * ceil(128 / S) for every S <= 8
+constexpr int kRedRows = 136;  // >= S * ceil(128 / S) for every S <= 8
+constexpr int kSplitKDefaultCtas = 148;
 
 template <int BN, int STAGES, int KSTG>
 __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__ CUtensorMap tmap_q,
@@ -517,14 +544,19 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
   constexpr int kBStage = KSTG * BN * kBK;
   constexpr int kPStage = KSTG * kPackedBlock;
   constexpr int BNP = BN + 4;  // padded reduction row (ints): conflict-free lane strides
+  static_assert(kBM * BNP * 4 <= STAGES * kBStage, "staged partial tile fits the B stages");
+  static_assert((BNP * 4) % 16 == 0, "bulk copies move whole 16-byte units");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sB = base;                                            // STAGES x kBStage
   uint8_t* sP = sB + STAGES * kBStage;                           // STAGES x kPStage
   int32_t* red = reinterpret_cast<int32_t*>(sP + STAGES * kPStage);  // [S][RB][BNP]
-  GemmSmem* sm = reinterpret_cast<GemmSmem*>(red + kRedRows * BNP);
-  uint64_t* red_full = &sm->acce[0];  // reused: arrivals from every epilogue warp of the cluster
+  int32_t* e_qs = red + kRedRows * BNP;                                // [BN] column code sums
+  float* e_sx = reinterpret_cast<float*>(e_qs + BN);                   // [BN] column scales
+  float* e_sw = e_sx + BN;                                             // [kBM] row scales
+  GemmSmem* sm = reinterpret_cast<GemmSmem*>(e_sw + kBM);
+  uint64_t* red_full = &sm->acce[0];  // incoming partial rows (transaction bytes)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t S = gridDim.x;  // cluster = the whole x dimension
@@ -547,10 +579,13 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
       mbar_init(&sm->empty[s], 1);
     }
     mbar_init(&sm->accf[0], 1);
-    mbar_init(red_full, 4 * S);
+    mbar_init(red_full, 1);
     mbar_init(&sm->drain, 1);
     sm->abort_flag = 0;
     fence_mbar_init();
+    // Arm before the cluster barrier below: no peer sends before it.
+    const int own_rows = min(RB, kBM - static_cast<int>(rank) * RB);
+    mbar_arrive_expect_tx(red_full, S * static_cast<uint32_t>(own_rows) * BNP * 4);
   }
   if (warp == 2) {
     tmem_alloc(&sm->tmem_base, kTmemCols);
@@ -558,7 +593,9 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
   }
   tc_fence_before();
   __syncthreads();
-  cluster_sync_all();  // every CTA's barriers exist before any remote arrive
+  // Cluster barrier, phase 0: published barrier inits. Only the epilogue's sends
+  // depend on it, so every thread arrives now and waits when it must.
+  cluster_arrive();
   tc_fence_after();
   const uint32_t tmem = sm->tmem_base;
   pdl_launch_dependents();
@@ -662,11 +699,22 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
     pdl_wait();
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // tile row = TMEM lane
-    const int owner = r / RB;
-    const int orow = r - owner * RB;
-    const uint32_t dst = map_rank(smem_u32(red + (static_cast<int>(rank) * RB + orow) * BNP), owner);
+    // Scalars for the owned rows' outputs, fetched while the MMAs run and
+    // published by the epilogue barrier below.
+    const int t = tid - 256;
+    if (t < BN) {
+      e_qs[t] = t < N ? qsum[t] : 0;
+      e_sx[t] = (t < N && !acc_out) ? s_x[t] : 0.0f;
+    }
+    {
+      const int m = mt * kBM + t;
+      e_sw[t] = (m < M && !acc_out) ? s_w[m] : 0.0f;
+    }
     bool have = nst > 0 && wait_or_abort(sm, &sm->accf[0], 0);
     tc_fence_after();
+    // Stage the partial tile locally; the pipeline buffers are free once every
+    // MMA has completed (accf).
+    int32_t* part = reinterpret_cast<int32_t*>(sB);
     const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll 1
     for (int j0 = 0; j0 < BN; j0 += 16) {
@@ -679,45 +727,83 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        st_cluster_v4(dst + (j0 + 4 * i) * 4, v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        *reinterpret_cast<uint4*>(part + r * BNP + j0 + 4 * i) =
+            make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     }
     tc_fence_before();
-    __syncwarp();
-    if (lane == 0)
-      for (uint32_t o = 0; o < S; ++o) mbar_arrive_cluster(map_rank(smem_u32(red_full), o));
-    // Reduce and write this rank's rows.
-    // Every thread acquires at cluster scope, so each sees the remote stores.
+    fence_proxy_async_smem();  // generic stores -> visible to the bulk-copy engine
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps
+    cluster_wait();  // phase 0: every peer's red_full is initialised and armed
+    if (tid == 256) {
+      for (uint32_t o = 0; o < S; ++o) {
+        const int rows_o = min(RB, kBM - static_cast<int>(o) * RB);
+        if (rows_o <= 0) continue;
+        bulk_s2cluster(map_rank(smem_u32(red + static_cast<int>(rank) * RB * BNP), o),
+                       smem_u32(part + static_cast<int>(o) * RB * BNP),
+                       static_cast<uint32_t>(rows_o) * BNP * 4, map_rank(smem_u32(red_full), o));
+      }
+    }
+    // Reduce and write this rank's rows once every peer's rows have landed.
     bool ok = false;
     for (uint32_t i = 0; i < kWaitLimit && !ok; ++i) ok = mbar_try_wait_cluster(red_full, 0);
     if (!ok) record_error(DEVERR_MBAR_TIMEOUT);
-    // rows of this rank, all 128 epilogue threads: idx -> (col j, row rr), rr fastest so
-    // consecutive threads store consecutive m of one output row n.
+    __syncwarp();
+    // Phase 1: this CTA's incoming copies are complete (so are the peers' reads
+    // behind them); the wait before exit makes that true cluster-wide.
+    cluster_arrive();
+    // Lane = row (coalesced stores over m); each warp takes 4-column groups
+    // (quarter, quarter + 4, ...): one 16-byte load per source rank, all issued
+    // before the sums (a 4-word row run of red is conflict-free across 8 lanes).
     const int row0 = static_cast<int>(rank) * RB;
     const int nrows = (row0 + RB <= kBM ? RB : kBM - row0);
-    const int t = tid - 256;
-    if (ok && nrows > 0) {
-      for (int idx = t; idx < nrows * BN; idx += 128) {
-        const int j = idx / nrows, rr = idx - j * nrows;
+    if (ok) {
+      for (int rb = 0; rb < nrows; rb += 32) {
+        const int rr = rb + lane;
         const int m = mt * kBM + row0 + rr;
-        if (j >= N || m >= M) continue;
-        int sum = 0;
-        for (uint32_t src = 0; src < S; ++src) sum += red[(src * RB + rr) * BNP + j];
-        const int d = sum - qsum[j];
-        const size_t o = static_cast<size_t>(j) * M + m;
-        if (acc_out) {
-          acc_out[o] = d;
-        } else {
-          const float fd = static_cast<float>(d);
-          const float sw = s_w[m], sx = s_x[j];
-          y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx)
-                                     : __fmul_rn(fd, __fmul_rn(sw, sx));
+        if (rr >= nrows || m >= M) continue;
+        const float sw = e_sw[row0 + rr];
+        for (int g = quarter; g < BN / 4 && 4 * g < N; g += 4) {
+          const int j0 = 4 * g;
+          uint4 pv[8];
+#pragma unroll
+          for (uint32_t src = 0; src < 8; ++src)
+            if (src < S) pv[src] = *reinterpret_cast<const uint4*>(red + (src * RB + rr) * BNP + j0);
+          int sum[4] = {0, 0, 0, 0};
+#pragma unroll
+          for (uint32_t src = 0; src < 8; ++src)
+            if (src < S) {
+              sum[0] += static_cast<int>(pv[src].x);
+              sum[1] += static_cast<int>(pv[src].y);
+              sum[2] += static_cast<int>(pv[src].z);
+              sum[3] += static_cast<int>(pv[src].w);
+            }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int j = j0 + c;
+            if (j >= N) break;
+            const int d = sum[c] - e_qs[j];
+            const size_t o = static_cast<size_t>(j) * M + m;
+            if (acc_out) {
+              acc_out[o] = d;
+            } else {
+              const float fd = static_cast<float>(d);
+              const float sx = e_sx[j];
+              y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx)
+                                         : __fmul_rn(fd, __fmul_rn(sw, sx));
+            }
+          }
         }
       }
     }
   }
 
+  if (warp < 8) {  // phase 0 then phase 1 for the roles that send and receive nothing
+    cluster_wait();
+    cluster_arrive();
+  }
   tc_fence_before();
   __syncthreads();
+  cluster_wait();  // phase 1: no copy still reads or writes any CTA's shared memory
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem, kTmemCols);
 }
@@ -827,14 +913,19 @@ cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, cons
 }
 
 template <int BN, int STAGES, int KSTG>
+size_t gemm_sk_smem_bytes() {
+  constexpr int BNP = BN + 4;
+  return 1024 + static_cast<size_t>(STAGES) * (KSTG * BN * kBK + KSTG * kPackedBlock) +
+         static_cast<size_t>(kRedRows) * BNP * 4 + (2 * BN + kBM) * 4 + sizeof(GemmSmem);
+}
+
+template <int BN, int STAGES, int KSTG>
 cudaError_t gemm_sk(const WeightView& W, const int8_t* q, const float* s_x, const int32_t* qsum,
                     int n, float* y, int32_t* acc, int order, int S, cudaStream_t s) {
   CUtensorMap qmap, wmap;
   if (!make_q_map(&qmap, q, n, W.in_dim, BN, KSTG) || !make_w_map(&wmap, W, KSTG))
     return cudaErrorInvalidValue;
-  constexpr int BNP = BN + 4;
-  const size_t smem = 1024 + static_cast<size_t>(STAGES) * (KSTG * BN * kBK + KSTG * kPackedBlock) +
-                      static_cast<size_t>(kRedRows) * BNP * 4 + sizeof(GemmSmem);
+  const size_t smem = gemm_sk_smem_bytes<BN, STAGES, KSTG>();
   auto kern = k_gemm_sk<BN, STAGES, KSTG>;
   static int configured[64] = {0};
   int dev = 0;
@@ -864,19 +955,63 @@ cudaError_t gemm_sk(const WeightView& W, const int8_t* q, const float* s_x, cons
                             W.in_dim, order);
 }
 
-// Cluster size for split-K: enough CTAs to cover the SMs, at most 8, and no
-// more ranks than 2-block stages.
-int split_k_factor(const WeightView& W, int n) {
-  // Measured on B200: the DSMEM reduction (~2 us) and the limited number of
-  // co-resident clusters of 7-8 CTAs outweigh the shorter K loops for every
-  // BitNet shape, so split-K stays off until its reduction is cheaper.
-  if (kSplitKEnabled == 0 || n > 128) return 1;
+// Clusters of S CTAs of k_gemm_sk<BN, STAGES, KSTG> that fit on the device at once
+// (cached per device and S). Clusters must sit inside one GPC, so this falls off
+// faster than num_sms / S (B200: 74 for S = 2, 33 for 4, 22 for 6, 15 for 8).
+template <int BN, int STAGES, int KSTG>
+int sk_max_clusters(int S) {
+  static int cache[64][9] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || S < 2 || S > 8) return 0;
+  if (cache[dev][S]) return cache[dev][S] > 0 ? cache[dev][S] : 0;
+  auto kern = k_gemm_sk<BN, STAGES, KSTG>;
+  const size_t smem = gemm_sk_smem_bytes<BN, STAGES, KSTG>();
+  int count = 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S, 1);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&count, kern, &cfg) != cudaSuccess) count = 0;
+  }
+  cudaGetLastError();  // a refused query only disables split-K
+  cache[dev][S] = count > 0 ? count : -1;
+  return count;
+}
+
+// Upper bound on the CTAs of one split-K launch. SMs left free let the next
+// kernel of a decode step start early (programmatic dependent launch) and
+// prefetch its weights. OBN_GEMM_SPLIT_K=<n> overrides it (0 disables split-K);
+// read once per process.
+int split_k_cta_cap() {
+  static const int cap = [] {
+    const char* e = std::getenv("OBN_GEMM_SPLIT_K");
+    return e ? std::atoi(e) : kSplitKDefaultCtas;
+  }();
+  return cap;
+}
+
+// Cluster size for split-K: the largest S <= 8 (and <= the number of K stages)
+// for which one cluster per 128-row tile fits on the device in a single wave
+// within the CTA cap; 1 (no split) when that leaves S < 2.
+template <int BN, int STAGES, int KSTG>
+int split_k_factor(const WeightView& W) {
   const int num_m = (W.out_dim + kBM - 1) / kBM;
-  const int total_st = (W.in_dim / kBK + 1) / 2;
-  int S = (num_sms() - 4) / num_m;
-  if (S > 8) S = 8;
-  if (S > total_st) S = total_st;
-  return S < 2 ? 1 : S;
+  const int cap = split_k_cta_cap();
+  const int total_st = (W.in_dim / kBK + KSTG - 1) / KSTG;
+  for (int S = total_st < 8 ? total_st : 8; S >= 2; --S)
+    if (S * num_m <= cap && num_m <= sk_max_clusters<BN, STAGES, KSTG>(S))
+      return (S == 2 && BN >= 64) ? 1 : S;  // measured: a 2-way split of a >= 64-token tile gains nothing
+  return 1;
 }
 
 }  // namespace
@@ -888,13 +1023,16 @@ bool gemm_supported(const WeightView& W, int n) {
 cudaError_t launch_gemm(const WeightView& W, const int8_t* q, const float* s_x,
                         const int32_t* qsum, int n, float* y, int32_t* acc, int order,
                         cudaStream_t s) {
-  const int S = split_k_factor(W, n);
-  if (S > 1) {
-    if (n <= 16) return gemm_sk<16, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
-    if (n <= 32) return gemm_sk<32, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
-    if (n <= 64) return gemm_sk<64, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
+  // Few 128-row tiles: split K over a cluster per tile.
+  int S = 1;
+  if (n <= 16 && (S = split_k_factor<16, 4, 2>(W)) > 1)
+    return gemm_sk<16, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
+  if (n > 16 && n <= 32 && (S = split_k_factor<32, 4, 2>(W)) > 1)
+    return gemm_sk<32, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
+  if (n > 32 && n <= 64 && (S = split_k_factor<64, 4, 2>(W)) > 1)
+    return gemm_sk<64, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
+  if (n > 64 && n <= 128 && (S = split_k_factor<128, 3, 2>(W)) > 1)
     return gemm_sk<128, 3, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
-  }
   // Small token tiles: 4-block stages (16 MMAs per commit) amortise the commit cost.
   if (n <= 16) return gemm_bn<16, 3, 4, true>(W, q, s_x, qsum, n, y, acc, order, s);
   if (n <= 32) return gemm_bn<32, 3, 4, true>(W, q, s_x, qsum, n, y, acc, order, s);

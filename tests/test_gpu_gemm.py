@@ -55,10 +55,12 @@ def test_gemm_forward_matches_oracle(torch, n):
 
 @pytest.mark.parametrize("M,K,n", [(128, 2560, 16), (300, 2560, 64), (2560, 2560, 32),
                                    (3840, 2560, 128), (6912, 2560, 100), (2560, 6912, 64),
-                                   (1000, 384, 48), (640, 1280, 128), (2560, 9216, 16)])
+                                   (1000, 384, 48), (640, 1280, 128), (2560, 9216, 16),
+                                   (2000, 640, 20), (1920, 1664, 40)])
 def test_gemm_split_k_cluster_bitexact(torch, M, K, n):
     # token counts <= 128 with few 128-row tiles run split-K over a cluster of up
-    # to 8 CTAs (reduction through distributed shared memory)
+    # to 8 CTAs (bulk-copy reduce-scatter through distributed shared memory);
+    # these shapes reach cluster sizes 2 through 8, including ragged row splits
     got, want = run_acc(torch, M, K, n, M + 7 * K + n)
     assert np.array_equal(got, want)
 
