@@ -357,7 +357,10 @@ int obn_check_device_errors(void) {
   e = obn::read_and_clear_dev_error(&word);
   if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
   if (word != 0)
-    return fail(OBN_ERR_DEVICE_TIMEOUT, "a bounded device-side wait gave up (code %u)", word);
+    return fail(OBN_ERR_DEVICE_TIMEOUT, "%s (device error code %u)",
+                word == 1u ? "a bounded device-side wait gave up"
+                                                 : "a kernel was launched outside its geometry",
+                word);
   return OBN_OK;
 }
 

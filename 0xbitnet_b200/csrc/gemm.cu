@@ -170,7 +170,8 @@ constexpr uint32_t idesc_i8() {
 }
 
 // Bounded wait that gives up at once after another role aborted.
-OBN_DEVINL bool wait_or_abort(GemmSmem* sm, uint64_t* bar, uint32_t parity) {
+template <class Smem>
+OBN_DEVINL bool wait_or_abort(Smem* sm, uint64_t* bar, uint32_t parity) {
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 1023u) == 1023u && sm->abort_flag) return false;
@@ -468,16 +469,30 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
 // ---- split-K over a thread-block cluster ---------------------------------------------
 //
 // Decode-sized token counts leave too few 128-row tiles to occupy the GPU
-// (e.g. 20 tiles for a 2560-row layer). k_gemm_sk gives each tile a cluster of
-// S CTAs (S <= 8) that split its K stages; each CTA accumulates its partial in
-// its own TMEM. The reduction is a reduce-scatter over distributed shared
-// memory driven by the bulk-copy engine: each CTA stages its partial tile in
-// its own shared memory, then one thread sends every owner rank r the rows
-// [r*RB, r*RB+RB) (RB = ceil(128/S)) with one cp.async.bulk shared::cta ->
-// shared::cluster copy into slot [src] of the owner's buffer, completing as
-// transaction bytes on the owner's mbarrier; the owner sums its S slots in rank
-// order (integers: exact) and writes the outputs. Cluster barriers at entry and
-// exit keep every CTA's shared memory alive while peers copy into or out of it.
+// (20 tiles for a 2560-row layer). k_gemm_sk gives each tile a cluster of S
+// CTAs (S <= 8); rank r takes the K blocks [r*KB/S, (r+1)*KB/S). A CTA's whole
+// slice is in flight at once (at most sk_blocks<BN>() blocks: their
+// activations, packed weights and expanded codes all fit), so no buffer is
+// recycled and the MMAs end in a single tcgen05.commit:
+//   - the producer issues every weight copy first, then, after the wait on the
+//     previous kernel, every activation copy, with one barrier each per block;
+//   - the expansion warps turn each block's weights into codes in TMEM as soon
+//     as they land, overlapping the previous kernel's tail;
+//   - the MMA warp issues a block's 4 MMAs once its codes and activations are in.
+// Each CTA accumulates its partial in its own TMEM. The reduction is a
+// reduce-scatter over distributed shared memory driven by the bulk-copy engine:
+// each CTA stages its partial tile in its own shared memory, then one thread
+// sends every owner rank o the rows [o*RB, o*RB+RB) (RB = ceil(128/S)) with one
+// cp.async.bulk shared::cta -> shared::cluster copy into slot [src] of the
+// owner's buffer, completing as transaction bytes on the owner's mbarrier; the
+// owner sums its S slots in rank order (integers: exact) and writes the outputs.
+// A split cluster barrier (arrive early, wait late) orders the barrier inits
+// before the first send and keeps every CTA's shared memory alive until no copy
+// reads or writes it.
+//
+// One CTA per SM (shared memory is padded past half an SM): two CTAs of
+// different clusters on one SM would serialise on the TMEM allocation while
+// each cluster waits for all of its ranks.
 
 OBN_DEVINL uint32_t cluster_ctarank() {
   uint32_t r;
@@ -495,16 +510,6 @@ OBN_DEVINL uint32_t map_rank(uint32_t smem_addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
   return r;
-}
-OBN_DEVINL void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b),
-               "r"(c), "r"(d)
-               : "memory");
-}
-OBN_DEVINL void mbar_arrive_cluster(uint32_t cluster_bar_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
-                   cluster_bar_addr)
-               : "memory");
 }
 // Shared memory of this CTA -> shared memory of a CTA in the cluster (mapa
 // addresses), completing `bytes` of transactions on that CTA's mbarrier.
@@ -531,8 +536,81 @@ OBN_DEVINL bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
 
 constexpr int kRedRows = 136;  // >= S * ceil(128 / S) for every S <= 8
 constexpr int kSplitKDefaultCtas = 148;
+constexpr size_t kSkMinSmem = 120 * 1024;
 
-template <int BN, int STAGES, int KSTG>
+constexpr int kSkGroup = 4;  // K blocks behind one barrier (16 MMAs per burst)
+
+template <int NB>
+struct SkSmem {
+  static constexpr int NG = (NB + kSkGroup - 1) / kSkGroup;
+  uint64_t wfull[NG];   // packed weights of group g landed
+  uint64_t afull[NG];   // activations of group g landed
+  uint64_t full_a[NG];  // codes of group g in TMEM (one arrival per expanding warp)
+  uint64_t accf;        // every MMA done
+  uint64_t red_full;    // incoming partial rows (transaction bytes)
+  uint64_t drain;
+  uint32_t tmem_base;
+  volatile int abort_flag;
+};
+
+// K blocks one split-K CTA holds at once: TMEM (BN accumulator columns + 32 code
+// columns per block <= 512) and shared memory (4 KB of weights + BN*128 bytes
+// of activations per block, next to the reduction buffer).
+template <int BN>
+constexpr int sk_blocks() {
+  return BN <= 32 ? 15 : BN <= 64 ? 14 : 7;
+}
+
+template <int BN>
+constexpr size_t sk_smem_bytes() {
+  return 1024 + static_cast<size_t>(sk_blocks<BN>()) * (BN * kBK + kPackedBlock) +
+         static_cast<size_t>(kRedRows) * (BN + 4) * 4 + (2 * BN + kBM) * 4 +
+         sizeof(SkSmem<sk_blocks<BN>()>);
+}
+
+template <int BN>
+constexpr size_t sk_smem_launch() {
+  return sk_smem_bytes<BN>() < kSkMinSmem ? kSkMinSmem : sk_smem_bytes<BN>();
+}
+
+// Expansion of the groups g = set, set + 2, ... of a split-K CTA's slice by one
+// of its two 4-warp sets (warps 4-7: set 0, warps 8-11: set 1). Thread = weight
+// row = TMEM lane (warp % 4 selects the lane quarter); codes c = w + 1 as u8.
+// All of a group's TMEM stores are in flight before one wait.
+template <int BN, int NB>
+OBN_DEVINL void sk_expand(SkSmem<NB>* sm, const uint8_t* sP, uint32_t tmem, int nb, int set) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r = (warp & 3) * 32 + lane;
+  const int sub = r >> 4, rr = r & 15;
+  const int ng = (nb + kSkGroup - 1) / kSkGroup;
+  for (int g = set; g < ng; g += 2) {
+    if (!wait_or_abort(sm, &sm->wfull[g], 0)) break;
+    const int bg = g * kSkGroup, be = min(bg + kSkGroup, nb);
+    for (int b = bg; b < be; ++b) {
+      const uint8_t* p = sP + b * kPackedBlock + sub * kSubtileBytes + rr * 16;
+      uint32_t v[32];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint4 w = *reinterpret_cast<const uint4*>(p + h * 256);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int sh = 6 - 2 * q, c = 2 * q + h;
+          v[4 * c + 0] = (w.x >> sh) & 0x03030303u;
+          v[4 * c + 1] = (w.y >> sh) & 0x03030303u;
+          v[4 * c + 2] = (w.z >> sh) & 0x03030303u;
+          v[4 * c + 3] = (w.w >> sh) & 0x03030303u;
+        }
+      }
+      tmem_st32(tmem + (static_cast<uint32_t>(r & ~31) << 16) + BN + b * 32, v);
+    }
+    tmem_st_wait();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm->full_a[g]);
+  }
+}
+
+template <int BN>
 __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__ CUtensorMap tmap_q,
                                                          const __grid_constant__ CUtensorMap tmap_w,
                                                          const float* __restrict__ s_w,
@@ -541,51 +619,51 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
                                                          float* __restrict__ y,
                                                          int32_t* __restrict__ acc_out, int M,
                                                          int N, int K, int order) {
-  constexpr int kBStage = KSTG * BN * kBK;
-  constexpr int kPStage = KSTG * kPackedBlock;
-  constexpr int BNP = BN + 4;  // padded reduction row (ints): conflict-free lane strides
-  static_assert(kBM * BNP * 4 <= STAGES * kBStage, "staged partial tile fits the B stages");
+  constexpr int NB = sk_blocks<BN>();
+  constexpr int kBBlock = BN * kBK;  // activation bytes per block
+  constexpr int BNP = BN + 4;        // padded reduction row (ints): conflict-free lane strides
+  constexpr uint32_t kTmemCols = 512;
+  static_assert(BN + 32 * NB <= static_cast<int>(kTmemCols), "TMEM budget");
+  static_assert(kBM * BNP * 4 <= NB * kBBlock, "staged partial tile fits the activation blocks");
   static_assert((BNP * 4) % 16 == 0, "bulk copies move whole 16-byte units");
+  static_assert(sk_smem_bytes<BN>() <= 232448, "shared memory budget");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* sB = base;                                            // STAGES x kBStage
-  uint8_t* sP = sB + STAGES * kBStage;                           // STAGES x kPStage
-  int32_t* red = reinterpret_cast<int32_t*>(sP + STAGES * kPStage);  // [S][RB][BNP]
+  uint8_t* sB = base;                                                // NB x [BN][128], SW128
+  uint8_t* sP = sB + NB * kBBlock;                                   // NB x 4 KB packed
+  int32_t* red = reinterpret_cast<int32_t*>(sP + NB * kPackedBlock);  // [S][RB][BNP]
   int32_t* e_qs = red + kRedRows * BNP;                                // [BN] column code sums
   float* e_sx = reinterpret_cast<float*>(e_qs + BN);                   // [BN] column scales
   float* e_sw = e_sx + BN;                                             // [kBM] row scales
-  GemmSmem* sm = reinterpret_cast<GemmSmem*>(e_sw + kBM);
-  uint64_t* red_full = &sm->acce[0];  // incoming partial rows (transaction bytes)
+  SkSmem<NB>* sm = reinterpret_cast<SkSmem<NB>*>(e_sw + kBM);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t S = gridDim.x;  // cluster = the whole x dimension
   const uint32_t rank = cluster_ctarank();
   const int mt = blockIdx.y;
   const int KB = K / kBK;
-  const int total_st = (KB + KSTG - 1) / KSTG;
-  const int st0 = static_cast<int>(rank * total_st / S);
-  const int st1 = static_cast<int>((rank + 1) * total_st / S);
-  const int nst = st1 - st0;
+  const int b0 = static_cast<int>(rank * KB / S);
+  const int nb_slice = static_cast<int>((rank + 1) * KB / S) - b0;
+  const int nb = min(nb_slice, NB);  // the host keeps every slice within NB blocks
   const int RB = (kBM + static_cast<int>(S) - 1) / static_cast<int>(S);
-  constexpr uint32_t kTmemNeed = BN + 32 * KSTG * STAGES;
-  constexpr uint32_t kTmemCols = kTmemNeed <= 128 ? 128 : kTmemNeed <= 256 ? 256 : 512;
-  static_assert(kTmemNeed <= 512, "TMEM budget");
+  if (tid == 0 && (nb_slice > NB || S > 8)) record_error(DEVERR_BAD_LAUNCH);
 
+  const int ng = (nb + kSkGroup - 1) / kSkGroup;
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&sm->full_tma[s], 1);
-      mbar_init(&sm->full_a[s], 4);
-      mbar_init(&sm->empty[s], 1);
+    for (int g = 0; g < ng; ++g) {
+      mbar_init(&sm->wfull[g], 1);
+      mbar_init(&sm->afull[g], 1);
+      mbar_init(&sm->full_a[g], 4);
     }
-    mbar_init(&sm->accf[0], 1);
-    mbar_init(red_full, 1);
+    mbar_init(&sm->accf, 1);
+    mbar_init(&sm->red_full, 1);
     mbar_init(&sm->drain, 1);
     sm->abort_flag = 0;
     fence_mbar_init();
-    // Arm before the cluster barrier below: no peer sends before it.
+    // Armed before this CTA's cluster arrive: no peer sends before its wait.
     const int own_rows = min(RB, kBM - static_cast<int>(rank) * RB);
-    mbar_arrive_expect_tx(red_full, S * static_cast<uint32_t>(own_rows) * BNP * 4);
+    mbar_arrive_expect_tx(&sm->red_full, S * static_cast<uint32_t>(own_rows) * BNP * 4);
   }
   if (warp == 2) {
     tmem_alloc(&sm->tmem_base, kTmemCols);
@@ -602,61 +680,61 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // The weights do not depend on the previous kernel; the activations do.
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_q) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_w) : "memory");
-    }
-    bool waited = false;
-    int it = 0;
-    for (; it < nst; ++it) {
-      const int s = it % STAGES;
-      const uint32_t ph = (it / STAGES) & 1u;
-      if (!wait_or_abort(sm, &sm->empty[s], ph ^ 1u)) break;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&sm->full_tma[s], kBStage + kPStage);
-        tma_load_3d(sP + s * kPStage, &tmap_w, 0, (st0 + it) * KSTG, mt * (kBM / kSubRows),
-                    &sm->full_tma[s]);
+      for (int g = 0; g < ng; ++g) {
+        const int bg = g * kSkGroup, ne = min(kSkGroup, nb - bg);
+        mbar_arrive_expect_tx(&sm->wfull[g], ne * kPackedBlock);
+        for (int b = bg; b < bg + ne; ++b)
+          tma_load_3d(sP + b * kPackedBlock, &tmap_w, 0, b0 + b, mt * (kBM / kSubRows),
+                      &sm->wfull[g]);
       }
-      if (!waited) {
-        pdl_wait();
-        waited = true;
-      }
-      if (lane == 0) tma_load_3d(sB + s * kBStage, &tmap_q, 0, 0, (st0 + it) * KSTG, &sm->full_tma[s]);
-      __syncwarp();
     }
-    if (!waited) pdl_wait();
-    for (int j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
-      mbar_wait(&sm->full_tma[j % STAGES], (j / STAGES) & 1u);
+    __syncwarp();
+    pdl_wait();
+    if (lane == 0)
+      for (int g = 0; g < ng; ++g) {
+        const int bg = g * kSkGroup, ne = min(kSkGroup, nb - bg);
+        mbar_arrive_expect_tx(&sm->afull[g], ne * kBBlock);
+        for (int b = bg; b < bg + ne; ++b)
+          tma_load_3d(sB + b * kBBlock, &tmap_q, 0, 0, b0 + b, &sm->afull[g]);
+      }
+    __syncwarp();
+    // Every copy has landed before the CTA exits (immediate unless it aborted).
+    for (int g = 0; g < ng; ++g) {
+      mbar_wait(&sm->wfull[g], 0);
+      mbar_wait(&sm->afull[g], 0);
+    }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    pdl_wait();
     constexpr uint32_t idesc = idesc_i8<BN>();
     bool ok = true;
-    for (int it = 0; it < nst; ++it) {
-      const int s = it % STAGES;
-      const uint32_t ph = (it / STAGES) & 1u;
-      if (!wait_or_abort(sm, &sm->full_a[s], ph)) {  // implies the TMA bytes landed
+    // One wait pair per group, then a straight burst of its MMAs (a wait costs
+    // about as much as two MMAs even when its phase completed long ago).
+    for (int g = 0; g < ng; ++g) {
+      if (!wait_or_abort(sm, &sm->full_a[g], 0) || !wait_or_abort(sm, &sm->afull[g], 0)) {
         ok = false;
         break;
       }
       tc_fence_after();
       if (lane == 0) {
-#pragma unroll
-        for (int bb = 0; bb < KSTG; ++bb) {
-          const uint32_t b_addr = smem_u32(sB + s * kBStage + bb * BN * kBK);
-          const uint32_t a_tmem = tmem + BN + (s * KSTG + bb) * 32;
+        const int bg = g * kSkGroup, be = min(bg + kSkGroup, nb);
+        for (int b = bg; b < be; ++b) {
+          const uint32_t b_addr = smem_u32(sB + b * kBBlock);
+          const uint32_t a_tmem = tmem + BN + b * 32;
 #pragma unroll
           for (int kk = 0; kk < kBK / 32; ++kk)
             mma_i8_ts(tmem, a_tmem + kk * 8, sw128_desc(b_addr + kk * 32), idesc,
-                      (it > 0 || bb > 0 || kk > 0) ? 1u : 0u);
+                      (b > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(&sm->empty[s]);
       }
       __syncwarp();
     }
     if (lane == 0) {
-      if (ok) mma_commit(&sm->accf[0]);
+      if (ok) mma_commit(&sm->accf);
       mma_commit(&sm->drain);
     }
     __syncwarp();
@@ -664,38 +742,11 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
     __syncwarp();
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ expansion
-    pdl_wait();
-    const int r = tid - 128;
-    const int sub = r >> 4, rr = r & 15;
-    for (int it = 0; it < nst; ++it) {
-      const int s = it % STAGES;
-      const uint32_t ph = (it / STAGES) & 1u;
-      if (!wait_or_abort(sm, &sm->full_tma[s], ph)) break;
-#pragma unroll
-      for (int bb = 0; bb < KSTG; ++bb) {
-        const uint8_t* p = sP + s * kPStage + (sub * KSTG + bb) * kSubtileBytes + rr * 16;
-        uint32_t v[32];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const uint4 w = *reinterpret_cast<const uint4*>(p + h * 256);
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int sh = 6 - 2 * g, c = 2 * g + h;
-            v[4 * c + 0] = (w.x >> sh) & 0x03030303u;
-            v[4 * c + 1] = (w.y >> sh) & 0x03030303u;
-            v[4 * c + 2] = (w.z >> sh) & 0x03030303u;
-            v[4 * c + 3] = (w.w >> sh) & 0x03030303u;
-          }
-        }
-        tmem_st32(tmem + (static_cast<uint32_t>(r & ~31) << 16) + BN + (s * KSTG + bb) * 32, v);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm->full_a[s]);
-    }
+    sk_expand<BN, NB>(sm, sP, tmem, nb, 0);
   } else if (warp >= 8) {
     // ------------------------------------------------------------ epilogue
+    // First the odd expansion groups (no dependence on the previous kernel).
+    sk_expand<BN, NB>(sm, sP, tmem, nb, 1);
     pdl_wait();
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // tile row = TMEM lane
@@ -710,9 +761,9 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
       const int m = mt * kBM + t;
       e_sw[t] = (m < M && !acc_out) ? s_w[m] : 0.0f;
     }
-    bool have = nst > 0 && wait_or_abort(sm, &sm->accf[0], 0);
+    bool have = nb > 0 && wait_or_abort(sm, &sm->accf, 0);
     tc_fence_after();
-    // Stage the partial tile locally; the pipeline buffers are free once every
+    // Stage the partial tile locally; the activation blocks are free once every
     // MMA has completed (accf).
     int32_t* part = reinterpret_cast<int32_t*>(sB);
     const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -740,73 +791,77 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
         if (rows_o <= 0) continue;
         bulk_s2cluster(map_rank(smem_u32(red + static_cast<int>(rank) * RB * BNP), o),
                        smem_u32(part + static_cast<int>(o) * RB * BNP),
-                       static_cast<uint32_t>(rows_o) * BNP * 4, map_rank(smem_u32(red_full), o));
+                       static_cast<uint32_t>(rows_o) * BNP * 4, map_rank(smem_u32(&sm->red_full), o));
       }
     }
-    // Reduce and write this rank's rows once every peer's rows have landed.
-    bool ok = false;
-    for (uint32_t i = 0; i < kWaitLimit && !ok; ++i) ok = mbar_try_wait_cluster(red_full, 0);
-    if (!ok) record_error(DEVERR_MBAR_TIMEOUT);
-    __syncwarp();
-    // Phase 1: this CTA's incoming copies are complete (so are the peers' reads
-    // behind them); the wait before exit makes that true cluster-wide.
-    cluster_arrive();
-    // Lane = row (coalesced stores over m); each warp takes 4-column groups
-    // (quarter, quarter + 4, ...): one 16-byte load per source rank, all issued
-    // before the sums (a 4-word row run of red is conflict-free across 8 lanes).
-    const int row0 = static_cast<int>(rank) * RB;
-    const int nrows = (row0 + RB <= kBM ? RB : kBM - row0);
-    if (ok) {
-      for (int rb = 0; rb < nrows; rb += 32) {
-        const int rr = rb + lane;
-        const int m = mt * kBM + row0 + rr;
-        if (rr >= nrows || m >= M) continue;
-        const float sw = e_sw[row0 + rr];
-        for (int g = quarter; g < BN / 4 && 4 * g < N; g += 4) {
-          const int j0 = 4 * g;
-          uint4 pv[8];
+  }
+
+  // ---------------------------------------------------------------- owner reduce
+  // All 12 warps: a single warp per SM sub-partition leaves the dependent
+  // load-add-scale-store chains exposed. The epilogue warps published the
+  // column and row scalars before their barrier; the others finish phase 0 now.
+  if (warp < 8) cluster_wait();
+  __syncthreads();
+  bool ok = false;
+  for (uint32_t i = 0; i < kWaitLimit && !ok; ++i) ok = mbar_try_wait_cluster(&sm->red_full, 0);
+  if (!ok && tid == 0) record_error(DEVERR_MBAR_TIMEOUT);
+  __syncwarp();
+  // Phase 1: this CTA's incoming copies are complete (so are the peers' reads
+  // behind them); the wait before exit makes that true cluster-wide.
+  cluster_arrive();
+  // Work item (row block of 32, 4-column group) per warp; lane = row, so the
+  // stores run over consecutive m. One 16-byte load per source rank, all issued
+  // before the sums (a 4-word run of red is conflict-free across 8 lanes).
+  const int row0 = static_cast<int>(rank) * RB;
+  const int nrows = (row0 + RB <= kBM ? RB : kBM - row0);
+  const int nrb = (nrows + 31) >> 5;  // 1 or 2 row blocks (RB <= 64)
+  const int ngrp = min(BN, N + 3) >> 2;
+  if (ok) {
+    for (int item = warp; item < nrb * ngrp; item += kThreads / 32) {
+      const int rb = item % nrb, grp = item / nrb;
+      const int rr = rb * 32 + lane;
+      const int m = mt * kBM + row0 + rr;
+      if (rr >= nrows || m >= M) continue;
+      const int j0 = 4 * grp;
+      uint4 pv[8];
 #pragma unroll
-          for (uint32_t src = 0; src < 8; ++src)
-            if (src < S) pv[src] = *reinterpret_cast<const uint4*>(red + (src * RB + rr) * BNP + j0);
-          int sum[4] = {0, 0, 0, 0};
+      for (uint32_t src = 0; src < 8; ++src)
+        if (src < S) pv[src] = *reinterpret_cast<const uint4*>(red + (src * RB + rr) * BNP + j0);
+      int sum[4] = {0, 0, 0, 0};
 #pragma unroll
-          for (uint32_t src = 0; src < 8; ++src)
-            if (src < S) {
-              sum[0] += static_cast<int>(pv[src].x);
-              sum[1] += static_cast<int>(pv[src].y);
-              sum[2] += static_cast<int>(pv[src].z);
-              sum[3] += static_cast<int>(pv[src].w);
-            }
+      for (uint32_t src = 0; src < 8; ++src)
+        if (src < S) {
+          sum[0] += static_cast<int>(pv[src].x);
+          sum[1] += static_cast<int>(pv[src].y);
+          sum[2] += static_cast<int>(pv[src].z);
+          sum[3] += static_cast<int>(pv[src].w);
+        }
+      const float sw = e_sw[row0 + rr];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int j = j0 + c;
-            if (j >= N) break;
-            const int d = sum[c] - e_qs[j];
-            const size_t o = static_cast<size_t>(j) * M + m;
-            if (acc_out) {
-              acc_out[o] = d;
-            } else {
-              const float fd = static_cast<float>(d);
-              const float sx = e_sx[j];
-              y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx)
-                                         : __fmul_rn(fd, __fmul_rn(sw, sx));
-            }
-          }
+      for (int c = 0; c < 4; ++c) {
+        const int j = j0 + c;
+        if (j >= N) break;
+        const int d = sum[c] - e_qs[j];
+        const size_t o = static_cast<size_t>(j) * M + m;
+        if (acc_out) {
+          acc_out[o] = d;
+        } else {
+          const float fd = static_cast<float>(d);
+          const float sx = e_sx[j];
+          y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx)
+                                     : __fmul_rn(fd, __fmul_rn(sw, sx));
         }
       }
     }
   }
 
-  if (warp < 8) {  // phase 0 then phase 1 for the roles that send and receive nothing
-    cluster_wait();
-    cluster_arrive();
-  }
   tc_fence_before();
   __syncthreads();
   cluster_wait();  // phase 1: no copy still reads or writes any CTA's shared memory
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem, kTmemCols);
 }
+
 
 // ---- host side ------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -912,21 +967,14 @@ cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, cons
                             W.in_dim, order);
 }
 
-template <int BN, int STAGES, int KSTG>
-size_t gemm_sk_smem_bytes() {
-  constexpr int BNP = BN + 4;
-  return 1024 + static_cast<size_t>(STAGES) * (KSTG * BN * kBK + KSTG * kPackedBlock) +
-         static_cast<size_t>(kRedRows) * BNP * 4 + (2 * BN + kBM) * 4 + sizeof(GemmSmem);
-}
-
-template <int BN, int STAGES, int KSTG>
+template <int BN>
 cudaError_t gemm_sk(const WeightView& W, const int8_t* q, const float* s_x, const int32_t* qsum,
                     int n, float* y, int32_t* acc, int order, int S, cudaStream_t s) {
   CUtensorMap qmap, wmap;
-  if (!make_q_map(&qmap, q, n, W.in_dim, BN, KSTG) || !make_w_map(&wmap, W, KSTG))
+  if (!make_q_map(&qmap, q, n, W.in_dim, BN, 1) || !make_w_map(&wmap, W, 1))
     return cudaErrorInvalidValue;
-  const size_t smem = gemm_sk_smem_bytes<BN, STAGES, KSTG>();
-  auto kern = k_gemm_sk<BN, STAGES, KSTG>;
+  const size_t smem = sk_smem_launch<BN>();
+  auto kern = k_gemm_sk<BN>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -955,18 +1003,18 @@ cudaError_t gemm_sk(const WeightView& W, const int8_t* q, const float* s_x, cons
                             W.in_dim, order);
 }
 
-// Clusters of S CTAs of k_gemm_sk<BN, STAGES, KSTG> that fit on the device at once
-// (cached per device and S). Clusters must sit inside one GPC, so this falls off
-// faster than num_sms / S (B200: 74 for S = 2, 33 for 4, 22 for 6, 15 for 8).
-template <int BN, int STAGES, int KSTG>
+// Clusters of S CTAs of k_gemm_sk<BN> that fit on the device at once (cached per
+// device and S). Clusters must sit inside one GPC, so this falls off faster than
+// num_sms / S (B200: 74 for S = 2, 33 for 4, 22 for 6, 15 for 8).
+template <int BN>
 int sk_max_clusters(int S) {
   static int cache[64][9] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || S < 2 || S > 8) return 0;
   if (cache[dev][S]) return cache[dev][S] > 0 ? cache[dev][S] : 0;
-  auto kern = k_gemm_sk<BN, STAGES, KSTG>;
-  const size_t smem = gemm_sk_smem_bytes<BN, STAGES, KSTG>();
+  auto kern = k_gemm_sk<BN>;
+  const size_t smem = sk_smem_launch<BN>();
   int count = 0;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) == cudaSuccess) {
@@ -988,10 +1036,8 @@ int sk_max_clusters(int S) {
   return count;
 }
 
-// Upper bound on the CTAs of one split-K launch. SMs left free let the next
-// kernel of a decode step start early (programmatic dependent launch) and
-// prefetch its weights. OBN_GEMM_SPLIT_K=<n> overrides it (0 disables split-K);
-// read once per process.
+// Upper bound on the CTAs of one split-K launch; OBN_GEMM_SPLIT_K=<n> overrides
+// it (0 disables split-K). Read once per process.
 int split_k_cta_cap() {
   static const int cap = [] {
     const char* e = std::getenv("OBN_GEMM_SPLIT_K");
@@ -1000,24 +1046,28 @@ int split_k_cta_cap() {
   return cap;
 }
 
-// Cluster size for split-K: the largest S <= 8 (and <= the number of K stages)
-// for which one cluster per 128-row tile fits on the device in a single wave
-// within the CTA cap; 1 (no split) when that leaves S < 2.
-template <int BN, int STAGES, int KSTG>
+// Cluster size for split-K: the largest S <= 8 whose K slices fit one CTA
+// (<= sk_blocks<BN>() blocks) and for which one cluster per 128-row tile fits on
+// the device in a single wave within the CTA cap; 1 (no split) otherwise.
+template <int BN>
 int split_k_factor(const WeightView& W) {
   const int num_m = (W.out_dim + kBM - 1) / kBM;
   const int cap = split_k_cta_cap();
-  const int total_st = (W.in_dim / kBK + KSTG - 1) / KSTG;
-  for (int S = total_st < 8 ? total_st : 8; S >= 2; --S)
-    if (S * num_m <= cap && num_m <= sk_max_clusters<BN, STAGES, KSTG>(S))
+  const int KB = W.in_dim / kBK;
+  for (int S = KB < 8 ? KB : 8; S >= 2; --S) {
+    if ((KB + S - 1) / S > sk_blocks<BN>()) break;  // a smaller S only lengthens the slices
+    if (S * num_m <= cap && num_m <= sk_max_clusters<BN>(S))
       return (S == 2 && BN >= 64) ? 1 : S;  // measured: a 2-way split of a >= 64-token tile gains nothing
+  }
   return 1;
 }
 
 }  // namespace
 
 bool gemm_supported(const WeightView& W, int n) {
-  return n >= kGemmMinTokens && W.in_dim % kBK == 0 && W.m_pad % kBM == 0 && encode_fn() != nullptr;
+  if (W.in_dim % kBK != 0 || W.m_pad % kBM != 0 || encode_fn() == nullptr) return false;
+  // Below 16 tokens only the split-K form beats the dp4a GEMV (measured on B200).
+  return n >= kGemmMinTokens || (n >= kGemmMinSplitTokens && split_k_factor<16>(W) > 1);
 }
 
 cudaError_t launch_gemm(const WeightView& W, const int8_t* q, const float* s_x,
@@ -1025,14 +1075,14 @@ cudaError_t launch_gemm(const WeightView& W, const int8_t* q, const float* s_x,
                         cudaStream_t s) {
   // Few 128-row tiles: split K over a cluster per tile.
   int S = 1;
-  if (n <= 16 && (S = split_k_factor<16, 4, 2>(W)) > 1)
-    return gemm_sk<16, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
-  if (n > 16 && n <= 32 && (S = split_k_factor<32, 4, 2>(W)) > 1)
-    return gemm_sk<32, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
-  if (n > 32 && n <= 64 && (S = split_k_factor<64, 4, 2>(W)) > 1)
-    return gemm_sk<64, 4, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
-  if (n > 64 && n <= 128 && (S = split_k_factor<128, 3, 2>(W)) > 1)
-    return gemm_sk<128, 3, 2>(W, q, s_x, qsum, n, y, acc, order, S, s);
+  if (n <= 16 && (S = split_k_factor<16>(W)) > 1)
+    return gemm_sk<16>(W, q, s_x, qsum, n, y, acc, order, S, s);
+  if (n > 16 && n <= 32 && (S = split_k_factor<32>(W)) > 1)
+    return gemm_sk<32>(W, q, s_x, qsum, n, y, acc, order, S, s);
+  if (n > 32 && n <= 64 && (S = split_k_factor<64>(W)) > 1)
+    return gemm_sk<64>(W, q, s_x, qsum, n, y, acc, order, S, s);
+  if (n > 64 && n <= 128 && (S = split_k_factor<128>(W)) > 1)
+    return gemm_sk<128>(W, q, s_x, qsum, n, y, acc, order, S, s);
   // Small token tiles: 4-block stages (16 MMAs per commit) amortise the commit cost.
   if (n <= 16) return gemm_bn<16, 3, 4, true>(W, q, s_x, qsum, n, y, acc, order, s);
   if (n <= 32) return gemm_bn<32, 3, 4, true>(W, q, s_x, qsum, n, y, acc, order, s);

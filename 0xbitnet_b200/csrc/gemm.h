@@ -5,8 +5,10 @@
 
 namespace obn {
 
-// Smallest token count routed to the tensor-core GEMM.
+// Smallest token count routed to the tensor-core GEMM, and to its split-K
+// (thread-block cluster) form when the layer has few 128-row tiles.
 constexpr int kGemmMinTokens = 16;
+constexpr int kGemmMinSplitTokens = 4;
 
 // True when launch_gemm handles this shape (otherwise the dp4a path runs).
 bool gemm_supported(const WeightView& W, int n);

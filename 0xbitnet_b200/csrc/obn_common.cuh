@@ -19,6 +19,7 @@ namespace obn {
 enum : uint32_t {
   DEVERR_NONE = 0,
   DEVERR_MBAR_TIMEOUT = 1,
+  DEVERR_BAD_LAUNCH = 2,  // launch geometry outside what the kernel was built for
 };
 // Internal linkage: every translation unit (built without -rdc) owns its own
 // copy and exposes it through a host reader (kernels.h).

@@ -1,8 +1,10 @@
 """GPU parity of the tensor-core (tcgen05 kind::i8) ternary GEMM path.
 
-Token counts >= 16 run on the tensor cores. Shapes cover partial tiles in both
-the weight-row (128) and token (32/64/128/256) dimensions, single and many K
-blocks, one and several tiles per persistent CTA.
+Token counts >= 16 run on the tensor cores, and so do 4-15 tokens when the
+layer has few enough 128-row tiles for the split-K (cluster) form. Shapes cover
+partial tiles in both the weight-row (128) and token (16/32/64/128/256)
+dimensions, single and many K blocks, one and several tiles per persistent CTA,
+and cluster sizes 2 through 8.
 """
 import numpy as np
 import pytest
@@ -42,7 +44,7 @@ def test_gemm_acc_bitexact(torch, M, K, n):
     assert np.array_equal(got, want)
 
 
-@pytest.mark.parametrize("n", [16, 32, 64, 512])
+@pytest.mark.parametrize("n", [4, 8, 16, 32, 64, 512])
 def test_gemm_forward_matches_oracle(torch, n):
     M, K = 2560, 2560
     L = synth().layer(700 + n, M, K)
@@ -56,7 +58,8 @@ def test_gemm_forward_matches_oracle(torch, n):
 @pytest.mark.parametrize("M,K,n", [(128, 2560, 16), (300, 2560, 64), (2560, 2560, 32),
                                    (3840, 2560, 128), (6912, 2560, 100), (2560, 6912, 64),
                                    (1000, 384, 48), (640, 1280, 128), (2560, 9216, 16),
-                                   (2000, 640, 20), (1920, 1664, 40)])
+                                   (2000, 640, 20), (1920, 1664, 40), (2560, 2560, 4),
+                                   (3840, 2560, 8), (2560, 6912, 12), (6912, 2560, 5)])
 def test_gemm_split_k_cluster_bitexact(torch, M, K, n):
     # token counts <= 128 with few 128-row tiles run split-K over a cluster of up
     # to 8 CTAs (bulk-copy reduce-scatter through distributed shared memory);
