@@ -1056,8 +1056,7 @@ int split_k_factor(const WeightView& W) {
   const int KB = W.in_dim / kBK;
   for (int S = KB < 8 ? KB : 8; S >= 2; --S) {
     if ((KB + S - 1) / S > sk_blocks<BN>()) break;  // a smaller S only lengthens the slices
-    if (S * num_m <= cap && num_m <= sk_max_clusters<BN>(S))
-      return (S == 2 && BN >= 64) ? 1 : S;  // measured: a 2-way split of a >= 64-token tile gains nothing
+    if (S * num_m <= cap && num_m <= sk_max_clusters<BN>(S)) return S;
   }
   return 1;
 }
