@@ -56,8 +56,9 @@ def parse_args():
     p.add_argument("--prefill", type=str, default="512,2048,8192",
                    help="config-2 token counts for the prefill TOPS block ('' to skip)")
     p.add_argument("--case", type=str, default=None,
-                   help="SHAPE:B — run a few forwards of one 2B shape at B tokens and exit "
-                        "(a small, self-contained workload for ncu captures)")
+                   help="SHAPE:B — run a few forwards of one 2B shape (or of 'all' five in "
+                        "turn) at B tokens and exit (a small, self-contained workload for ncu "
+                        "captures)")
     return p.parse_args()
 
 
@@ -394,7 +395,8 @@ def run_ours(args):
     obn.check_device_errors()
 
     step_bytes = {B: args.layers * sum(fwd_bytes(M, K, B) for _, (M, K) in shp) for B in batches}
-    launches_per_step = 2 * args.layers * len(shp) * len(batches)
+    # B = 1: one fused kernel per forward; B > 1: RMSNorm+quantize, then the matmul.
+    launches_per_step = sum(1 if B == 1 else 2 for B in batches) * args.layers * len(shp)
 
     def step(evs=None):
         for j, B in enumerate(batches):
@@ -499,7 +501,10 @@ def run_ours(args):
             ms = k0.elapsed_time(k1) / reps
             nl = args.layers * len(shp)
             kb = args.layers * sum(gemv_kernel_bytes(M, K, B) for _, (M, K) in shp)
-            name = ("k_gemv (dp4a, B=%d)" % B) if B < 16 else ("k_gemm (tcgen05 kind::i8, B=%d)" % B)
+            # Every BitNet-2B shape has < 74 row tiles, so from 4 tokens up the
+            # library takes the split-K cluster GEMM (launch list in profiles/).
+            name = ("k_gemv (dp4a, B=%d)" % B) if B < 4 else (
+                "k_gemm_sk (tcgen05 kind::i8, split-K over clusters, B=%d)" % B)
             kernels[B] = {"kernel": name, "bound": "hbm", "us": ms * 1e3 / nl, "bytes": kb / nl,
                           "step_share_ms": ms}
             del gk
@@ -573,24 +578,29 @@ def run_ours(args):
 
 
 def run_case(spec: str):
-    """A few BitLinear forwards of one shape (4 layers, cold weights) for profilers."""
+    """A few BitLinear forwards of one shape, or of every shape in turn ("all"),
+    4 layers each with distinct weights, for profilers: SHAPE:B, e.g. gate:64."""
     import torch
     obn = importlib.import_module("0xbitnet_b200")
     synth = importlib.import_module("0xbitnet_b200.synthetic")
     name, B = spec.split(":")
     B = int(B)
-    M, K = synth.SHAPES_2B[name]
-    layers = []
-    for i in range(4):
-        packed, s_w, gamma = synth.layer_device(77 + i, M, K)
-        layers.append(obn.BitLinear(packed, s_w, gamma, K, M))
-    x = torch.randn(B, K, device="cuda")
-    for _ in range(3):
+    names = list(synth.SHAPES_2B) if name == "all" else [name]
+    for nm in names:
+        M, K = synth.SHAPES_2B[nm]
+        layers = []
+        for i in range(4):
+            packed, s_w, gamma = synth.layer_device(77 + i, M, K)
+            layers.append(obn.BitLinear(packed, s_w, gamma, K, M))
+        x = torch.randn(B, K, device="cuda")
+        for _ in range(3):
+            for L in layers:
+                L.forward(x)
+        torch.cuda.synchronize()
+        obn.check_device_errors()
         for L in layers:
-            L.forward(x)
-    torch.cuda.synchronize()
-    obn.check_device_errors()
-    print(f"case {name} {M}x{K} B={B}: ok")
+            L.close()
+        print(f"case {nm} {M}x{K} B={B}: ok")
 
 
 def main():
