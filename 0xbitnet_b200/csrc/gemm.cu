@@ -192,7 +192,6 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                                                       int K, int order) {
   constexpr int kAStage = KSTG * kBM * kBK;      // expanded A bytes per stage (smem variant)
   constexpr int kBStage = KSTG * BN * kBK;       // activation bytes per stage
-  constexpr int kColWords = (BN + 31) / 32;     // column scalars held per lane
   constexpr int kPStage = KSTG * kPackedBlock;   // packed weight bytes per stage
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
@@ -413,35 +412,28 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
       const int mt = t % num_m, nt = t / num_m;
       const int a = ti & 1;
       const uint32_t aph = (ti >> 1) & 1u;
-      // This tile's per-row and per-column scalars are fetched before the
-      // accumulator is ready, so no global load sits between accf and the stores.
-      const int m = mt * kBM + quarter * 32 + lane;
-      const float sw = (m < M && !acc_out) ? s_w[m] : 0.0f;
-      int qs_r[kColWords];
-      float sx_r[kColWords];
-#pragma unroll
-      for (int i = 0; i < kColWords; ++i) {
-        const int c = nt * BN + 32 * i + lane;
-        qs_r[i] = c < N ? qsum[c] : 0;
-        sx_r[i] = (c < N && !acc_out) ? s_x[c] : 0.0f;
-      }
       if (!wait_or_abort(sm, &sm->accf[a], aph)) break;
       tc_fence_after();
+      const int m = mt * kBM + quarter * 32 + lane;
+      const float sw = (m < M && !acc_out) ? s_w[m] : 0.0f;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
-      uint32_t v[2][16];
-      tmem_ld16(taddr, v[0]);
-      tmem_ld_wait();
-#pragma unroll
+#pragma unroll 1
       for (int j0 = 0; j0 < BN; j0 += 16) {
-        const int cur = (j0 / 16) & 1;
-        if (j0 + 16 < BN) tmem_ld16(taddr + j0 + 16, v[cur ^ 1]);  // overlaps the stores below
+        uint32_t v[16];
+        tmem_ld16(taddr + j0, v);
+        tmem_ld_wait();
+        const int n0 = nt * BN + j0;
+        // Column j's code sum and scale, fetched once per warp and broadcast.
+        const int nl = n0 + (lane & 15);
+        const int qs_l = nl < N ? qsum[nl] : 0;
+        const float sx_l = (nl < N && !acc_out) ? s_x[nl] : 0.0f;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int cj = j0 + j, n = nt * BN + cj;
-          const int qs_j = __shfl_sync(0xffffffffu, qs_r[cj / 32], cj % 32);
-          const float sx_j = __shfl_sync(0xffffffffu, sx_r[cj / 32], cj % 32);
+          const int n = n0 + j;
+          const int qs_j = __shfl_sync(0xffffffffu, qs_l, j);
+          const float sx_j = __shfl_sync(0xffffffffu, sx_l, j);
           if (n < N && m < M) {
-            const int d = static_cast<int>(v[cur][j]) - qs_j;
+            const int d = static_cast<int>(v[j]) - qs_j;
             const size_t o = static_cast<size_t>(n) * M + m;
             if (acc_out) {
               acc_out[o] = d;
@@ -452,7 +444,6 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
             }
           }
         }
-        tmem_ld_wait();
       }
       tc_fence_before();
       __syncwarp();
