@@ -120,6 +120,30 @@ class BitLinear:
 
     __call__ = forward
 
+    def forward_tp(self, input: torch.Tensor, out_total: int, col0: int,
+                   out_mc: int | None = None, out_ranks: list[int] | None = None,
+                   n: int | None = None) -> None:
+        """Tensor-parallel forward: this layer holds rows [col0, col0 + out_dim) of
+        an out_total-row weight; writes them into columns [col0, col0 + out_dim) of
+        every rank's [n, out_total] f32 output, through the multicast address
+        `out_mc` or the per-rank device addresses `out_ranks` (ints). The caller
+        orders all ranks' calls before reading (a barrier on the stream)."""
+        _require_cuda_f32(input, "input")
+        if n is None:
+            n = input.numel() // self.in_dim
+        if (out_mc is None) == (out_ranks is None):
+            raise ValueError("give exactly one of out_mc and out_ranks")
+        world = len(out_ranks) if out_ranks is not None else self._tp_world
+        ranks = None
+        if out_ranks is not None:
+            ranks = (ctypes.c_void_p * len(out_ranks))(*[ctypes.c_void_p(p) for p in out_ranks])
+        ws = self._workspace(n)
+        check(lib().obn_bitlinear_forward_tp(
+            self._h, _ptr(input), n, ctypes.c_void_p(out_mc) if out_mc is not None else None,
+            ranks, world, out_total, col0, _ptr(ws), ws.numel(), _stream(self.device)))
+
+    _tp_world = 1
+
     def matmul(self, q: torch.Tensor, scales: torch.Tensor, qsum: torch.Tensor,
                n: int | None = None) -> torch.Tensor:
         """Ternary GEMV/GEMM on already-quantized activations (int8 [n, in_dim])."""

@@ -338,6 +338,56 @@ int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, int n, flo
   return OBN_OK;
 }
 
+int obn_bitlinear_forward_tp(const obn_bitlinear* layer, const float* x, int n, float* y_mc,
+                             float* const* y_ranks, int world, int out_total, int col0,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (int rc = check_layer(layer)) return rc;
+  if (!x || !workspace || (!y_mc && !y_ranks))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (world < 1 || world > obn::kMaxGatherRanks)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "world must be in 1..%d (got %d)", obn::kMaxGatherRanks,
+                world);
+  if (col0 < 0 || out_total <= 0 || static_cast<long long>(col0) + layer->out_dim > out_total)
+    return fail(OBN_ERR_INVALID_ARGUMENT,
+                "columns [%d, %d) do not fit an output of %d columns", col0,
+                col0 + layer->out_dim, out_total);
+  if (n < obn::kGemmMinTokens || !obn::gemm_supported(view(layer), n))
+    return fail(OBN_ERR_UNSUPPORTED, "the gathered forward needs n >= %d tokens (got %d)",
+                obn::kGemmMinTokens, n);
+  const size_t need = obn_bitlinear_workspace_bytes(layer, n);
+  if (workspace_bytes < need)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than the %zu needed",
+                workspace_bytes, need);
+  if (!aligned(workspace, 256) || !aligned(x, 16))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "workspace must be 256-byte and x 16-byte aligned");
+  obn::GatherOut go;
+  go.mc = y_mc;
+  go.world = world;
+  go.ldy = out_total;
+  go.col0 = col0;
+  if (!y_mc)
+    for (int r = 0; r < world; ++r) {
+      if (!y_ranks[r]) return fail(OBN_ERR_INVALID_ARGUMENT, "y_ranks[%d] is null", r);
+      if (!aligned(y_ranks[r], 4))
+        return fail(OBN_ERR_INVALID_ARGUMENT, "y_ranks[%d] is not 4-byte aligned", r);
+      go.ranks[r] = y_ranks[r];
+    }
+  else if (!aligned(y_mc, 4))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "y_mc is not 4-byte aligned");
+  auto* base = static_cast<uint8_t*>(workspace);
+  auto* q = reinterpret_cast<int8_t*>(base);
+  auto* sc = reinterpret_cast<float*>(base + align256(static_cast<size_t>(n) * layer->in_dim));
+  auto* qs = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(sc) + align256(sizeof(float) * n));
+  auto s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = obn::launch_rmsnorm_quant(x, layer->norm, layer->eps, n, layer->in_dim, q, sc,
+                                            qs, s);
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
+  e = obn::launch_gemm_gather(view(layer), q, sc, qs, n, obn::kOrderGemm, go, s);
+  if (e != cudaSuccess) return cuda_fail(e, "gathered ternary GEMM launch");
+  return OBN_OK;
+}
+
 int obn_bitlinear_export_i2s(const obn_bitlinear* layer, uint8_t* dst_dev, void* stream) {
   clear_error();
   if (int rc = check_layer(layer)) return rc;

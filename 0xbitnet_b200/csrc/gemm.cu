@@ -181,7 +181,17 @@ OBN_DEVINL bool wait_or_abort(Smem* sm, uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-template <int BN, int STAGES, int KSTG, bool A_TMEM>
+// Output modes of k_gemm: the plain [N][M] output, or a tensor-parallel gather
+// that writes this rank's columns of every rank's [N][ldy] output as it goes.
+enum : int { kOutLocal = 0, kOutMulticast = 1, kOutPeers = 2 };
+
+// One f32 store through a multicast (NVLS) address: the switch writes it into
+// every rank's buffer bound to the multicast object.
+OBN_DEVINL void multimem_st_f32(float* addr, float v) {
+  asm volatile("multimem.st.global.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
+}
+
+template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal>
 __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CUtensorMap tmap_q,
                                                       const __grid_constant__ CUtensorMap tmap_w,
                                                       const float* __restrict__ s_w,
@@ -189,7 +199,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                                                       const int32_t* __restrict__ qsum,
                                                       float* __restrict__ y,
                                                       int32_t* __restrict__ acc_out, int M, int N,
-                                                      int K, int order) {
+                                                      int K, int order, const GatherOut go) {
   constexpr int kAStage = KSTG * kBM * kBK;      // expanded A bytes per stage (smem variant)
   constexpr int kBStage = KSTG * BN * kBK;       // activation bytes per stage
   constexpr int kPStage = KSTG * kPackedBlock;   // packed weight bytes per stage
@@ -435,12 +445,24 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
           if (n < N && m < M) {
             const int d = static_cast<int>(v[j]) - qs_j;
             const size_t o = static_cast<size_t>(n) * M + m;
-            if (acc_out) {
+            if (OUT == kOutLocal && acc_out) {
               acc_out[o] = d;
             } else {
               const float fd = static_cast<float>(d);
-              y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx_j)
-                                         : __fmul_rn(fd, __fmul_rn(sw, sx_j));
+              const float val = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx_j)
+                                                    : __fmul_rn(fd, __fmul_rn(sw, sx_j));
+              if constexpr (OUT == kOutLocal) {
+                y[o] = val;
+              } else {
+                const size_t og = static_cast<size_t>(n) * go.ldy + go.col0 + m;
+                if constexpr (OUT == kOutMulticast) {
+                  multimem_st_f32(go.mc + og, val);
+                } else {
+#pragma unroll
+                  for (int p = 0; p < kMaxGatherRanks; ++p)
+                    if (p < go.world) go.ranks[p][og] = val;
+                }
+              }
             }
           }
         }
@@ -449,6 +471,9 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm->acce[a]);
     }
+    // Gathered outputs: this thread's remote stores are performed before the
+    // kernel completes, so a stream-ordered barrier after it publishes them.
+    if constexpr (OUT != kOutLocal) __threadfence_system();
   }
 
   tc_fence_before();
@@ -924,15 +949,16 @@ bool make_w_map(CUtensorMap* map, const WeightView& W, int KSTG) {
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, int KSTG, bool A_TMEM>
+template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal>
 cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, const int32_t* qsum,
-                    int n, float* y, int32_t* acc, int order, cudaStream_t s) {
+                    int n, float* y, int32_t* acc, int order, cudaStream_t s,
+                    const GatherOut& go = GatherOut{}) {
   if (!encode_fn()) return cudaErrorNotSupported;
   CUtensorMap qmap, wmap;
   if (!make_q_map(&qmap, q, n, W.in_dim, BN, KSTG) || !make_w_map(&wmap, W, KSTG))
     return cudaErrorInvalidValue;
   const size_t smem = gemm_smem_bytes<BN, STAGES, KSTG, A_TMEM>();
-  auto kern = k_gemm<BN, STAGES, KSTG, A_TMEM>;
+  auto kern = k_gemm<BN, STAGES, KSTG, A_TMEM, OUT>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -955,7 +981,7 @@ cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, cons
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, qmap, wmap, W.s_w, s_x, qsum, y, acc, W.out_dim, n,
-                            W.in_dim, order);
+                            W.in_dim, order, go);
 }
 
 template <int BN>
@@ -1079,6 +1105,18 @@ cudaError_t launch_gemm(const WeightView& W, const int8_t* q, const float* s_x,
   if (n <= 64) return gemm_bn<64, 3, 4, true>(W, q, s_x, qsum, n, y, acc, order, s);
   if (n <= 128) return gemm_bn<128, 4, 2, true>(W, q, s_x, qsum, n, y, acc, order, s);
   return gemm_bn<256, 4, 1, false>(W, q, s_x, qsum, n, y, acc, order, s);
+}
+
+cudaError_t launch_gemm_gather(const WeightView& W, const int8_t* q, const float* s_x,
+                               const int32_t* qsum, int n, int order, const GatherOut& go,
+                               cudaStream_t s) {
+  if (go.world < 1 || go.world > kMaxGatherRanks) return cudaErrorInvalidValue;
+  if (go.mc) {
+    if (n <= 128) return gemm_bn<128, 4, 2, true, kOutMulticast>(W, q, s_x, qsum, n, nullptr, nullptr, order, s, go);
+    return gemm_bn<256, 4, 1, false, kOutMulticast>(W, q, s_x, qsum, n, nullptr, nullptr, order, s, go);
+  }
+  if (n <= 128) return gemm_bn<128, 4, 2, true, kOutPeers>(W, q, s_x, qsum, n, nullptr, nullptr, order, s, go);
+  return gemm_bn<256, 4, 1, false, kOutPeers>(W, q, s_x, qsum, n, nullptr, nullptr, order, s, go);
 }
 
 cudaError_t read_and_clear_dev_error_gemm(uint32_t* out) {

@@ -10,6 +10,21 @@ namespace obn {
 constexpr int kGemmMinTokens = 16;
 constexpr int kGemmMinSplitTokens = 4;
 
+// Output of a tensor-parallel (output-feature split) GEMM: this rank computes
+// columns [col0, col0 + out_dim) of an [n][ldy] f32 output that every rank
+// holds, and writes them into all of those outputs from its epilogue: one
+// multimem store through `mc` (an NVLS multicast address bound to every rank's
+// buffer) or, when mc is null, one store per rank through `ranks` (each rank's
+// buffer as mapped on this device: peer stores over NVLink).
+constexpr int kMaxGatherRanks = 8;
+struct GatherOut {
+  float* mc = nullptr;
+  float* ranks[kMaxGatherRanks] = {};
+  int world = 0;
+  int ldy = 0;
+  int col0 = 0;
+};
+
 // True when launch_gemm handles this shape (otherwise the dp4a path runs).
 bool gemm_supported(const WeightView& W, int n);
 
@@ -17,5 +32,10 @@ bool gemm_supported(const WeightView& W, int n);
 cudaError_t launch_gemm(const WeightView& W, const int8_t* q, const float* s_x,
                         const int32_t* qsum, int n, float* y, int32_t* acc, int order,
                         cudaStream_t s);
+
+// The tensor-parallel gather form of the GEMM (n >= kGemmMinTokens).
+cudaError_t launch_gemm_gather(const WeightView& W, const int8_t* q, const float* s_x,
+                               const int32_t* qsum, int n, int order, const GatherOut& go,
+                               cudaStream_t s);
 
 }  // namespace obn

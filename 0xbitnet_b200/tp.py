@@ -1,0 +1,97 @@
+"""Tensor-parallel BitLinear: output features split over ranks, gathered in the GEMM.
+
+Config-4 prefill plan for a 3B-class layer: each rank (one GPU) owns the
+contiguous row block [col0, col0 + rows) of the I2_S weight — a row slice of the
+GGUF tensor, so nothing is repacked across ranks — computes its [n, rows] part
+and writes it from the GEMM epilogue into columns [col0, col0 + rows) of the
+[n, out_total] f32 output that every rank holds (``obn_bitlinear_forward_tp``):
+through one NVLS multicast address when the group has one (a single store per
+element, replicated by the NVSwitch), otherwise through each rank's buffer as
+mapped on this device (one peer store per rank over NVLink). The output buffers
+are symmetric memory (``torch.distributed._symmetric_memory``: PyTorch allocates
+them and exchanges the mappings; libobn only receives plain device addresses).
+
+The reference has no multi-GPU path; the layer it distributes is
+``BitLinear::forward`` (packages/rust/crates/oxbitnet/src/nn/bitlinear.rs:52-97).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import i2s
+
+__all__ = ["row_range", "slice_i2s_rows", "GatherOutput", "TPBitLinear"]
+
+
+def row_range(out_dim: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous row block of `rank`: [rank*out_dim//world, (rank+1)*out_dim//world)."""
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    return rank * out_dim // world, (rank + 1) * out_dim // world
+
+
+def slice_i2s_rows(blob, in_dim: int, out_dim: int, row0: int, row1: int) -> np.ndarray:
+    """Rows [row0, row1) of a GGUF I2_S tensor as an I2_S tensor of its own
+    (packed rows + the same 32-byte scale trailer)."""
+    rows, scale = i2s.split_tensor(blob, in_dim, out_dim)
+    if not 0 <= row0 < row1 <= out_dim:
+        raise ValueError(f"bad row range [{row0}, {row1}) of {out_dim}")
+    return i2s.make_tensor(rows[row0:row1], scale)
+
+
+class GatherOutput:
+    """The [n_max, out_total] f32 output every rank holds, in symmetric memory."""
+
+    def __init__(self, n_max: int, out_total: int, group=None, device=None):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        self.group = group if group is not None else dist.group.WORLD
+        self.device = device if device is not None else torch.device("cuda",
+                                                                     torch.cuda.current_device())
+        self.n_max, self.out_total = n_max, out_total
+        self.buf = symm_mem.empty((n_max, out_total), dtype=torch.float32, device=self.device)
+        self.handle = symm_mem.rendezvous(self.buf, self.group)
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        # buffer_ptrs / multicast_ptr address each rank's allocation; the tensor may
+        # start at an offset inside it (the same offset on every rank).
+        base = [int(p) for p in self.handle.buffer_ptrs]
+        off = self.buf.data_ptr() - base[self.rank]
+        self.rank_ptrs = [p + off for p in base]
+        mc = int(getattr(self.handle, "multicast_ptr", 0) or 0)
+        self.mc_ptr = mc + off if mc else 0
+
+    def view(self, n: int):
+        return self.buf[:n]
+
+    def barrier(self) -> None:
+        """Stream-ordered barrier over the group (every rank's writes landed)."""
+        self.handle.barrier(channel=0)
+
+
+class TPBitLinear:
+    """This rank's row block of a BitLinear, with a gathered forward."""
+
+    def __init__(self, blob, in_dim: int, out_total: int, world: int, rank: int,
+                 norm_weight=None, eps: float = 1e-5, device: int = 0):
+        from .bitlinear import BitLinear
+        self.row0, self.row1 = row_range(out_total, world, rank)
+        self.in_dim, self.out_total, self.world, self.rank = in_dim, out_total, world, rank
+        part = slice_i2s_rows(blob, in_dim, out_total, self.row0, self.row1)
+        self.layer = BitLinear.from_i2s(part, in_dim, self.row1 - self.row0,
+                                        norm_weight=norm_weight, eps=eps, device=device)
+
+    def forward(self, x, out: GatherOutput, multicast: bool = True) -> None:
+        """x [n, in_dim] f32 on this rank's GPU; fills out.view(n) on every rank
+        once every rank has called it and the barrier has run."""
+        n = x.numel() // self.in_dim
+        if n > out.n_max or out.out_total != self.out_total:
+            raise ValueError("output buffer does not fit this forward")
+        if multicast and out.mc_ptr:
+            self.layer.forward_tp(x, self.out_total, self.row0, out_mc=out.mc_ptr, n=n)
+        else:
+            self.layer.forward_tp(x, self.out_total, self.row0, out_ranks=out.rank_ptrs, n=n)
+
+    def close(self) -> None:
+        self.layer.close()

@@ -122,6 +122,27 @@ OBN_API int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, in
 OBN_API int obn_bitlinear_forward_noalloc(const obn_bitlinear* layer, const float* x, int n,
                                           float* y, void* stream);
 
+/* Tensor-parallel BitLinear::forward (bitlinear.rs:52-97) with the output
+ * features split over `world` ranks (one GPU each) and the result gathered on
+ * every rank, in one kernel per rank: `layer` holds the contiguous row block
+ * [col0, col0 + out_dim) of an out_total-row weight; this call computes the
+ * [n, out_dim] slice and its GEMM epilogue writes it straight into columns
+ * [col0, col0 + out_dim) of the [n, out_total] f32 output that every rank holds:
+ *   y_mc != NULL  a multicast (NVLS) device address bound to every rank's output
+ *                 buffer: one store per element reaches all of them through the
+ *                 NVSwitch;
+ *   y_mc == NULL  y_ranks (host array of `world` device pointers) gives each
+ *                 rank's output buffer as mapped on this device (this rank's own
+ *                 buffer and peer mappings of the others): one store per rank.
+ * Needs n >= 16 (the tensor-core GEMM; OBN_ERR_UNSUPPORTED otherwise) and
+ * world <= 8. Stream-ordered: before reading its output a rank must order
+ * every rank's call before the read (for instance a barrier on the stream).
+ * Numerics are those of obn_bitlinear_forward for the same rows. */
+OBN_API int obn_bitlinear_forward_tp(const obn_bitlinear* layer, const float* x, int n,
+                                     float* y_mc, float* const* y_ranks, int world,
+                                     int out_total, int col0, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
 /* ---- kernel-level entry points (one per reference shader) ------------------ */
 
 /* Fused rmsnorm.wgsl + quantize.wgsl: per token, optional RMSNorm with gamma
