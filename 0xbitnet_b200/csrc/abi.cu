@@ -375,6 +375,10 @@ int obn_bitlinear_forward_tp(const obn_bitlinear* layer, const float* x, int n, 
     }
   else if (!aligned(y_mc, 4))
     return fail(OBN_ERR_INVALID_ARGUMENT, "y_mc is not 4-byte aligned");
+  go.vec4 = out_total % 4 == 0 && col0 % 4 == 0 && layer->out_dim % 4 == 0;
+  if (y_mc) go.vec4 = go.vec4 && aligned(y_mc, 16);
+  else
+    for (int r = 0; r < world; ++r) go.vec4 = go.vec4 && aligned(y_ranks[r], 16);
   auto* base = static_cast<uint8_t*>(workspace);
   auto* q = reinterpret_cast<int8_t*>(base);
   auto* sc = reinterpret_cast<float*>(base + align256(static_cast<size_t>(n) * layer->in_dim));

@@ -190,6 +190,15 @@ enum : int { kOutLocal = 0, kOutMulticast = 1, kOutPeers = 2 };
 OBN_DEVINL void multimem_st_f32(float* addr, float v) {
   asm volatile("multimem.st.global.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }
+OBN_DEVINL void multimem_st_v4(float* addr, float4 v) {
+  asm volatile("multimem.st.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(v.x),
+               "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
+// Epilogue staging of the gather modes: per epilogue warp one [16 tokens][32
+// rows] f32 block, so each thread can store 4 consecutive rows of one token.
+constexpr int kGatherStageBytes = 4 * 16 * 32 * 4;
 
 template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal>
 __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CUtensorMap tmap_q,
@@ -211,6 +220,8 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
   uint8_t* sB = sA + (A_TMEM ? 0 : STAGES * kAStage);  // STAGES x kBStage
   uint8_t* sP = sB + STAGES * kBStage;                 // STAGES x kPStage
   GemmSmem* sm = reinterpret_cast<GemmSmem*>(sP + STAGES * kPStage);
+  float* sE = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(sm + 1) + 15) &
+                                       ~static_cast<uintptr_t>(15));  // gather staging
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int KB = K / kBK;
@@ -437,6 +448,40 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
         const int nl = n0 + (lane & 15);
         const int qs_l = nl < N ? qsum[nl] : 0;
         const float sx_l = (nl < N && !acc_out) ? s_x[nl] : 0.0f;
+        if (OUT != kOutLocal && go.vec4) {
+          // Stage the chunk as [16 tokens][32 rows], then 16-byte stores of 4
+          // consecutive rows (conflict-free: 8 lanes read one token's 128 bytes).
+          float* st = sE + (warp & 3) * (16 * 32);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int qs_j = __shfl_sync(0xffffffffu, qs_l, j);
+            const float sx_j = __shfl_sync(0xffffffffu, sx_l, j);
+            const float fd = static_cast<float>(static_cast<int>(v[j]) - qs_j);
+            st[j * 32 + lane] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx_j)
+                                                    : __fmul_rn(fd, __fmul_rn(sw, sx_j));
+          }
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int i = it * 32 + lane;
+            const int jj = i >> 3, r4 = (i & 7) * 4;
+            const int n = n0 + jj;
+            const int mrow = mt * kBM + quarter * 32 + r4;
+            if (n < N && mrow < M) {
+              const float4 v4 = *reinterpret_cast<const float4*>(st + jj * 32 + r4);
+              const size_t og = static_cast<size_t>(n) * go.ldy + go.col0 + mrow;
+              if constexpr (OUT == kOutMulticast) {
+                multimem_st_v4(go.mc + og, v4);
+              } else {
+#pragma unroll
+                for (int p = 0; p < kMaxGatherRanks; ++p)
+                  if (p < go.world) *reinterpret_cast<float4*>(go.ranks[p] + og) = v4;
+              }
+            }
+          }
+          __syncwarp();
+          continue;
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int n = n0 + j;
@@ -898,12 +943,12 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <int BN, int STAGES, int KSTG, bool A_TMEM>
+template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal>
 size_t gemm_smem_bytes() {
   return 1024 +
          static_cast<size_t>(STAGES) *
              ((A_TMEM ? 0 : KSTG * kBM * kBK) + KSTG * BN * kBK + KSTG * kPackedBlock) +
-         sizeof(GemmSmem);
+         sizeof(GemmSmem) + (OUT == kOutLocal ? 0 : 16 + kGatherStageBytes);
 }
 
 int num_sms() {
@@ -957,7 +1002,7 @@ cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, cons
   CUtensorMap qmap, wmap;
   if (!make_q_map(&qmap, q, n, W.in_dim, BN, KSTG) || !make_w_map(&wmap, W, KSTG))
     return cudaErrorInvalidValue;
-  const size_t smem = gemm_smem_bytes<BN, STAGES, KSTG, A_TMEM>();
+  const size_t smem = gemm_smem_bytes<BN, STAGES, KSTG, A_TMEM, OUT>();
   auto kern = k_gemm<BN, STAGES, KSTG, A_TMEM, OUT>;
   static int configured[64] = {0};
   int dev = 0;

@@ -23,6 +23,7 @@ struct GatherOut {
   int world = 0;
   int ldy = 0;
   int col0 = 0;
+  int vec4 = 0;  // ldy, col0, out_dim multiples of 4 and every base 16-byte aligned
 };
 
 // True when launch_gemm handles this shape (otherwise the dp4a path runs).

@@ -55,6 +55,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--prefill", type=str, default="512,2048,8192",
                    help="config-2 token counts for the prefill TOPS block ('' to skip)")
+    p.add_argument("--tp-tokens", type=int, default=16384,
+                   help="config-4 tensor-parallel prefill tokens when run on N > 1 GPUs (0 skips)")
     p.add_argument("--case", type=str, default=None,
                    help="SHAPE:B — run a few forwards of one 2B shape (or of 'all' five in "
                         "turn) at B tokens and exit (a small, self-contained workload for ncu "
@@ -319,6 +321,116 @@ def measure_prefill(args, obn, synth, dev, stream):
     return out
 
 
+def measure_tp_prefill(args, obn, synth, dev, stream, world, rank):
+    """Config 4 on N > 1 GPUs: the 3B-class shapes (hidden 3072, FFN 9216; QKV
+    assumed MHA 9216x3072), --tp-tokens prefill tokens, one layer of 5 BitLinears,
+    output features split over the ranks and gathered on every rank. Two forms:
+    "fused" = obn_bitlinear_forward_tp (each GEMM epilogue stores its columns into
+    every rank's output, NVLS multicast when the group has it, else peer stores)
+    + one stream barrier; "nccl" = the same row-slice GEMM into a local buffer,
+    NCCL all_gather_into_tensor, re-layout to [tokens, out] on every rank. Whole-job
+    TOPS = sum 2*T*M*K / device time (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    tp = importlib.import_module("0xbitnet_b200.tp")
+    T = args.tp_tokens
+    shp = list(synth.SHAPES_3B.items())
+    parts, outs, xs, locs, gath = [], [], [], [], []
+    for i, (name, (M, K)) in enumerate(shp):
+        L = synth.layer(30_000 + i, M, K)  # seeded: identical on every rank
+        parts.append(tp.TPBitLinear(L.blob(), K, M, world, rank, norm_weight=L.gamma,
+                                    device=dev.index))
+        outs.append(tp.GatherOutput(T, M, device=dev))
+        g = torch.Generator(device=dev)
+        g.manual_seed(31_000 + i)
+        xs.append(torch.randn(T, K, generator=g, device=dev))
+        locs.append(torch.empty(T, M // world, device=dev))
+        gath.append(torch.empty(world, T, M // world, device=dev))
+    ops = sum(2.0 * T * M * K for _, (M, K) in shp)
+    has_mc = bool(outs[0].mc_ptr)
+
+    def fused(mc=False):
+        for i in range(len(shp)):
+            parts[i].forward(xs[i], outs[i], multicast=mc)
+        outs[-1].barrier()  # one stream barrier after all five gathered GEMMs
+
+    def local():
+        for i in range(len(shp)):
+            parts[i].layer.forward(xs[i], out=locs[i])
+
+    def nccl():
+        for i, (name, (M, K)) in enumerate(shp):
+            parts[i].layer.forward(xs[i], out=locs[i])
+            dist.all_gather_into_tensor(gath[i], locs[i])
+            outs[i].view(T).view(T, world, M // world).copy_(gath[i].permute(1, 0, 2))
+
+    def timed(fn, reps=3):
+        with torch.cuda.stream(stream):
+            fn()
+            stream.synchronize()
+            dist.barrier()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                fn()
+            e1.record(stream)
+            stream.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # parity: the gathered output equals the NCCL all-gather of the same slices
+    with torch.cuda.stream(stream):
+        nccl()
+        stream.synchronize()
+        ref = [o.view(T).clone() for o in outs]
+        for o in outs:
+            o.view(T).fill_(float("nan"))
+        outs[-1].barrier()
+        fused(has_mc)
+        stream.synchronize()
+    same = all(torch.equal(o.view(T), r) for o, r in zip(outs, ref))
+    if has_mc:  # and the peer-store form
+        with torch.cuda.stream(stream):
+            for o in outs:
+                o.view(T).fill_(float("nan"))
+            outs[-1].barrier()
+            fused(False)
+            stream.synchronize()
+        same = same and all(torch.equal(o.view(T), r) for o, r in zip(outs, ref))
+    flag = torch.tensor([1 if same else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    del ref
+    peers_ms = timed(lambda: fused(False))
+    mc_ms = timed(lambda: fused(True)) if has_mc else None
+    fused_ms = min(peers_ms, mc_ms) if mc_ms is not None else peers_ms
+    nccl_ms = timed(nccl)
+    local_ms = timed(local)
+    # NVLink bound: every rank must receive (world-1)/world of each f32 output
+    ingress = sum(T * M * 4 * (world - 1) / world for _, (M, K) in shp)
+    out = {
+        "workload": "config 4: 3B-class shapes (hidden 3072, FFN 9216, QKV assumed MHA "
+                    "9216x3072), %d tokens, 1 layer x 5 BitLinears, output features split "
+                    "over %d GPUs and gathered on every rank" % (T, world),
+        "tokens": T, "world": world,
+        "fused_form": "NVLS multicast stores" if fused_ms == mc_ms else "peer stores over NVLink",
+        "fused_ms": fused_ms, "fused_tops": ops / (fused_ms / 1e3) / 1e12,
+        "fused_peer_stores_ms": peers_ms, "fused_multicast_ms": mc_ms,
+        "nccl_allgather_ms": nccl_ms, "nccl_allgather_tops": ops / (nccl_ms / 1e3) / 1e12,
+        "local_gemm_ms": local_ms,
+        "nvlink_ingress_bytes_per_gpu": ingress,
+        "nvlink_bound_ms": ingress / 770e9 * 1e3,
+        "parity_bitexact_vs_nccl": bool(flag.item()),
+    }
+    for p_ in parts:
+        p_.close()
+    del outs, xs, locs, gath
+    torch.cuda.synchronize()
+    dist.barrier()
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -539,6 +651,9 @@ def run_ours(args):
                     "avg_launch_us": k["us"], "bytes_per_launch_avg": k["bytes"], "traffic": tr}
 
     prefill = measure_prefill(args, obn, synth, dev, stream) if args.prefill else None
+    tp_prefill = None
+    if world > 1 and args.tp_tokens > 0:
+        tp_prefill = measure_tp_prefill(args, obn, synth, dev, stream, world, rank)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -562,6 +677,7 @@ def run_ours(args):
             "roofline": roofline,
             "rooflines_per_batch": rooflines,
             "prefill": prefill,
+            "tp_prefill": tp_prefill,
             "cpu_baseline": cpu,
             "clocks": clock_info,
             "e2e": {"value": e2e_value, "unit": "GB/s",
