@@ -37,6 +37,7 @@ SIGNATURES = {
     "obn_bitlinear_forward": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "obn_bitlinear_forward_noalloc": (_I, [_P, _P, _I, _P, _P]),
     "obn_bitlinear_forward_tp": (_I, [_P, _P, _I, _P, _P, _I, _I, _I, _P, _SZ, _P]),
+    "obn_lm_head_f16": (_I, [_P, _I, _I, _P, _P, _F, _I, _P, _P]),
     "obn_rmsnorm_quantize": (_I, [_P, _P, _F, _I, _I, _P, _P, _P, _P]),
     "obn_rmsnorm": (_I, [_P, _P, _F, _I, _I, _P, _P]),
     "obn_ternary_matmul": (_I, [_P, _P, _P, _P, _I, _P, _P]),

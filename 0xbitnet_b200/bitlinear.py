@@ -206,6 +206,24 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5) -> torch.T
     return y
 
 
+def lm_head_f16(embed: torch.Tensor, x: torch.Tensor, norm_weight: torch.Tensor | None = None,
+                eps: float = 1e-5) -> torch.Tensor:
+    """The f16 LM head behind the final RMSNorm (model.rs:226-262; f32_matmul.wgsl):
+    embed [vocab, dim] float16 and x [n, dim] f32 on one CUDA device ->
+    logits [n, vocab] f32."""
+    if not (embed.is_cuda and embed.dtype == torch.float16 and embed.is_contiguous()):
+        raise TypeError("embed must be a contiguous float16 CUDA tensor")
+    _require_cuda_f32(x, "x")
+    if norm_weight is not None:
+        _require_cuda_f32(norm_weight, "norm_weight")
+    vocab, dim = embed.shape
+    n = x.numel() // dim
+    logits = torch.empty((n, vocab), dtype=torch.float32, device=x.device)
+    check(lib().obn_lm_head_f16(_ptr(embed), vocab, dim, _ptr(x), _ptr(norm_weight),
+                                ctypes.c_float(eps), n, _ptr(logits), _stream(x.device)))
+    return logits
+
+
 def check_device_errors() -> None:
     """Raises ObnError if a bounded in-kernel wait gave up since the last check."""
     check(lib().obn_check_device_errors())

@@ -14,6 +14,7 @@
 #include "gemm.h"
 #include "kernels.h"
 #include "layout.cuh"
+#include "lmhead.h"
 
 struct obn_bitlinear {
   int device = 0;
@@ -389,6 +390,28 @@ int obn_bitlinear_forward_tp(const obn_bitlinear* layer, const float* x, int n, 
   if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
   e = obn::launch_gemm_gather(view(layer), q, sc, qs, n, obn::kOrderGemm, go, s);
   if (e != cudaSuccess) return cuda_fail(e, "gathered ternary GEMM launch");
+  return OBN_OK;
+}
+
+int obn_lm_head_f16(const void* embed, int vocab, int dim, const float* x,
+                    const float* norm_weight, float eps, int n, float* logits, void* stream) {
+  clear_error();
+  if (!embed || !x || !logits) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (vocab <= 0 || dim <= 0 || n <= 0)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "need vocab, dim and n > 0 (got %d, %d, %d)", vocab,
+                dim, n);
+  if (dim % 8 != 0 || dim > 14336)
+    return fail(OBN_ERR_UNSUPPORTED, "dim must be a multiple of 8 and at most 14336 (got %d)",
+                dim);
+  if (!aligned(embed, 16) || !aligned(x, 16) || (norm_weight && !aligned(norm_weight, 4)) ||
+      !aligned(logits, 4))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "embed and x must be 16-byte aligned");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (int rc = check_device(dev)) return rc;
+  cudaError_t e = obn::launch_lm_head_f16(embed, vocab, dim, x, norm_weight, eps, n, logits,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "lm head launch");
   return OBN_OK;
 }
 

@@ -77,30 +77,6 @@ __global__ void k_export(const uint8_t* __restrict__ t, uint8_t* __restrict__ ro
 
 // ---------------------------------------------------------------------------
 // Block reductions for 256 threads
-// ---------------------------------------------------------------------------
-// The exact tree of rmsnorm.wgsl:47-55: partial[tid] += partial[tid + stride]
-// for stride = 128 .. 1. Strides 128 and 64 go through shared memory, 32 .. 1
-// through shuffles (lane l adds lane l + stride: the same pairing).
-OBN_DEVINL float tree_sum_256(float v, float* sh) {
-  const int tid = threadIdx.x;
-  sh[tid] = v;
-  __syncthreads();
-  if (tid < 128) sh[tid] = __fadd_rn(sh[tid], sh[tid + 128]);
-  __syncthreads();
-  if (tid < 64) sh[tid] = __fadd_rn(sh[tid], sh[tid + 64]);
-  __syncthreads();
-  if (tid < 32) {
-    float a = __fadd_rn(sh[tid], sh[tid + 32]);
-#pragma unroll
-    for (int s = 16; s >= 1; s >>= 1) a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, s));
-    if (tid == 0) sh[0] = a;
-  }
-  __syncthreads();
-  const float r = sh[0];
-  __syncthreads();
-  return r;
-}
-
 // Max is order-independent: any reduction order gives the shader's result.
 OBN_DEVINL float block_max_256(float v, float* sh) {
 #pragma unroll

@@ -143,6 +143,19 @@ OBN_API int obn_bitlinear_forward_tp(const obn_bitlinear* layer, const float* x,
                                      int out_total, int col0, void* workspace,
                                      size_t workspace_bytes, void* stream);
 
+/* The f16 LM head behind the final RMSNorm: dispatch_final_norm + dispatch_lm_head_with
+ * (model.rs:226-262, 393-430) running rmsnorm.wgsl then f32_matmul.wgsl:27-74 (tied
+ * embedding or separate f16 head): logits[t, v] = sum_d y[t, d] * f32(embed[v, d]) for
+ * t < n, v < vocab, with y = RMSNorm(x[t]) * norm_weight (norm_weight NULL: y = x[t]).
+ * embed: [vocab, dim] IEEE binary16, row-major, 16-byte aligned; dim % 8 == 0 and
+ * dim <= 14336. x: [n, dim] f32 (16-byte aligned); logits: [n, vocab] f32. Every logit is
+ * the shader's: 256 lane partials over d-pairs, then its halving tree, in f32. The
+ * reference calls it with the last token only (n = 1); n > 1 streams the table once per
+ * 4 tokens. Stream-ordered, no workspace. */
+OBN_API int obn_lm_head_f16(const void* embed, int vocab, int dim, const float* x,
+                            const float* norm_weight, float eps, int n, float* logits,
+                            void* stream);
+
 /* ---- kernel-level entry points (one per reference shader) ------------------ */
 
 /* Fused rmsnorm.wgsl + quantize.wgsl: per token, optional RMSNorm with gamma

@@ -25,6 +25,7 @@ _f32p = ctypes.POINTER(ctypes.c_float)
 _i8p = ctypes.POINTER(ctypes.c_int8)
 _u8p = ctypes.POINTER(ctypes.c_uint8)
 _i32p = ctypes.POINTER(ctypes.c_int32)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
 
 
 def build() -> str:
@@ -44,6 +45,8 @@ def lib() -> ctypes.CDLL:
         L.orc_mulberry32_next.restype = ctypes.c_double
         L.orc_i2s_pack_row.restype = ctypes.c_size_t
         L.orc_max_threads.restype = ctypes.c_int
+        L.orc_half_to_float.restype = ctypes.c_float
+        L.orc_half_to_float.argtypes = [ctypes.c_uint16]
         _lib = L
     return _lib
 
@@ -190,3 +193,34 @@ def bitlinear_omp(x, w_i2s, s_w, M: int, K: int, norm_w=None, eps: float = 1e-5,
 
 def max_threads() -> int:
     return int(lib().orc_max_threads())
+
+
+# ---- LM head (f32_matmul.wgsl:27-74; final RMSNorm: rmsnorm.wgsl) ----------
+def half_to_float(bits: int) -> float:
+    """binary16 bit pattern -> float32 (unpack2x16float), one value."""
+    return float(lib().orc_half_to_float(bits & 0xFFFF))
+
+
+def lm_head_f16(hidden: np.ndarray, embed: np.ndarray, norm_w: np.ndarray | None = None,
+                eps: float = 1e-5) -> np.ndarray:
+    """logits [N, V] = RMSNorm(hidden) (when norm_w is given) times the f16
+    embedding [V, D], in the shader's per-lane order and halving tree."""
+    h = np.ascontiguousarray(hidden, np.float32)
+    D = h.shape[-1]
+    h = h.reshape(-1, D)
+    if norm_w is not None:
+        h = rmsnorm(h, norm_w, eps)
+    e = np.ascontiguousarray(embed, np.float16).view(np.uint16)
+    V = e.shape[0]
+    out = np.empty((h.shape[0], V), np.float32)
+    lib().orc_lm_head_f16(_p(h, _f32p), _p(e, _u16p), h.shape[0], V, D, _p(out, _f32p))
+    return out
+
+
+def f32_matmul_seq(hidden: np.ndarray, embed: np.ndarray, N: int, V: int, D: int) -> np.ndarray:
+    """reference.ts:342-360 refF32Matmul: sequential f32 sum per (n, v)."""
+    h = np.ascontiguousarray(hidden, np.float32)
+    e = np.ascontiguousarray(embed, np.float32)
+    out = np.empty(N * V, np.float32)
+    lib().orc_f32_matmul_seq(_p(h, _f32p), _p(e, _f32p), N, V, D, _p(out, _f32p))
+    return out

@@ -218,6 +218,69 @@ void orc_bitlinear(const float* x, int n, const float* norm_w, float eps,
   free(normed);
 }
 
+/* ---- LM head (packages/core/src/shaders/f32_matmul.wgsl:27-74) ---------- */
+/* IEEE binary16 -> binary32, exact (unpack2x16float). */
+float orc_half_to_float(uint16_t h) {
+  uint32_t sign = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 0x1Fu, m = h & 0x3FFu, bits;
+  if (e == 0x1Fu) {
+    bits = sign | 0x7F800000u | (m << 13);            /* inf / nan */
+  } else if (e != 0) {
+    bits = sign | ((e + 112u) << 23) | (m << 13);     /* normal: rebias 15 -> 127 */
+  } else if (m == 0) {
+    bits = sign;                                      /* signed zero */
+  } else {                                            /* subnormal: normalise */
+    int shift = 0;
+    while (!(m & 0x400u)) { m <<= 1; ++shift; }
+    bits = sign | ((uint32_t)(113 - shift) << 23) | ((m & 0x3FFu) << 13);
+  }
+  float f;
+  memcpy(&f, &bits, sizeof f);
+  return f;
+}
+
+/* logits[n, v] = sum_d hidden[n, d] * f32(embed[v, d]), the shader's order: lane
+ * tid of 256 accumulates the d-pairs dh = tid, tid + 256, ... (two products per
+ * pair, :51-57), then the halving tree (:63-68). embed [V, D] binary16. */
+void orc_lm_head_f16(const float* hidden, const uint16_t* embed, int N, int V, int D,
+                     float* out) {
+  float part[ORC_LANES];
+  const int dh_n = D / 2;
+  for (int n = 0; n < N; ++n) {
+    const float* h = hidden + (size_t)n * D;
+    for (int v = 0; v < V; ++v) {
+      const uint16_t* e = embed + (size_t)v * D;
+      for (int tid = 0; tid < ORC_LANES; ++tid) {
+        float acc = 0.0f;
+        for (int dh = tid; dh < dh_n; dh += ORC_LANES) {
+          const int d = dh * 2;
+          float t0 = h[d] * orc_half_to_float(e[d]);
+          acc = acc + t0;
+          float t1 = h[d + 1] * orc_half_to_float(e[d + 1]);
+          acc = acc + t1;
+        }
+        part[tid] = acc;
+      }
+      for (int stride = ORC_LANES / 2; stride > 0; stride >>= 1)
+        for (int tid = 0; tid < stride; ++tid) part[tid] = part[tid] + part[tid + stride];
+      out[(size_t)n * V + v] = part[0];
+    }
+  }
+}
+
+/* The TS test helper refF32Matmul (helpers/reference.ts:342-360): one
+ * sequential sum over d with an f32 embedding. */
+void orc_f32_matmul_seq(const float* hidden, const float* embed, int N, int V, int D, float* out) {
+  for (int n = 0; n < N; ++n)
+    for (int v = 0; v < V; ++v) {
+      float sum = 0.0f;
+      for (int d = 0; d < D; ++d) {
+        float t = hidden[(size_t)n * D + d] * embed[(size_t)v * D + d];
+        sum = sum + t;
+      }
+      out[(size_t)n * V + v] = sum;
+    }
+}
+
 int orc_max_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();

@@ -363,3 +363,70 @@ def test_bitlinear_omp_identical():
         x = orc.randf32(n * K, 11 + n).reshape(n, K)
         ref, _, _ = orc.bitlinear(x, packed, s_w, M, K, norm_w=g)
         assert np.array_equal(orc.bitlinear_omp(x, packed, s_w, M, K, norm_w=g, threads=4), ref)
+
+
+# ---- LM head: f32-matmul.test.ts (refF32Matmul) and the f16 shader order ----
+# packages/core/src/shaders/__tests__/f32-matmul.test.ts
+
+
+def test_f32_matmul_simple_dot_products():  # :6-21
+    out = orc.f32_matmul_seq(np.array([1, 2, 3], np.float32),
+                             np.array([1, 0, 0, 0, 1, 0], np.float32), 1, 2, 3)
+    assert out.tolist() == [1.0, 2.0]
+
+
+def test_f32_matmul_layout_and_tokens():  # :23-54
+    assert orc.f32_matmul_seq(orc.randf32(8, 1), orc.randf32(12, 2), 2, 3, 4).shape == (6,)
+    out = orc.f32_matmul_seq(np.array([1, 0, 0, 1, 1, 1], np.float32),
+                             np.array([1, 0, 0, 1], np.float32), 3, 2, 2)
+    assert out.tolist() == [1, 0, 0, 1, 1, 1]
+
+
+def test_f32_matmul_zero_hidden():  # :56-68
+    out = orc.f32_matmul_seq(np.zeros(4, np.float32), orc.randf32(20, 3), 1, 5, 4)
+    assert np.all(out == 0)
+
+
+def test_f32_matmul_manual_dot():  # :70-89
+    h, e = orc.randf32(16, 10), orc.randf32(24, 20)
+    out = orc.f32_matmul_seq(h, e, 2, 3, 8)
+    want = (h.reshape(2, 8).astype(np.float64) @ e.reshape(3, 8).astype(np.float64).T).ravel()
+    np.testing.assert_allclose(out, want, rtol=1e-5, atol=1e-6)
+
+
+def test_lm_head_f16_shader_order_agrees_with_helper():
+    # the shader (f16 table, 256-lane partials + tree) against the TS helper
+    # (one sequential sum) on a table exactly representable in f16
+    N, V, D = 2, 7, 2560
+    h = orc.randf32(N * D, 5).reshape(N, D)
+    e16 = orc.randf32(V * D, 6).astype(np.float16).reshape(V, D)
+    out = orc.lm_head_f16(h, e16)
+    seq = orc.f32_matmul_seq(h, e16.astype(np.float32), N, V, D).reshape(N, V)
+    e64 = e16.astype(np.float64)
+    exact = h.astype(np.float64) @ e64.T
+    l1 = np.abs(h.astype(np.float64)) @ np.abs(e64).T
+    # both orders stay within f32 summation error of the exact dot product
+    # (about 20 roundings for the 256-lane tree, D for the sequential sum)
+    assert np.all(np.abs(out - exact) <= 4e-6 * l1)
+    assert np.all(np.abs(seq - exact) <= D * 6e-8 * l1)
+    # identity rows pick single hidden entries exactly
+    eye = np.zeros((3, D), np.float16)
+    eye[0, 0] = eye[1, 1] = eye[2, D - 1] = 1
+    assert orc.lm_head_f16(h[:1], eye).tolist() == [[h[0, 0], h[0, 1], h[0, D - 1]]]
+    assert np.all(orc.lm_head_f16(np.zeros((1, D), np.float32), e16) == 0)
+
+
+def test_lm_head_f16_with_final_norm():
+    D = 256
+    x = orc.randf32(D, 7).reshape(1, D)
+    g = (1 + 0.1 * orc.randf32(D, 8)).astype(np.float32)
+    e16 = orc.randf32(3 * D, 9).astype(np.float16).reshape(3, D)
+    assert np.array_equal(orc.lm_head_f16(x, e16, g, 1e-5),
+                          orc.lm_head_f16(orc.rmsnorm(x, g, 1e-5), e16))
+
+
+def test_half_to_float_exact():
+    bits = np.arange(0, 65536, 7, dtype=np.uint16)
+    finite = bits[np.isfinite(bits.view(np.float16))]
+    got = np.array([orc.half_to_float(int(b)) for b in finite], np.float32)
+    assert np.array_equal(got, finite.view(np.float16).astype(np.float32))
