@@ -431,6 +431,40 @@ def measure_tp_prefill(args, obn, synth, dev, stream, world, rank):
     return out
 
 
+def measure_lm_head(obn, dev, stream, peak):
+    """Next-row kernel: the f16 LM head of BitNet-2B (128256 x 2560, 656.7 MB) behind
+    the final RMSNorm, one token as the reference runs it; the table exceeds L2, so
+    every launch streams it from HBM. Bytes per launch = V*D*2 + D*4 (x) + D*4
+    (gamma) + V*4 (logits)."""
+    import torch
+    V, D = 128256, 2560
+    g = torch.Generator(device=dev)
+    g.manual_seed(40_000)
+    embed = (torch.randn(V, D, generator=g, device=dev) * 0.05).to(torch.float16)
+    x = torch.randn(1, D, generator=g, device=dev)
+    gamma = 1 + 0.1 * torch.randn(D, generator=g, device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            obn.lm_head_f16(embed, x, gamma)
+        stream.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        reps = 20
+        e0.record(stream)
+        for _ in range(reps):
+            obn.lm_head_f16(embed, x, gamma)
+        e1.record(stream)
+        stream.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    nbytes = V * D * 2 + D * 8 + V * 4
+    ach = nbytes / (us * 1e-6) / 1e9
+    del embed
+    return {"kernel": "k_lm_head_f16<1> (final RMSNorm + f16 LM head GEMV, 1 token)",
+            "shape": [V, D], "bytes_per_launch": nbytes, "avg_launch_us": us,
+            "achieved_gbs": ach, "peak_gbs": peak, "frac": ach / peak,
+            "tokens_per_s": 1e6 / us}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -651,6 +685,7 @@ def run_ours(args):
                     "avg_launch_us": k["us"], "bytes_per_launch_avg": k["bytes"], "traffic": tr}
 
     prefill = measure_prefill(args, obn, synth, dev, stream) if args.prefill else None
+    lm_head = measure_lm_head(obn, dev, stream, peak)
     tp_prefill = None
     if world > 1 and args.tp_tokens > 0:
         tp_prefill = measure_tp_prefill(args, obn, synth, dev, stream, world, rank)
@@ -678,6 +713,7 @@ def run_ours(args):
             "rooflines_per_batch": rooflines,
             "prefill": prefill,
             "tp_prefill": tp_prefill,
+            "lm_head": lm_head,
             "cpu_baseline": cpu,
             "clocks": clock_info,
             "e2e": {"value": e2e_value, "unit": "GB/s",
