@@ -33,6 +33,8 @@ SIGNATURES = {
     "obn_bitlinear_free": (None, [_P]),
     "obn_bitlinear_in_dim": (_I, [_P]),
     "obn_bitlinear_out_dim": (_I, [_P]),
+    "obn_bitlinear_rows": (_I, [_P]),
+    "obn_bitlinear_load_i2s_gated": (_I, [_P, _SZ, _P, _SZ, _I, _I, _P, _F, _I, ctypes.POINTER(_P)]),
     "obn_bitlinear_workspace_bytes": (_SZ, [_P, _I]),
     "obn_bitlinear_forward": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "obn_bitlinear_forward_noalloc": (_I, [_P, _P, _I, _P, _P]),

@@ -81,10 +81,31 @@ class BitLinear:
         self._init(handle, in_dim, out_dim)
         return self
 
+    @classmethod
+    def from_i2s_gated(cls, gate: bytes | np.ndarray, up: bytes | np.ndarray, in_dim: int,
+                       out_dim: int, norm_weight: np.ndarray | None = None, eps: float = 1e-5,
+                       device: int = 0) -> "BitLinear":
+        """The gated FFN's gate and up projections (two GGUF I2_S tensors) as one
+        layer whose forward is relu(x W_gate^T)^2 * (x W_up^T) (ffn.rs:70-79)."""
+        bufs = [np.frombuffer(t, np.uint8) if isinstance(t, (bytes, bytearray))
+                else np.ascontiguousarray(t, np.uint8).reshape(-1) for t in (gate, up)]
+        nw = None if norm_weight is None else np.ascontiguousarray(norm_weight, np.float32)
+        handle = ctypes.c_void_p()
+        check(lib().obn_bitlinear_load_i2s_gated(
+            bufs[0].ctypes.data_as(ctypes.c_void_p), bufs[0].size,
+            bufs[1].ctypes.data_as(ctypes.c_void_p), bufs[1].size, in_dim, out_dim,
+            None if nw is None else nw.ctypes.data_as(ctypes.c_void_p),
+            ctypes.c_float(eps), device, ctypes.byref(handle)))
+        self = cls.__new__(cls)
+        self.device = torch.device("cuda", device)
+        self._init(handle, in_dim, out_dim)
+        return self
+
     def _init(self, handle: ctypes.c_void_p, in_dim: int, out_dim: int) -> None:
         self._h = handle
         self.in_dim = in_dim
         self.out_dim = out_dim
+        self.rows = int(lib().obn_bitlinear_rows(handle))  # 2 * out_dim when gated
         self._ws: dict[int, torch.Tensor] = {}
 
     @property
@@ -148,7 +169,7 @@ class BitLinear:
                n: int | None = None) -> torch.Tensor:
         """Ternary GEMV/GEMM on already-quantized activations (int8 [n, in_dim])."""
         n = q.shape[0] if n is None else n
-        out = torch.empty((n, self.out_dim), dtype=torch.float32, device=self.device)
+        out = torch.empty((n, self.rows), dtype=torch.float32, device=self.device)
         check(lib().obn_ternary_matmul(self._h, _ptr(q), _ptr(scales), _ptr(qsum), n,
                                        _ptr(out), _stream(self.device)))
         return out
@@ -156,14 +177,14 @@ class BitLinear:
     def acc(self, q: torch.Tensor, qsum: torch.Tensor) -> torch.Tensor:
         """Exact int32 accumulators sum_k w[m,k] q[t,k] -> [n, out_dim]."""
         n = q.shape[0]
-        out = torch.empty((n, self.out_dim), dtype=torch.int32, device=self.device)
+        out = torch.empty((n, self.rows), dtype=torch.int32, device=self.device)
         check(lib().obn_ternary_acc(self._h, _ptr(q), _ptr(qsum), n, _ptr(out),
                                     _stream(self.device)))
         return out
 
     def export_i2s(self) -> torch.Tensor:
         """Device weights back in I2_S rows [out_dim, in_dim/4] (uint8)."""
-        out = torch.empty((self.out_dim, self.in_dim // 4), dtype=torch.uint8, device=self.device)
+        out = torch.empty((self.rows, self.in_dim // 4), dtype=torch.uint8, device=self.device)
         check(lib().obn_bitlinear_export_i2s(self._h, _ptr(out), _stream(self.device)))
         return out
 

@@ -19,7 +19,9 @@
 struct obn_bitlinear {
   int device = 0;
   int in_dim = 0;   // K
-  int out_dim = 0;  // M
+  int out_dim = 0;  // output features of the forward
+  int rows = 0;     // weight rows the matmul computes (2 * out_dim when gated)
+  int gated = 0;    // merged gate|up FFN projection: forward = relu(gate)^2 * up
   int m_pad = 0;
   float eps = 1e-5f;
   uint8_t* w = nullptr;     // T16 layout, m_pad * K / 4 bytes
@@ -81,7 +83,7 @@ int check_dims(int in_dim, int out_dim) {
 }
 
 obn::WeightView view(const obn_bitlinear* L) {
-  return obn::WeightView{L->w, L->s_w, L->in_dim, L->out_dim, L->m_pad};
+  return obn::WeightView{L->w, L->s_w, L->in_dim, L->rows, L->m_pad};
 }
 
 void free_layer(obn_bitlinear* L) {
@@ -103,6 +105,7 @@ int alloc_layer(int in_dim, int out_dim, float eps, obn_bitlinear** out) {
   cudaGetDevice(&L->device);
   L->in_dim = in_dim;
   L->out_dim = out_dim;
+  L->rows = out_dim;
   L->m_pad = obn::round_up(out_dim, obn::kTileRows);
   L->eps = eps;
   const size_t wbytes = static_cast<size_t>(L->m_pad) * in_dim / 4;
@@ -194,6 +197,73 @@ int obn_bitlinear_load_i2s(const uint8_t* i2s_tensor, size_t nbytes, int in_dim,
   return OBN_OK;
 }
 
+int obn_bitlinear_load_i2s_gated(const uint8_t* gate_i2s, size_t gate_bytes,
+                                 const uint8_t* up_i2s, size_t up_bytes, int in_dim, int out_dim,
+                                 const float* norm_weight, float eps, int device,
+                                 obn_bitlinear** out_layer) {
+  clear_error();
+  if (!gate_i2s || !up_i2s || !out_layer)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  *out_layer = nullptr;
+  if (int rc = check_dims(in_dim, out_dim)) return rc;
+  if (out_dim > (1 << 29)) return fail(OBN_ERR_INVALID_ARGUMENT, "out_dim %d too large", out_dim);
+  const size_t row_bytes = static_cast<size_t>(in_dim) / 4;
+  const size_t packed = static_cast<size_t>(out_dim) * row_bytes;
+  if (gate_bytes < packed + 32 || up_bytes < packed + 32)
+    return fail(OBN_ERR_INVALID_ARGUMENT,
+                "each I2_S tensor of %dx%d needs %zu bytes (packed + 32-byte scale), got %zu and "
+                "%zu",
+                out_dim, in_dim, packed + 32, gate_bytes, up_bytes);
+  if (int rc = check_device(device)) return rc;
+  DeviceGuard g(device);
+  float gscale, uscale;  // loader.rs:129-131
+  std::memcpy(&gscale, gate_i2s + packed, sizeof(float));
+  std::memcpy(&uscale, up_i2s + packed, sizeof(float));
+  const int rows = 2 * out_dim;
+  obn_bitlinear* L = nullptr;
+  if (int rc = alloc_layer(in_dim, rows, eps, &L)) return rc;
+  L->out_dim = out_dim;
+  L->gated = 1;
+  // Row 2i = gate row i, row 2i + 1 = up row i: a gate row and its up row always
+  // share a tile, a subtile and a split-K owner range.
+  std::vector<uint8_t> merged(2 * packed);
+  for (int i = 0; i < out_dim; ++i) {
+    std::memcpy(&merged[(2 * static_cast<size_t>(i)) * row_bytes], gate_i2s + i * row_bytes,
+                row_bytes);
+    std::memcpy(&merged[(2 * static_cast<size_t>(i) + 1) * row_bytes], up_i2s + i * row_bytes,
+                row_bytes);
+  }
+  std::vector<float> table(L->m_pad, 0.0f);
+  for (int i = 0; i < out_dim; ++i) {
+    table[2 * i] = gscale;
+    table[2 * i + 1] = uscale;
+  }
+  uint8_t* staging = nullptr;
+  cudaError_t e = cudaMalloc(&staging, merged.size());
+  if (e != cudaSuccess) {
+    free_layer(L);
+    cudaGetLastError();
+    return fail(OBN_ERR_OUT_OF_MEMORY, "cudaMalloc of %zu staging bytes failed", merged.size());
+  }
+  e = cudaMemcpy(staging, merged.data(), merged.size(), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = obn::launch_repack_i2s(staging, L->w, rows, in_dim, L->m_pad, 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(L->s_w, table.data(), sizeof(float) * L->m_pad, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && norm_weight) {
+    e = cudaMalloc(&L->norm, sizeof(float) * in_dim);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(L->norm, norm_weight, sizeof(float) * in_dim, cudaMemcpyHostToDevice);
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(staging);
+  if (e != cudaSuccess) {
+    free_layer(L);
+    return cuda_fail(e, "loading gated I2_S tensors");
+  }
+  *out_layer = L;
+  return OBN_OK;
+}
+
 int obn_bitlinear_create(const void* packed_dev, const float* scales_dev, const float* norm_dev,
                          float eps, int in_dim, int out_dim, void* stream,
                          obn_bitlinear** out_layer) {
@@ -232,10 +302,13 @@ void obn_bitlinear_free(obn_bitlinear* layer) { free_layer(layer); }
 
 int obn_bitlinear_in_dim(const obn_bitlinear* layer) { return layer ? layer->in_dim : 0; }
 int obn_bitlinear_out_dim(const obn_bitlinear* layer) { return layer ? layer->out_dim : 0; }
+int obn_bitlinear_rows(const obn_bitlinear* layer) { return layer ? layer->rows : 0; }
 
 size_t obn_bitlinear_workspace_bytes(const obn_bitlinear* layer, int n) {
   if (!layer || n <= 0) return 0;
-  return align256(static_cast<size_t>(n) * layer->in_dim) + 2 * align256(sizeof(float) * n);
+  const size_t pre = layer->gated ? align256(sizeof(float) * n * static_cast<size_t>(layer->rows))
+                                  : 0;  // interleaved gate|up outputs before the activation
+  return align256(static_cast<size_t>(n) * layer->in_dim) + 2 * align256(sizeof(float) * n) + pre;
 }
 
 int obn_ternary_matmul(const obn_bitlinear* layer, const int8_t* q, const float* scales,
@@ -319,23 +392,32 @@ int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, int n, flo
   auto* q = reinterpret_cast<int8_t*>(base);
   auto* sc = reinterpret_cast<float*>(base + align256(static_cast<size_t>(n) * layer->in_dim));
   auto* qs = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(sc) + align256(sizeof(float) * n));
+  // Gated layers: the matmul writes the interleaved [n, 2*out_dim] gate|up outputs
+  // here, and relu(gate)^2 * up goes to y.
+  float* ym = layer->gated ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(qs) +
+                                                      align256(sizeof(float) * n))
+                           : y;
   auto s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (n == 1 && layer->in_dim <= obn::kGemvMaxK) {  // whole BitLinear in one kernel
-    e = obn::launch_bitlinear_n1(view(layer), layer->norm, layer->eps, x, y, s);
+    e = obn::launch_bitlinear_n1(view(layer), layer->norm, layer->eps, x, ym, s);
     if (e != cudaSuccess) return cuda_fail(e, "bitlinear (n=1) launch");
-    return OBN_OK;
+  } else {
+    e = obn::launch_rmsnorm_quant(x, layer->norm, layer->eps, n, layer->in_dim, q, sc, qs, s);
+    if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
+    const int order = n == 1 ? obn::kOrderGemv : obn::kOrderGemm;  // bitlinear.rs:90-94
+    if (obn::gemm_supported(view(layer), n))
+      e = obn::launch_gemm(view(layer), q, sc, qs, n, ym, nullptr, order, s);
+    else if (layer->in_dim <= obn::kGemvMaxK)
+      e = obn::launch_gemv(view(layer), q, sc, qs, n, ym, nullptr, order, s);
+    else
+      return fail(OBN_ERR_UNSUPPORTED, "in_dim %d exceeds the kernels' limit", layer->in_dim);
+    if (e != cudaSuccess) return cuda_fail(e, "ternary matmul launch");
   }
-  e = obn::launch_rmsnorm_quant(x, layer->norm, layer->eps, n, layer->in_dim, q, sc, qs, s);
-  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
-  const int order = n == 1 ? obn::kOrderGemv : obn::kOrderGemm;  // bitlinear.rs:90-94
-  if (obn::gemm_supported(view(layer), n))
-    e = obn::launch_gemm(view(layer), q, sc, qs, n, y, nullptr, order, s);
-  else if (layer->in_dim <= obn::kGemvMaxK)
-    e = obn::launch_gemv(view(layer), q, sc, qs, n, y, nullptr, order, s);
-  else
-    return fail(OBN_ERR_UNSUPPORTED, "in_dim %d exceeds the kernels' limit", layer->in_dim);
-  if (e != cudaSuccess) return cuda_fail(e, "ternary matmul launch");
+  if (layer->gated) {  // ffn.rs:70-79: activation.wgsl (ReLU^2) then elementwise.wgsl (multiply)
+    e = obn::launch_relu2_mul(ym, n, layer->out_dim, y, s);
+    if (e != cudaSuccess) return cuda_fail(e, "relu^2 * up launch");
+  }
   return OBN_OK;
 }
 
@@ -353,6 +435,8 @@ int obn_bitlinear_forward_tp(const obn_bitlinear* layer, const float* x, int n, 
     return fail(OBN_ERR_INVALID_ARGUMENT,
                 "columns [%d, %d) do not fit an output of %d columns", col0,
                 col0 + layer->out_dim, out_total);
+  if (layer->gated)
+    return fail(OBN_ERR_UNSUPPORTED, "the gathered forward does not take a gated FFN layer");
   if (n < obn::kGemmMinTokens || !obn::gemm_supported(view(layer), n))
     return fail(OBN_ERR_UNSUPPORTED, "the gathered forward needs n >= %d tokens (got %d)",
                 obn::kGemmMinTokens, n);
@@ -420,7 +504,7 @@ int obn_bitlinear_export_i2s(const obn_bitlinear* layer, uint8_t* dst_dev, void*
   if (int rc = check_layer(layer)) return rc;
   if (!dst_dev || !aligned(dst_dev, 16))
     return fail(OBN_ERR_INVALID_ARGUMENT, "destination must be non-null and 16-byte aligned");
-  cudaError_t e = obn::launch_export_i2s(layer->w, dst_dev, layer->out_dim, layer->in_dim,
+  cudaError_t e = obn::launch_export_i2s(layer->w, dst_dev, layer->rows, layer->in_dim,
                                          static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "export launch");
   return OBN_OK;

@@ -676,6 +676,37 @@ cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps,
                     qsum);
 }
 
+namespace {
+// activation.wgsl:28-33 then elementwise.wgsl:31-32: two outputs per thread from
+// one 16-byte load of (gate, up, gate, up).
+__global__ __launch_bounds__(256) void k_relu2_mul(const float4* __restrict__ gu,
+                                                   const float* __restrict__ gu1, size_t pairs2,
+                                                   size_t total, float* __restrict__ y) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < pairs2) {
+    const float4 v = gu[i];
+    const float r0 = fmaxf(0.0f, v.x), r1 = fmaxf(0.0f, v.z);
+    y[2 * i] = __fmul_rn(__fmul_rn(r0, r0), v.y);
+    y[2 * i + 1] = __fmul_rn(__fmul_rn(r1, r1), v.w);
+  } else if (i == pairs2 && 2 * pairs2 < total) {  // odd element count: the last output
+    const size_t j = 2 * pairs2;
+    const float r = fmaxf(0.0f, gu1[2 * j]);
+    y[j] = __fmul_rn(__fmul_rn(r, r), gu1[2 * j + 1]);
+  }
+}
+}  // namespace
+
+cudaError_t launch_relu2_mul(const float* gu, int n, int d, float* y, cudaStream_t s) {
+  const size_t total = static_cast<size_t>(n) * d;
+  const size_t pairs2 = total / 2;
+  const size_t threads = pairs2 + 1;
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  return launch_pdl(k_relu2_mul, dim3(blocks), dim3(256), 0, s,
+                    reinterpret_cast<const float4*>(gu), gu, pairs2, total, y);
+}
+
 cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int d, float* y,
                            cudaStream_t s) {
   return launch_pdl(k_rmsnorm, dim3(n), dim3(256), 0, s, x, w, eps, d, y);

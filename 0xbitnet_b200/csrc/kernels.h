@@ -33,6 +33,11 @@ cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps,
 cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int d, float* y,
                            cudaStream_t s);
 
+// Gated FFN activation over interleaved gate|up outputs (activation.wgsl ReLU^2,
+// then elementwise.wgsl multiply): y[i] = (r * r) * gu[2i + 1], r = max(0, gu[2i]),
+// for i < n * d (gu: [n, 2d], y: [n, d]).
+cudaError_t launch_relu2_mul(const float* gu, int n, int d, float* y, cudaStream_t s);
+
 // Decode-path matmul on CUDA cores (dp4a) for any n (tokens in groups of 8).
 // Writes y (float, `order` rounding) or, when acc != nullptr, exact int32 sums.
 cudaError_t launch_gemv(const WeightView& W, const int8_t* q, const float* s_x,

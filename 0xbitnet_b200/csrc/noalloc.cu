@@ -56,6 +56,14 @@ extern "C" int obn_bitlinear_forward_noalloc(const obn_bitlinear* layer, const f
              n, obn_bitlinear_in_dim(layer), act, kNoAllocActBytes, kNoAllocMaxTokens);
     return obn::report_error(OBN_ERR_UNSUPPORTED, msg);
   }
+  if (obn_bitlinear_workspace_bytes(layer, n) > kNoAllocBytes) {
+    char msg[192];
+    snprintf(msg, sizeof(msg),
+             "obn_bitlinear_forward_noalloc: n=%d needs %zu scratch bytes; the fixed scratch "
+             "holds %zu",
+             n, obn_bitlinear_workspace_bytes(layer, n), kNoAllocBytes);
+    return obn::report_error(OBN_ERR_UNSUPPORTED, msg);
+  }
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)

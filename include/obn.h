@@ -77,6 +77,21 @@ OBN_API int obn_bitlinear_load_i2s(const uint8_t* i2s_tensor, size_t nbytes, int
                            const float* norm_weight, float eps, int device,
                            obn_bitlinear** out_layer);
 
+/* The gated FFN's gate and up projections merged into one layer
+ * (FFN::forward_gated, ffn.rs:70-79: gate_proj and up_proj on the same input,
+ * then activation.wgsl ReLU^2 on gate and elementwise.wgsl multiply by up).
+ * gate_i2s / up_i2s are the two GGUF I2_S tensors ([out_dim, in_dim] each plus
+ * their 32-byte scale trailers), sharing norm_weight and eps. The layer's
+ * forward quantizes the input once, runs one matmul over the 2 * out_dim
+ * interleaved weight rows (row 2i = gate row i, row 2i + 1 = up row i) and
+ * writes y[t, i] = (r * r) * up[t, i] with r = max(0, gate[t, i]): [n, out_dim].
+ * obn_ternary_matmul / obn_ternary_acc / obn_bitlinear_export_i2s on such a
+ * layer work on the interleaved rows (obn_bitlinear_rows(layer) of them). */
+OBN_API int obn_bitlinear_load_i2s_gated(const uint8_t* gate_i2s, size_t gate_bytes,
+                                         const uint8_t* up_i2s, size_t up_bytes, int in_dim,
+                                         int out_dim, const float* norm_weight, float eps,
+                                         int device, obn_bitlinear** out_layer);
+
 /* BitLinear::new(device, packed_weights, weight_scales, norm_weight, in_dim,
  * out_dim) (bitlinear.rs:31-49) over buffers already on the device in the
  * reference's layout: packed [out_dim, in_dim/16] u32, per-row scales
@@ -92,6 +107,9 @@ OBN_API void obn_bitlinear_free(obn_bitlinear* layer);
 /* Shape queries. */
 OBN_API int obn_bitlinear_in_dim(const obn_bitlinear* layer);
 OBN_API int obn_bitlinear_out_dim(const obn_bitlinear* layer);
+/* Weight rows the matmul entry points compute: out_dim, or 2 * out_dim for a
+ * gated layer. */
+OBN_API int obn_bitlinear_rows(const obn_bitlinear* layer);
 
 /* Device scratch that obn_bitlinear_forward needs for n tokens (bytes). */
 OBN_API size_t obn_bitlinear_workspace_bytes(const obn_bitlinear* layer, int n);

@@ -224,3 +224,12 @@ def f32_matmul_seq(hidden: np.ndarray, embed: np.ndarray, N: int, V: int, D: int
     out = np.empty(N * V, np.float32)
     lib().orc_f32_matmul_seq(_p(h, _f32p), _p(e, _f32p), N, V, D, _p(out, _f32p))
     return out
+
+
+# ---- gated FFN (ffn.rs:70-79: activation.wgsl ReLU^2, elementwise.wgsl multiply)
+def relu2_mul(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    g = np.ascontiguousarray(gate, np.float32)
+    u = np.ascontiguousarray(up, np.float32)
+    y = np.empty_like(g)
+    lib().orc_relu2_mul(_p(g, _f32p), _p(u, _f32p), ctypes.c_size_t(g.size), _p(y, _f32p))
+    return y

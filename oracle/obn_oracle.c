@@ -218,6 +218,17 @@ void orc_bitlinear(const float* x, int n, const float* norm_w, float eps,
   free(normed);
 }
 
+/* ---- Gated FFN activation (ffn.rs:70-79) ---------------------------------- */
+/* activation.wgsl:30-33 (ReLU^2: max(0, x), squared) on gate, then
+ * elementwise.wgsl:31-32 (multiply) by up: y = (r * r) * u. */
+void orc_relu2_mul(const float* gate, const float* up, size_t n, float* y) {
+  for (size_t i = 0; i < n; ++i) {
+    float r = fmaxf(0.0f, gate[i]);
+    float t = r * r;
+    y[i] = t * up[i];
+  }
+}
+
 /* ---- LM head (packages/core/src/shaders/f32_matmul.wgsl:27-74) ---------- */
 /* IEEE binary16 -> binary32, exact (unpack2x16float). */
 float orc_half_to_float(uint16_t h) {

@@ -92,6 +92,7 @@ void orc_bitlinear_omp(const float* x, int n, const float* norm_w, float eps,
                        const uint8_t* w_i2s, const float* s_w, int M, int K,
                        float* out, int threads);
 
+void orc_relu2_mul(const float* gate, const float* up, size_t n, float* y);
 float orc_half_to_float(uint16_t h);
 void orc_lm_head_f16(const float* hidden, const uint16_t* embed, int N, int V, int D, float* out);
 void orc_f32_matmul_seq(const float* hidden, const float* embed, int N, int V, int D, float* out);

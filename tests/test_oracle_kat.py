@@ -430,3 +430,10 @@ def test_half_to_float_exact():
     finite = bits[np.isfinite(bits.view(np.float16))]
     got = np.array([orc.half_to_float(int(b)) for b in finite], np.float32)
     assert np.array_equal(got, finite.view(np.float16).astype(np.float32))
+
+
+# ---- gated FFN activation: activation.test.ts / elementwise.test.ts ---------
+def test_relu2_mul():
+    g = np.array([-2.0, -0.0, 0.0, 0.5, 3.0], np.float32)
+    u = np.array([7.0, 1.0, 1.0, 2.0, -1.0], np.float32)
+    assert orc.relu2_mul(g, u).tolist() == [0.0, 0.0, 0.0, 0.5, -9.0]
