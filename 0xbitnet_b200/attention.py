@@ -1,0 +1,64 @@
+"""Decode attention around the BitLinear path (host mirror over libobn's C ABI).
+
+The reference's ``Attention::forward`` (packages/rust/crates/oxbitnet/src/nn/
+attention.rs:85-124) projects q/k/v with BitLinear, applies RoPE (rope.wgsl),
+appends k/v to an f32 KV cache, computes scores, softmax and the weighted sum
+of V (attention.wgsl, softmax.wgsl), then the o projection. Here the q/k/v
+projections are one merged BitLinear whose output feeds
+``rope_kv_append`` (RoPE + an fp16 cache append in one kernel) and
+``attention`` (split-KV GQA attention with a combine pass); the o projection
+is a BitLinear again.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._lib import check, lib
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(None)
+
+
+def _stream(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+class KVCache:
+    """fp16 caches [B, S_max, Hkv, head_dim] for keys and values of one layer."""
+
+    def __init__(self, B: int, S_max: int, Hkv: int, head_dim: int = 128, device=None):
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        self.k = torch.zeros((B, S_max, Hkv, head_dim), dtype=torch.float16, device=device)
+        self.v = torch.zeros_like(self.k)
+        self.B, self.S_max, self.Hkv, self.head_dim = B, S_max, Hkv, head_dim
+        self.seq_len = 0
+
+
+def rope_kv_append(qkv: torch.Tensor, cache: KVCache, H: int, n: int,
+                   theta_base: float = 500000.0) -> torch.Tensor:
+    """qkv [B*n, (H + 2*Hkv) * d] f32 of n new tokens per sequence -> rotated q
+    [B*n, H*d]; k (rotated) and v stored at positions seq_len .. seq_len + n - 1."""
+    d = cache.head_dim
+    q = torch.empty((cache.B * n, H * d), dtype=torch.float32, device=qkv.device)
+    check(lib().obn_rope_kv_append(_ptr(qkv), cache.B, n, H, cache.Hkv, d, cache.seq_len,
+                                   ctypes.c_float(theta_base), _ptr(q), _ptr(cache.k),
+                                   _ptr(cache.v), cache.S_max, _stream(qkv.device)))
+    return q
+
+
+def attention(q: torch.Tensor, cache: KVCache, H: int, n: int, seq_len: int,
+              scale: float | None = None) -> torch.Tensor:
+    """Causal GQA attention of the n newest tokens (the cache holds seq_len
+    positions per sequence): q [B*n, H*d] -> out [B*n, H*d]."""
+    d = cache.head_dim
+    sc = float(1.0 / (d ** 0.5)) if scale is None else scale
+    out = torch.empty_like(q)
+    need = int(lib().obn_attention_workspace_bytes(cache.B, n, H, d, seq_len))
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    check(lib().obn_attention_decode(_ptr(q), _ptr(cache.k), _ptr(cache.v), cache.B, n, H,
+                                     cache.Hkv, d, cache.S_max, seq_len, ctypes.c_float(sc),
+                                     _ptr(out), _ptr(ws), ws.numel(), _stream(q.device)))
+    return out

@@ -15,6 +15,7 @@
 #include "kernels.h"
 #include "layout.cuh"
 #include "lmhead.h"
+#include "attention.h"
 
 struct obn_bitlinear {
   int device = 0;
@@ -496,6 +497,62 @@ int obn_lm_head_f16(const void* embed, int vocab, int dim, const float* x,
   cudaError_t e = obn::launch_lm_head_f16(embed, vocab, dim, x, norm_weight, eps, n, logits,
                                           static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "lm head launch");
+  return OBN_OK;
+}
+
+int obn_rope_kv_append(const float* qkv, int B, int n, int H, int Hkv, int head_dim, int pos,
+                       float theta_base, float* q_out, void* k_cache, void* v_cache, int S_max,
+                       void* stream) {
+  clear_error();
+  if (!qkv || !q_out || !k_cache || !v_cache)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (B <= 0 || n <= 0 || H <= 0 || Hkv <= 0 || pos < 0 || S_max <= 0)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "sizes must be positive (pos >= 0)");
+  if (head_dim != obn::kAttnHeadDim)
+    return fail(OBN_ERR_UNSUPPORTED, "head_dim must be %d (got %d)", obn::kAttnHeadDim, head_dim);
+  if (static_cast<long long>(pos) + n > S_max)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "positions %d..%d exceed the cache of %d", pos,
+                pos + n - 1, S_max);
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(qkv, 8) || !aligned(q_out, 8))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "caches must be 16-byte, qkv and q_out 8-byte aligned");
+  cudaError_t e = obn::launch_rope_kv_append(
+      qkv, B, n, H, Hkv, head_dim, pos, theta_base, q_out, static_cast<__half*>(k_cache),
+      static_cast<__half*>(v_cache), S_max, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rope / kv append launch");
+  return OBN_OK;
+}
+
+size_t obn_attention_workspace_bytes(int B, int n, int H, int head_dim, int seq_len) {
+  if (B <= 0 || n <= 0 || H <= 0 || head_dim <= 0 || seq_len <= 0) return 0;
+  return obn::attention_workspace_bytes(B, n, H, head_dim, seq_len);
+}
+
+int obn_attention_decode(const float* q, const void* k_cache, const void* v_cache, int B, int n,
+                         int H, int Hkv, int head_dim, int S_max, int seq_len, float scale,
+                         float* out, void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (!q || !k_cache || !v_cache || !out || !workspace)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (B <= 0 || n <= 0 || H <= 0 || Hkv <= 0 || seq_len <= 0 || n > seq_len || seq_len > S_max)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "need 0 < n <= seq_len <= S_max (got %d, %d, %d)", n,
+                seq_len, S_max);
+  if (head_dim != obn::kAttnHeadDim)
+    return fail(OBN_ERR_UNSUPPORTED, "head_dim must be %d (got %d)", obn::kAttnHeadDim, head_dim);
+  const int G = H % Hkv == 0 ? H / Hkv : 0;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return fail(OBN_ERR_UNSUPPORTED, "H / Hkv must be 1, 2, 4 or 8 (got %d / %d)", H, Hkv);
+  const size_t need = obn::attention_workspace_bytes(B, n, H, head_dim, seq_len);
+  if (workspace_bytes < need)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than the %zu needed",
+                workspace_bytes, need);
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(workspace, 256) ||
+      !aligned(q, 4) || !aligned(out, 4))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "caches must be 16-byte, workspace 256-byte aligned");
+  cudaError_t e = obn::launch_attention(q, static_cast<const __half*>(k_cache),
+                                        static_cast<const __half*>(v_cache), B, n, H, Hkv,
+                                        head_dim, S_max, seq_len, scale, out, workspace,
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   return OBN_OK;
 }
 

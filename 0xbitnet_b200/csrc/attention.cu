@@ -1,0 +1,311 @@
+// attention.cu — decode attention for the layers around the BitLinear path, sm_100a.
+//
+// Reference: attention.rs:85-124 (Attention::forward), rope.wgsl, attention.wgsl
+// (compute_scores, attn_v) and softmax.wgsl. The reference keeps an f32 KV cache,
+// materialises the [H, N, S] score matrix and runs softmax in three passes. Here:
+//
+//  * k_rope_kv_append: one thread per (token row, head slot, dimension pair)
+//    reads the merged QKV projection output, rotates q and k with the
+//    shader's formula (theta = pos * base^(-2i/D), x0 c - x1 s, x0 s + x1 c,
+//    each product and sum rounded) and writes q (f32) and the k / v of the new
+//    tokens into the binary16 caches [B][S_max][Hkv][d] (half the bytes of the
+//    reference's f32 cache: the decode step streams the cache).
+//  * k_attn_split: one CTA per (128-key chunk, KV head, query row) — the G query
+//    heads of a KV group share each K/V chunk load. Thread = key for the scores
+//    (the dot over d is sequential in d, as attention.wgsl's, then * scale),
+//    thread = dimension for P.V (sequential over the chunk's keys); the chunk
+//    keeps its own max and sum (online softmax), written as partials.
+//  * k_attn_combine: per (query row, head) rescales the chunks' partials to the
+//    global max and divides by the global sum.
+//
+// Keys after a query's causal limit (k > q + (S - N), attention.wgsl:53) are
+// skipped; the reference's -FLT_MAX scores give them exactly zero weight. The
+// softmax is the same function in a different order of operations, so results
+// agree with the reference to rounding (tests: relative 2e-5 on the same fp16
+// cache contents).
+#include "attention.h"
+#include "obn_common.cuh"
+
+#include <cfloat>
+
+namespace obn {
+namespace {
+
+constexpr int kAttnThreads = 128;
+constexpr int kKStride = kAttnHeadDim + 8;  // halves per smem K row: 16-byte rows, no conflicts
+
+__global__ __launch_bounds__(256) void k_rope_kv_append(const float* __restrict__ qkv, int n,
+                                                        int H, int Hkv, int d, int pos,
+                                                        float theta_base, size_t total,
+                                                        float* __restrict__ q_out,
+                                                        __half* __restrict__ k_cache,
+                                                        __half* __restrict__ v_cache, int S_max) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int half = d >> 1;
+  const int slots = H + 2 * Hkv;
+  const int i = static_cast<int>(idx % half);
+  const size_t rest = idx / half;
+  const int j = static_cast<int>(rest % slots);  // head slot: q heads, k heads, v heads
+  const size_t r = rest / slots;                 // token row b * n + t
+  const int t = static_cast<int>(r % n);
+  const size_t b = r / n;
+  const float* src = qkv + (r * slots + j) * d + 2 * i;
+  const float x0 = src[0], x1 = src[1];
+  const int p = pos + t;
+  if (j >= H + Hkv) {  // v: stored as is
+    __half* dst = v_cache + ((b * S_max + p) * Hkv + (j - H - Hkv)) * d + 2 * i;
+    *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(x0, x1);
+    return;
+  }
+  // rope.wgsl:41-55
+  const float freq_exp = __fdiv_rn(__fmul_rn(-2.0f, static_cast<float>(i)), static_cast<float>(d));
+  const float theta = __fmul_rn(static_cast<float>(p), powf(theta_base, freq_exp));
+  float sn, c;
+  sincosf(theta, &sn, &c);
+  const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+  const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+  if (j < H) {
+    float* dst = q_out + (r * H + j) * d + 2 * i;
+    dst[0] = y0;
+    dst[1] = y1;
+  } else {
+    __half* dst = k_cache + ((b * S_max + p) * Hkv + (j - H)) * d + 2 * i;
+    *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(y0, y1);
+  }
+}
+
+OBN_DEVINL float warp_max(float v) {
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, s));
+  return v;
+}
+OBN_DEVINL float warp_sum(float v) {
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+  return v;
+}
+
+// Partials layout (workspace): for row r, head h, split c:
+//   acc[((r * H + h) * nsplit + c) * D + dim], then m[...] and l[...] after all acc.
+template <int G>
+__global__ __launch_bounds__(kAttnThreads) void k_attn_split(
+    const float* __restrict__ q, const __half* __restrict__ k_cache,
+    const __half* __restrict__ v_cache, int n, int H, int Hkv, int S_max, int seq_len, float scale,
+    int nsplit, float* __restrict__ part_acc, float* __restrict__ part_m,
+    float* __restrict__ part_l) {
+  constexpr int D = kAttnHeadDim;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __half* sK = reinterpret_cast<__half*>(smem);                       // [128][kKStride]
+  __half* sV = sK + kAttnChunk * kKStride;                            // [128][D]
+  float* sQ = reinterpret_cast<float*>(sV + kAttnChunk * D);          // [G][D]
+  float* sP = sQ + G * D;                                             // [G][128]
+  __shared__ float red[G][kAttnThreads / 32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = blockIdx.x, kvh = blockIdx.y;
+  const size_t r = blockIdx.z;  // query row b * n + t
+  const int t = static_cast<int>(r % n);
+  const size_t b = r / n;
+  const int limit = seq_len - n + t + 1;  // keys [0, limit) are visible to this query
+  const int s0 = c * kAttnChunk;
+  const int cnt = min(kAttnChunk, limit - s0);  // may be <= 0: an empty chunk
+  const size_t pbase = (r * H + static_cast<size_t>(kvh) * G) * nsplit + c;
+  if (cnt <= 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      part_acc[(pbase + static_cast<size_t>(g) * nsplit) * D + tid] = 0.0f;
+      if (tid == 0) {
+        part_m[pbase + static_cast<size_t>(g) * nsplit] = -FLT_MAX;
+        part_l[pbase + static_cast<size_t>(g) * nsplit] = 0.0f;
+      }
+    }
+    return;
+  }
+  // q rows of the group's heads, and the chunk's K and V rows (16-byte loads).
+  for (int e = tid; e < G * D; e += kAttnThreads)
+    sQ[e] = q[(r * H + static_cast<size_t>(kvh) * G) * D + e];
+  for (int e = tid; e < kAttnChunk * (D / 8); e += kAttnThreads) {
+    const int key = e / (D / 8), part = e % (D / 8);
+    uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = make_uint4(0u, 0u, 0u, 0u);
+    if (key < cnt) {
+      const size_t off = ((b * S_max + s0 + key) * Hkv + kvh) * D + part * 8;
+      kv = *reinterpret_cast<const uint4*>(k_cache + off);
+      vv = *reinterpret_cast<const uint4*>(v_cache + off);
+    }
+    *reinterpret_cast<uint4*>(sK + key * kKStride + part * 8) = kv;
+    *reinterpret_cast<uint4*>(sV + key * D + part * 8) = vv;
+  }
+  __syncthreads();
+  // Scores: thread = key, the dot sequential over d (attention.wgsl:48-51).
+  float sc[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) sc[g] = 0.0f;
+  const __half* krow = sK + tid * kKStride;
+#pragma unroll 4
+  for (int d8 = 0; d8 < D; d8 += 8) {
+    const uint4 w = *reinterpret_cast<const uint4*>(krow + d8);
+    const __half2* h2 = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 kf = __half22float2(h2[e]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        sc[g] = __fadd_rn(sc[g], __fmul_rn(sQ[g * D + d8 + 2 * e], kf.x));
+        sc[g] = __fadd_rn(sc[g], __fmul_rn(sQ[g * D + d8 + 2 * e + 1], kf.y));
+      }
+    }
+  }
+  const bool valid = tid < cnt;
+  float mg[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    sc[g] = valid ? __fmul_rn(sc[g], scale) : -FLT_MAX;
+    const float wm = warp_max(sc[g]);
+    if (lane == 0) red[g][warp] = wm;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    mg[g] = fmaxf(fmaxf(red[g][0], red[g][1]), fmaxf(red[g][2], red[g][3]));
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float p = valid ? expf(sc[g] - mg[g]) : 0.0f;
+    sP[g * kAttnChunk + tid] = p;
+    const float ws = warp_sum(p);
+    if (lane == 0) red[g][warp] = ws;
+  }
+  __syncthreads();
+  // P.V: thread = dimension, sequential over the chunk's keys.
+  float acc[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) acc[g] = 0.0f;
+  for (int key = 0; key < cnt; ++key) {
+    const float v = __half2float(sV[key * D + tid]);
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = __fadd_rn(acc[g], __fmul_rn(sP[g * kAttnChunk + key], v));
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const size_t pi = pbase + static_cast<size_t>(g) * nsplit;
+    part_acc[pi * D + tid] = acc[g];
+    if (tid == 0) {
+      part_m[pi] = mg[g];
+      part_l[pi] = (red[g][0] + red[g][1]) + (red[g][2] + red[g][3]);
+    }
+  }
+}
+
+// One CTA per (query row, head): thread = dimension.
+__global__ __launch_bounds__(kAttnThreads) void k_attn_combine(const float* __restrict__ part_acc,
+                                                               const float* __restrict__ part_m,
+                                                               const float* __restrict__ part_l,
+                                                               int nsplit,
+                                                               float* __restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  constexpr int D = kAttnHeadDim;
+  const size_t rh = blockIdx.x;  // r * H + h
+  const int tid = threadIdx.x;
+  float M = -FLT_MAX;
+  for (int c = 0; c < nsplit; ++c) M = fmaxf(M, part_m[rh * nsplit + c]);
+  float L = 0.0f, o = 0.0f;
+  for (int c = 0; c < nsplit; ++c) {
+    const float l = part_l[rh * nsplit + c];
+    if (l == 0.0f) continue;  // an empty chunk
+    const float w = expf(part_m[rh * nsplit + c] - M);
+    L = fmaf(w, l, L);
+    o = fmaf(w, part_acc[(rh * nsplit + c) * D + tid], o);
+  }
+  out[rh * D + tid] = o / L;
+}
+
+template <int G>
+cudaError_t launch_split(const float* q, const __half* k_cache, const __half* v_cache, int B,
+                         int n, int H, int Hkv, int S_max, int seq_len, float scale, int nsplit,
+                         float* pa, float* pm, float* pl, cudaStream_t s) {
+  constexpr int D = kAttnHeadDim;
+  const size_t smem = static_cast<size_t>(kAttnChunk) * kKStride * 2 +
+                      static_cast<size_t>(kAttnChunk) * D * 2 + static_cast<size_t>(G) * D * 4 +
+                      static_cast<size_t>(G) * kAttnChunk * 4;
+  auto kern = k_attn_split<G>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nsplit, Hkv, B * n);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, q, k_cache, v_cache, n, H, Hkv, S_max, seq_len, scale,
+                            nsplit, pa, pm, pl);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_attn(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s,
+                            Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+}  // namespace
+
+cudaError_t launch_rope_kv_append(const float* qkv, int B, int n, int H, int Hkv, int d, int pos,
+                                  float theta_base, float* q_out, __half* k_cache,
+                                  __half* v_cache, int S_max, cudaStream_t s) {
+  const size_t total = static_cast<size_t>(B) * n * (H + 2 * Hkv) * (d / 2);
+  const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
+  return launch_pdl_attn(k_rope_kv_append, dim3(blocks), dim3(256), s, qkv, n, H, Hkv, d, pos,
+                         theta_base, total, q_out, k_cache, v_cache, S_max);
+}
+
+size_t attention_workspace_bytes(int B, int n, int H, int d, int seq_len) {
+  const size_t nsplit = (static_cast<size_t>(seq_len) + kAttnChunk - 1) / kAttnChunk;
+  return static_cast<size_t>(B) * n * H * nsplit * (d + 2) * sizeof(float);
+}
+
+cudaError_t launch_attention(const float* q, const __half* k_cache, const __half* v_cache, int B,
+                             int n, int H, int Hkv, int d, int S_max, int seq_len, float scale,
+                             float* out, void* workspace, cudaStream_t s) {
+  if (d != kAttnHeadDim || Hkv <= 0 || H % Hkv != 0 || H / Hkv > kAttnMaxGroup)
+    return cudaErrorInvalidValue;
+  const int nsplit = (seq_len + kAttnChunk - 1) / kAttnChunk;
+  const size_t rows = static_cast<size_t>(B) * n * H * nsplit;
+  float* pa = static_cast<float*>(workspace);
+  float* pm = pa + rows * d;
+  float* pl = pm + rows;
+  const int G = H / Hkv;
+  cudaError_t e;
+  switch (G) {
+    case 1: e = launch_split<1>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, scale, nsplit, pa, pm, pl, s); break;
+    case 2: e = launch_split<2>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, scale, nsplit, pa, pm, pl, s); break;
+    case 4: e = launch_split<4>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, scale, nsplit, pa, pm, pl, s); break;
+    case 8: e = launch_split<8>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, scale, nsplit, pa, pm, pl, s); break;
+    default: return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess) return e;
+  return launch_pdl_attn(k_attn_combine, dim3(static_cast<unsigned>(B * n * H)),
+                         dim3(kAttnThreads), s, static_cast<const float*>(pa),
+                         static_cast<const float*>(pm), static_cast<const float*>(pl), nsplit,
+                         out);
+}
+
+}  // namespace obn

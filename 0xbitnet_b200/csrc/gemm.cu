@@ -1127,8 +1127,12 @@ int split_k_factor(const WeightView& W) {
 
 bool gemm_supported(const WeightView& W, int n) {
   if (W.in_dim % kBK != 0 || W.m_pad % kBM != 0 || encode_fn() == nullptr) return false;
-  // Below 16 tokens only the split-K form beats the dp4a GEMV (measured on B200).
-  return n >= kGemmMinTokens || (n >= kGemmMinSplitTokens && split_k_factor<16>(W) > 1);
+  // From 4 tokens the tensor cores beat the dp4a GEMV when they get most SMs:
+  // through split-K on layers with few row tiles, or directly on layers with
+  // more row tiles than half the SMs (measured on B200).
+  if (n >= kGemmMinTokens) return true;
+  if (n < kGemmMinSplitTokens) return false;
+  return split_k_factor<16>(W) > 1 || 2 * (W.m_pad / kBM) > num_sms();
 }
 
 cudaError_t launch_gemm(const WeightView& W, const int8_t* q, const float* s_x,

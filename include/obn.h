@@ -174,6 +174,34 @@ OBN_API int obn_lm_head_f16(const void* embed, int vocab, int dim, const float* 
                             const float* norm_weight, float eps, int n, float* logits,
                             void* stream);
 
+/* ---- decode attention around the BitLinear path ----------------------------- */
+/* RoPE + KV-cache append (attention.rs:98-104: apply_rope on q and k, then
+ * append_to_cache; rope.wgsl). qkv: [B*n, (H + 2*Hkv) * head_dim] f32, the merged QKV
+ * projection output of n new tokens of each of B sequences (q heads, then k heads,
+ * then v heads). Token t of a sequence sits at position pos + t. Writes q_out
+ * [B*n, H * head_dim] f32 (rotated) and stores the rotated k and the v of each new
+ * token into the caches k_cache / v_cache [B][S_max][Hkv][head_dim] (IEEE binary16,
+ * 16-byte aligned; the reference keeps f32). Needs head_dim == 128, pos + n <= S_max. */
+OBN_API int obn_rope_kv_append(const float* qkv, int B, int n, int H, int Hkv, int head_dim,
+                               int pos, float theta_base, float* q_out, void* k_cache,
+                               void* v_cache, int S_max, void* stream);
+
+/* Scratch bytes of obn_attention_decode for these sizes. */
+OBN_API size_t obn_attention_workspace_bytes(int B, int n, int H, int head_dim, int seq_len);
+
+/* Causal GQA attention of the n newest tokens of B sequences (attention.rs:106-121:
+ * compute_scores, softmax, compute_attn_v; attention.wgsl, softmax.wgsl): the caches
+ * hold seq_len positions per sequence, the n new ones last; query t attends to keys
+ * [0, seq_len - n + t]. q [B*n, H * head_dim] f32 -> out [B*n, H * head_dim] f32,
+ * scale = the score scale (the reference uses 1 / sqrt(head_dim)). Split-KV (128-key
+ * chunks) with a combine pass; the workspace (256-byte aligned) holds
+ * obn_attention_workspace_bytes(...) bytes. Needs head_dim == 128 and H / Hkv in
+ * {1, 2, 4, 8}. */
+OBN_API int obn_attention_decode(const float* q, const void* k_cache, const void* v_cache, int B,
+                                 int n, int H, int Hkv, int head_dim, int S_max, int seq_len,
+                                 float scale, float* out, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
 /* ---- kernel-level entry points (one per reference shader) ------------------ */
 
 /* Fused rmsnorm.wgsl + quantize.wgsl: per token, optional RMSNorm with gamma

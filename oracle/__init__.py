@@ -233,3 +233,29 @@ def relu2_mul(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
     y = np.empty_like(g)
     lib().orc_relu2_mul(_p(g, _f32p), _p(u, _f32p), ctypes.c_size_t(g.size), _p(y, _f32p))
     return y
+
+
+# ---- attention (rope.wgsl, attention.wgsl, softmax.wgsl; attention.rs:85-124)
+def rope(x: np.ndarray, heads: int, head_dim: int, pos_offset: int,
+         theta_base: float = 500000.0) -> np.ndarray:
+    """x [N, heads*head_dim] -> rotated copy (rope.wgsl:27-56)."""
+    y = np.ascontiguousarray(x, np.float32).copy()
+    N = y.size // (heads * head_dim)
+    lib().orc_rope(_p(y, _f32p), N, heads, head_dim, pos_offset, ctypes.c_float(theta_base))
+    return y
+
+
+def attention(q: np.ndarray, K: np.ndarray, V: np.ndarray, H: int, Hkv: int, d: int,
+              scale: float | None = None) -> np.ndarray:
+    """One sequence: q [N, H*d], K/V [S, Hkv*d] (S includes the N new tokens,
+    causal) -> out [N, H*d]."""
+    q = np.ascontiguousarray(q, np.float32)
+    K = np.ascontiguousarray(K, np.float32)
+    V = np.ascontiguousarray(V, np.float32)
+    N = q.size // (H * d)
+    S = K.size // (Hkv * d)
+    sc = float(np.float32(1.0) / np.sqrt(np.float32(d))) if scale is None else scale
+    out = np.empty((N, H * d), np.float32)
+    lib().orc_attention(_p(q, _f32p), _p(K, _f32p), _p(V, _f32p), N, S, H, Hkv, d,
+                        ctypes.c_float(sc), _p(out, _f32p))
+    return out

@@ -229,6 +229,75 @@ void orc_relu2_mul(const float* gate, const float* up, size_t n, float* y) {
   }
 }
 
+/* ---- RoPE (packages/core/src/shaders/rope.wgsl:27-56) --------------------- */
+/* x [N, heads, head_dim] in place: pair i of (token t, head h) at position
+ * pos_offset + t rotates by theta = pos * base^(-2i/D) (:43-45). */
+void orc_rope(float* x, int N, int heads, int head_dim, int pos_offset, float theta_base) {
+  const int half = head_dim / 2;
+  for (int t = 0; t < N; ++t)
+    for (int h = 0; h < heads; ++h)
+      for (int i = 0; i < half; ++i) {
+        float pos = (float)(t + pos_offset);
+        float freq_exp = -2.0f * (float)i / (float)head_dim;
+        float theta = pos * powf(theta_base, freq_exp);
+        float c = cosf(theta), sn = sinf(theta);
+        float* p = x + ((size_t)t * heads + h) * head_dim + 2 * i;
+        float x0 = p[0], x1 = p[1];
+        float a = x0 * c, b = x1 * sn, e = x0 * sn, f = x1 * c;
+        p[0] = a - b;                                /* :54-55 */
+        p[1] = e + f;
+      }
+}
+
+/* ---- Attention (attention.wgsl + softmax.wgsl, attention.rs:85-124) ------- */
+/* One sequence: q [N, H, d]; K, V [S, Hkv, d] (S includes the N new tokens);
+ * out [N, H, d]. scores = (sequential dot) * scale with the causal mask
+ * k > q + (S - N) -> -FLT_MAX (attention.wgsl:44-56); softmax.wgsl's three
+ * passes with 256-lane partials and halving trees; out = sequential sum over
+ * s of weight * V (attention.wgsl:87-95). */
+void orc_attention(const float* q, const float* K, const float* V, int N, int S, int H, int Hkv,
+                   int d, float scale, float* out) {
+  float* sc = (float*)malloc(sizeof(float) * (size_t)S);
+  float part[ORC_LANES];
+  const int group = H / Hkv;
+  for (int h = 0; h < H; ++h) {
+    const int kvh = h / group;
+    for (int t = 0; t < N; ++t) {
+      const float* qr = q + ((size_t)t * H + h) * d;
+      for (int s = 0; s < S; ++s) {
+        const float* kr = K + ((size_t)s * Hkv + kvh) * d;
+        float dot = 0.0f;
+        for (int i = 0; i < d; ++i) { float pr = qr[i] * kr[i]; dot = dot + pr; }
+        sc[s] = (s > t + (S - N)) ? -3.402823e+38f : dot * scale;
+      }
+      for (int tid = 0; tid < ORC_LANES; ++tid) {   /* softmax pass 1: max */
+        float m = -3.402823e+38f;
+        for (int c = tid; c < S; c += ORC_LANES) m = fmaxf(m, sc[c]);
+        part[tid] = m;
+      }
+      for (int st = ORC_LANES / 2; st > 0; st >>= 1)
+        for (int tid = 0; tid < st; ++tid) part[tid] = fmaxf(part[tid], part[tid + st]);
+      const float mx = part[0];
+      for (int tid = 0; tid < ORC_LANES; ++tid) {   /* pass 2: sum of exp */
+        float acc = 0.0f;
+        for (int c = tid; c < S; c += ORC_LANES) acc = acc + expf(sc[c] - mx);
+        part[tid] = acc;
+      }
+      for (int st = ORC_LANES / 2; st > 0; st >>= 1)
+        for (int tid = 0; tid < st; ++tid) part[tid] = part[tid] + part[tid + st];
+      const float inv = 1.0f / part[0];
+      for (int s = 0; s < S; ++s) sc[s] = expf(sc[s] - mx) * inv;   /* pass 3 */
+      float* orow = out + ((size_t)t * H + h) * d;
+      for (int i = 0; i < d; ++i) {
+        float sum = 0.0f;
+        for (int s = 0; s < S; ++s) { float pr = sc[s] * V[((size_t)s * Hkv + kvh) * d + i]; sum = sum + pr; }
+        orow[i] = sum;
+      }
+    }
+  }
+  free(sc);
+}
+
 /* ---- LM head (packages/core/src/shaders/f32_matmul.wgsl:27-74) ---------- */
 /* IEEE binary16 -> binary32, exact (unpack2x16float). */
 float orc_half_to_float(uint16_t h) {

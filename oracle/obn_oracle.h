@@ -93,6 +93,9 @@ void orc_bitlinear_omp(const float* x, int n, const float* norm_w, float eps,
                        float* out, int threads);
 
 void orc_relu2_mul(const float* gate, const float* up, size_t n, float* y);
+void orc_rope(float* x, int N, int heads, int head_dim, int pos_offset, float theta_base);
+void orc_attention(const float* q, const float* K, const float* V, int N, int S, int H, int Hkv,
+                   int d, float scale, float* out);
 float orc_half_to_float(uint16_t h);
 void orc_lm_head_f16(const float* hidden, const uint16_t* embed, int N, int V, int D, float* out);
 void orc_f32_matmul_seq(const float* hidden, const float* embed, int N, int V, int D, float* out);

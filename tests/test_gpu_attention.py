@@ -1,0 +1,94 @@
+"""GPU checks of the decode attention kernels against the oracle.
+
+RoPE + fp16 KV append against rope.wgsl's formula (q exact to the math
+library's last bits; the caches equal the binary16 rounding of the rotated k and
+of v), and the split-KV GQA attention against attention.wgsl + softmax.wgsl on
+the same fp16 cache contents: decode (one token, up to 2048 keys, several
+sequences), chunked prefill with the causal mask, and group sizes 1, 4 and 8.
+The tolerance (1e-4 relative, 1e-5 absolute) covers the math library's exp and
+the different summation order of the online softmax.
+"""
+import numpy as np
+import pytest
+
+import oracle as orc
+from _util import need_cuda
+
+pytestmark = pytest.mark.gpu
+
+
+def att():
+    import importlib
+    return importlib.import_module("0xbitnet_b200.attention")
+
+
+D = 128
+
+
+@pytest.mark.parametrize("B,n,H,Hkv,pos", [(2, 3, 20, 5, 100), (1, 1, 8, 8, 0), (3, 1, 16, 2, 2000)])
+def test_rope_kv_append(B, n, H, Hkv, pos):
+    torch = need_cuda()
+    S_max = pos + n + 5
+    rng = np.random.default_rng(B * 100 + n + pos)
+    qkv = rng.standard_normal((B * n, (H + 2 * Hkv) * D)).astype(np.float32)
+    cache = att().KVCache(B, S_max, Hkv, D)
+    cache.seq_len = pos
+    q = att().rope_kv_append(torch.from_numpy(qkv).cuda(), cache, H, n, 500000.0)
+    q = q.cpu().numpy()
+    kc, vc = cache.k.cpu().numpy(), cache.v.cpu().numpy()
+    tol = 1e-5 if pos < 200 else 1e-3  # theta = pos * base^(-2i/D): pow's last bit, scaled by pos
+    for b in range(B):
+        rows = qkv[b * n:(b + 1) * n]
+        qr = orc.rope(rows[:, :H * D], H, D, pos, 500000.0)
+        kr = orc.rope(rows[:, H * D:(H + Hkv) * D], Hkv, D, pos, 500000.0)
+        np.testing.assert_allclose(q[b * n:(b + 1) * n], qr, atol=tol, rtol=0)
+        got_k = kc[b, pos:pos + n].reshape(n, Hkv * D).astype(np.float32)
+        np.testing.assert_allclose(got_k, kr.astype(np.float16).astype(np.float32),
+                                   atol=tol, rtol=2e-3)
+        got_v = vc[b, pos:pos + n].reshape(n, Hkv * D)
+        assert np.array_equal(got_v, rows[:, (H + Hkv) * D:].astype(np.float16))
+
+
+@pytest.mark.parametrize("B,n,H,Hkv,S", [(1, 1, 20, 5, 1), (1, 1, 20, 5, 2048), (3, 1, 20, 5, 700),
+                                         (2, 5, 20, 5, 300), (1, 7, 8, 8, 7), (2, 1, 16, 2, 129),
+                                         (1, 130, 4, 1, 260)])
+def test_attention_matches_oracle(B, n, H, Hkv, S):
+    torch = need_cuda()
+    S_max = S + 3
+    rng = np.random.default_rng(B + n + H + S)
+    cache = att().KVCache(B, S_max, Hkv, D)
+    k = rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16)
+    v = rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16)
+    cache.k.copy_(torch.from_numpy(k))
+    cache.v.copy_(torch.from_numpy(v))
+    q = rng.standard_normal((B * n, H * D)).astype(np.float32)
+    out = att().attention(torch.from_numpy(q).cuda(), cache, H, n, S).cpu().numpy()
+    for b in range(B):
+        want = orc.attention(q[b * n:(b + 1) * n], k[b, :S].reshape(S, Hkv * D).astype(np.float32),
+                             v[b, :S].reshape(S, Hkv * D).astype(np.float32), H, Hkv, D)
+        np.testing.assert_allclose(out[b * n:(b + 1) * n], want, rtol=1e-4, atol=1e-5)
+
+
+def test_attention_decode_step_end_to_end():
+    # qkv of one new token -> rope + append -> attention, against the oracle on the
+    # same rounded cache
+    torch = need_cuda()
+    B, H, Hkv, S_prev = 2, 20, 5, 500
+    S_max = 1024
+    rng = np.random.default_rng(9)
+    cache = att().KVCache(B, S_max, Hkv, D)
+    k = rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16)
+    v = rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16)
+    cache.k.copy_(torch.from_numpy(k))
+    cache.v.copy_(torch.from_numpy(v))
+    cache.seq_len = S_prev
+    qkv = rng.standard_normal((B, (H + 2 * Hkv) * D)).astype(np.float32)
+    q = att().rope_kv_append(torch.from_numpy(qkv).cuda(), cache, H, 1)
+    out = att().attention(q, cache, H, 1, S_prev + 1).cpu().numpy()
+    kc, vc = cache.k.cpu().numpy(), cache.v.cpu().numpy()
+    qn = q.cpu().numpy()
+    for b in range(B):
+        S = S_prev + 1
+        want = orc.attention(qn[b:b + 1], kc[b, :S].reshape(S, -1).astype(np.float32),
+                             vc[b, :S].reshape(S, -1).astype(np.float32), H, Hkv, D)
+        np.testing.assert_allclose(out[b:b + 1], want, rtol=1e-4, atol=1e-5)

@@ -437,3 +437,43 @@ def test_relu2_mul():
     g = np.array([-2.0, -0.0, 0.0, 0.5, 3.0], np.float32)
     u = np.array([7.0, 1.0, 1.0, 2.0, -1.0], np.float32)
     assert orc.relu2_mul(g, u).tolist() == [0.0, 0.0, 0.0, 0.5, -9.0]
+
+
+# ---- RoPE / attention: rope.test.ts, softmax.test.ts, attention-*.test.ts ---
+def test_rope_position_zero_is_identity():  # rope.test.ts:6-15
+    x = orc.randf32(8, 1).reshape(1, 8)
+    assert np.allclose(orc.rope(x, 2, 4, 0, 10000.0), x, atol=1e-5)
+
+
+def test_rope_preserves_pair_norms_and_offset_shifts():  # rope.test.ts:17-51
+    x = orc.randf32(16, 2).reshape(1, 16)
+    y = orc.rope(x, 2, 8, 5, 10000.0)
+    n_in = np.hypot(x[0, 0::2], x[0, 1::2])
+    n_out = np.hypot(y[0, 0::2], y[0, 1::2])
+    assert np.all(np.abs(n_in - n_out) < 1e-5)
+    assert not np.allclose(orc.rope(x[:, :4], 1, 4, 3, 10000.0)[0, 0], x[0, 0], atol=1e-3)
+
+
+def test_attention_single_key_returns_v():
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((1, 4 * 8)).astype(np.float32)
+    K = rng.standard_normal((1, 2 * 8)).astype(np.float32)
+    V = rng.standard_normal((1, 2 * 8)).astype(np.float32)
+    out = orc.attention(q, K, V, 4, 2, 8).reshape(4, 8)
+    Vh = V.reshape(2, 8)
+    assert np.array_equal(out, np.stack([Vh[h // 2] for h in range(4)]))  # GQA grouping
+
+
+def test_attention_causal_first_query_sees_first_key():  # attention-scores.test.ts causal
+    rng = np.random.default_rng(1)
+    q = rng.standard_normal((3, 8)).astype(np.float32)
+    K = rng.standard_normal((3, 8)).astype(np.float32)
+    V = rng.standard_normal((3, 8)).astype(np.float32)
+    out = orc.attention(q, K, V, 1, 1, 8)
+    assert np.array_equal(out[0], V[0])
+
+
+def test_attention_uniform_scores_average_v():  # softmax.test.ts uniform
+    V = np.arange(12, dtype=np.float32).reshape(4, 3)
+    out = orc.attention(np.zeros((1, 3), np.float32), np.zeros((4, 3), np.float32), V, 1, 1, 3)
+    np.testing.assert_allclose(out[0], V.mean(0), rtol=1e-6)
