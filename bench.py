@@ -431,6 +431,118 @@ def measure_tp_prefill(args, obn, synth, dev, stream, world, rank):
     return out
 
 
+def measure_ffn_gate_up(args, obn, synth, dev, stream, batches):
+    """Next-row measurement: the FFN's gate and up projections of BitNet-2B (6912x2560
+    each) for 30 layers, as the reference runs them (two BitLinear forwards on the
+    same input, each quantizing it) against the merged gated layer (one quantize, one
+    matmul over the interleaved rows, ReLU^2 x up fused: one more pass than nothing,
+    two fewer than the reference's activation + multiply). Device time per layer."""
+    import torch
+    M, K = synth.SHAPES_2B["gate"]
+    nl = args.layers
+    sep, merged = [], []
+    for l in range(nl):
+        g = synth.layer(50_000 + 2 * l, M, K)
+        u = synth.layer(50_001 + 2 * l, M, K)
+        sep.append((obn.BitLinear.from_i2s(g.blob(), K, M, norm_weight=g.gamma, device=dev.index),
+                    obn.BitLinear.from_i2s(u.blob(), K, M, norm_weight=g.gamma, device=dev.index)))
+        merged.append(obn.BitLinear.from_i2s_gated(g.blob(), u.blob(), K, M, norm_weight=g.gamma,
+                                                   device=dev.index))
+    out = {"shape": [M, K], "layers": nl, "per_batch": {}}
+    for B in batches:
+        x = torch.randn(B, K, device=dev)
+        yg, yu, ym = (torch.empty(B, M, device=dev) for _ in range(3))
+
+        def run_sep():
+            for a, b in sep:
+                a.forward(x, out=yg)
+                b.forward(x, out=yu)
+
+        def run_merged():
+            for L in merged:
+                L.forward(x, out=ym)
+        res = {}
+        for name, fn in (("separate_gate_up_us", run_sep), ("merged_gated_us", run_merged)):
+            with torch.cuda.stream(stream):
+                fn()
+                stream.synchronize()
+                gph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gph, stream=stream):
+                    fn()
+                for _ in range(3):
+                    gph.replay()
+                stream.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                reps = 10
+                e0.record(stream)
+                for _ in range(reps):
+                    gph.replay()
+                e1.record(stream)
+                stream.synchronize()
+                res[name] = e0.elapsed_time(e1) * 1e3 / (reps * nl)
+                del gph
+        res["speedup"] = res["separate_gate_up_us"] / res["merged_gated_us"]
+        out["per_batch"][str(B)] = res
+    for a, b in sep:
+        a.close()
+        b.close()
+    for L in merged:
+        L.close()
+    torch.cuda.synchronize()
+    return out
+
+
+def measure_attention(dev, stream, peak, layers):
+    """Next-row kernels: one decode step's attention for BitNet-2B (20 heads, 5 KV
+    heads, head_dim 128) at context 2048 over `layers` layers, fp16 KV: RoPE + KV
+    append of the new token, then split-KV attention + combine. Bytes per layer and
+    sequence = the K and V cache read (2 * 2048 * 5 * 128 * 2) + q, out, new k/v."""
+    import torch
+    att = importlib.import_module("0xbitnet_b200.attention")
+    H, Hkv, Dh, ctx = 20, 5, 128, 2048
+    out = {"heads": H, "kv_heads": Hkv, "head_dim": Dh, "context": ctx, "layers": layers,
+           "per_batch": {}}
+    for B in (1, 64):
+        caches = [att.KVCache(B, ctx, Hkv, Dh, device=dev) for _ in range(layers)]
+        for c in caches:
+            c.k.normal_()
+            c.v.normal_()
+            c.seq_len = ctx - 1
+        qkv = torch.randn(B, (H + 2 * Hkv) * Dh, device=dev)
+
+        def step():
+            for c in caches:
+                q = att.rope_kv_append(qkv, c, H, 1)
+                att.attention(q, c, H, 1, ctx)
+        with torch.cuda.stream(stream):
+            step()
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step()
+            for _ in range(3):
+                g.replay()
+            stream.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            reps = 10
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+            stream.synchronize()
+            del g
+        us = e0.elapsed_time(e1) * 1e3 / (reps * layers)
+        nbytes = B * (2 * ctx * Hkv * Dh * 2 + (H + 2 * Hkv) * Dh * 4 + H * Dh * 8)
+        out["per_batch"][str(B)] = {"us_per_layer": us, "bytes_per_layer": nbytes,
+                                    "achieved_gbs": nbytes / (us * 1e-6) / 1e9,
+                                    "frac": nbytes / (us * 1e-6) / 1e9 / peak}
+        del caches
+    torch.cuda.synchronize()
+    return out
+
+
 def measure_lm_head(obn, dev, stream, peak):
     """Next-row kernel: the f16 LM head of BitNet-2B (128256 x 2560, 656.7 MB) behind
     the final RMSNorm, one token as the reference runs it; the table exceeds L2, so
@@ -686,6 +798,8 @@ def run_ours(args):
 
     prefill = measure_prefill(args, obn, synth, dev, stream) if args.prefill else None
     lm_head = measure_lm_head(obn, dev, stream, peak)
+    ffn_gate_up = measure_ffn_gate_up(args, obn, synth, dev, stream, batches)
+    attention = measure_attention(dev, stream, peak, min(args.layers, 30))
     tp_prefill = None
     if world > 1 and args.tp_tokens > 0:
         tp_prefill = measure_tp_prefill(args, obn, synth, dev, stream, world, rank)
@@ -714,6 +828,8 @@ def run_ours(args):
             "prefill": prefill,
             "tp_prefill": tp_prefill,
             "lm_head": lm_head,
+            "ffn_gate_up": ffn_gate_up,
+            "attention_decode": attention,
             "cpu_baseline": cpu,
             "clocks": clock_info,
             "e2e": {"value": e2e_value, "unit": "GB/s",
