@@ -34,6 +34,7 @@ SIGNATURES = {
     "obn_bitlinear_in_dim": (_I, [_P]),
     "obn_bitlinear_out_dim": (_I, [_P]),
     "obn_bitlinear_rows": (_I, [_P]),
+    "obn_bitlinear_create_gated": (_I, [_P, _P, _P, _P, _P, _F, _I, _I, _P, ctypes.POINTER(_P)]),
     "obn_bitlinear_load_i2s_gated": (_I, [_P, _SZ, _P, _SZ, _I, _I, _P, _F, _I, ctypes.POINTER(_P)]),
     "obn_bitlinear_workspace_bytes": (_SZ, [_P, _I]),
     "obn_bitlinear_forward": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
@@ -43,6 +44,8 @@ SIGNATURES = {
     "obn_rope_kv_append": (_I, [_P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _I, _P]),
     "obn_attention_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "obn_attention_decode": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _SZ, _P]),
+    "obn_add": (_I, [_P, _P, _SZ, _P, _P]),
+    "obn_embed_f16": (_I, [_P, _I, _I, _P, _I, _P, _P]),
     "obn_rmsnorm_quantize": (_I, [_P, _P, _F, _I, _I, _P, _P, _P, _P]),
     "obn_rmsnorm": (_I, [_P, _P, _F, _I, _I, _P, _P]),
     "obn_ternary_matmul": (_I, [_P, _P, _P, _P, _I, _P, _P]),

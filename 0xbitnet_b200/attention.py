@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import ctypes
 
+import numpy as np
 import torch
 
 from ._lib import check, lib
@@ -38,26 +39,33 @@ class KVCache:
 
 
 def rope_kv_append(qkv: torch.Tensor, cache: KVCache, H: int, n: int,
-                   theta_base: float = 500000.0) -> torch.Tensor:
+                   theta_base: float = 500000.0, q_out: torch.Tensor | None = None,
+                   pos: int | None = None) -> torch.Tensor:
     """qkv [B*n, (H + 2*Hkv) * d] f32 of n new tokens per sequence -> rotated q
-    [B*n, H*d]; k (rotated) and v stored at positions seq_len .. seq_len + n - 1."""
+    [B*n, H*d]; k (rotated) and v stored at positions pos .. pos + n - 1
+    (pos defaults to cache.seq_len)."""
     d = cache.head_dim
-    q = torch.empty((cache.B * n, H * d), dtype=torch.float32, device=qkv.device)
-    check(lib().obn_rope_kv_append(_ptr(qkv), cache.B, n, H, cache.Hkv, d, cache.seq_len,
+    q = q_out if q_out is not None else torch.empty((cache.B * n, H * d), dtype=torch.float32,
+                                                     device=qkv.device)
+    pos = cache.seq_len if pos is None else pos
+    check(lib().obn_rope_kv_append(_ptr(qkv), cache.B, n, H, cache.Hkv, d, pos,
                                    ctypes.c_float(theta_base), _ptr(q), _ptr(cache.k),
                                    _ptr(cache.v), cache.S_max, _stream(qkv.device)))
     return q
 
 
 def attention(q: torch.Tensor, cache: KVCache, H: int, n: int, seq_len: int,
-              scale: float | None = None) -> torch.Tensor:
+              scale: float | None = None, out: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Causal GQA attention of the n newest tokens (the cache holds seq_len
     positions per sequence): q [B*n, H*d] -> out [B*n, H*d]."""
     d = cache.head_dim
-    sc = float(1.0 / (d ** 0.5)) if scale is None else scale
-    out = torch.empty_like(q)
+    # attention.rs: scale = 1 / sqrt(head_dim) in f32
+    sc = float(np.float32(1.0) / np.sqrt(np.float32(d))) if scale is None else scale
+    out = out if out is not None else torch.empty_like(q)
     need = int(lib().obn_attention_workspace_bytes(cache.B, n, H, d, seq_len))
-    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    ws = workspace if workspace is not None and workspace.numel() >= need else \
+        torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
     check(lib().obn_attention_decode(_ptr(q), _ptr(cache.k), _ptr(cache.v), cache.B, n, H,
                                      cache.Hkv, d, cache.S_max, seq_len, ctypes.c_float(sc),
                                      _ptr(out), _ptr(ws), ws.numel(), _stream(q.device)))

@@ -101,6 +101,29 @@ class BitLinear:
         self._init(handle, in_dim, out_dim)
         return self
 
+    @classmethod
+    def create_gated(cls, gate_packed: torch.Tensor, gate_scales: torch.Tensor,
+                     up_packed: torch.Tensor, up_scales: torch.Tensor,
+                     norm_weight: torch.Tensor | None, in_dim: int, out_dim: int,
+                     eps: float = 1e-5) -> "BitLinear":
+        """from_i2s_gated over device tensors (I2_S rows [out_dim, in_dim/4] and
+        row scales [out_dim] for gate and for up)."""
+        for t, nm in ((gate_scales, "gate_scales"), (up_scales, "up_scales")):
+            _require_cuda_f32(t, nm)
+        if norm_weight is not None:
+            _require_cuda_f32(norm_weight, "norm_weight")
+        device = gate_packed.device
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            check(lib().obn_bitlinear_create_gated(
+                _ptr(gate_packed), _ptr(gate_scales), _ptr(up_packed), _ptr(up_scales),
+                _ptr(norm_weight), ctypes.c_float(eps), in_dim, out_dim, _stream(device),
+                ctypes.byref(handle)))
+        self = cls.__new__(cls)
+        self.device = device
+        self._init(handle, in_dim, out_dim)
+        return self
+
     def _init(self, handle: ctypes.c_void_p, in_dim: int, out_dim: int) -> None:
         self._h = handle
         self.in_dim = in_dim

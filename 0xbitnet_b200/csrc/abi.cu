@@ -299,6 +299,61 @@ int obn_bitlinear_create(const void* packed_dev, const float* scales_dev, const 
   return OBN_OK;
 }
 
+int obn_bitlinear_create_gated(const void* gate_packed_dev, const float* gate_scales_dev,
+                               const void* up_packed_dev, const float* up_scales_dev,
+                               const float* norm_dev, float eps, int in_dim, int out_dim,
+                               void* stream, obn_bitlinear** out_layer) {
+  clear_error();
+  if (!gate_packed_dev || !gate_scales_dev || !up_packed_dev || !up_scales_dev || !out_layer)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  *out_layer = nullptr;
+  if (int rc = check_dims(in_dim, out_dim)) return rc;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (int rc = check_device(dev)) return rc;
+  auto s = static_cast<cudaStream_t>(stream);
+  const size_t rb = static_cast<size_t>(in_dim) / 4;
+  obn_bitlinear* L = nullptr;
+  if (int rc = alloc_layer(in_dim, 2 * out_dim, eps, &L)) return rc;
+  L->out_dim = out_dim;
+  L->gated = 1;
+  uint8_t* staging = nullptr;
+  cudaError_t e = cudaMalloc(&staging, 2 * rb * out_dim);
+  if (e != cudaSuccess) {
+    free_layer(L);
+    cudaGetLastError();
+    return fail(OBN_ERR_OUT_OF_MEMORY, "cudaMalloc of staging bytes failed");
+  }
+  // rows 2i <- gate row i, 2i + 1 <- up row i; the same for the scale table
+  e = cudaMemcpy2DAsync(staging, 2 * rb, gate_packed_dev, rb, rb, out_dim,
+                        cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpy2DAsync(staging + rb, 2 * rb, up_packed_dev, rb, rb, out_dim,
+                          cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess)
+    e = obn::launch_repack_i2s(staging, L->w, 2 * out_dim, in_dim, L->m_pad, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(L->s_w, 0, sizeof(float) * L->m_pad, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpy2DAsync(L->s_w, 2 * sizeof(float), gate_scales_dev, sizeof(float),
+                          sizeof(float), out_dim, cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpy2DAsync(L->s_w + 1, 2 * sizeof(float), up_scales_dev, sizeof(float),
+                          sizeof(float), out_dim, cudaMemcpyDeviceToDevice, s);
+  if (e == cudaSuccess && norm_dev) {
+    e = cudaMalloc(&L->norm, sizeof(float) * in_dim);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(L->norm, norm_dev, sizeof(float) * in_dim, cudaMemcpyDeviceToDevice, s);
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // the staging rows are read by then
+  cudaFree(staging);
+  if (e != cudaSuccess) {
+    free_layer(L);
+    return cuda_fail(e, "creating gated BitLinear");
+  }
+  *out_layer = L;
+  return OBN_OK;
+}
+
 void obn_bitlinear_free(obn_bitlinear* layer) { free_layer(layer); }
 
 int obn_bitlinear_in_dim(const obn_bitlinear* layer) { return layer ? layer->in_dim : 0; }
@@ -553,6 +608,26 @@ int obn_attention_decode(const float* q, const void* k_cache, const void* v_cach
                                         head_dim, S_max, seq_len, scale, out, workspace,
                                         static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  return OBN_OK;
+}
+
+int obn_add(const float* a, const float* b, size_t count, float* y, void* stream) {
+  clear_error();
+  if (!a || !b || !y) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  cudaError_t e = obn::launch_add(a, b, count, y, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "add launch");
+  return OBN_OK;
+}
+
+int obn_embed_f16(const void* table, int vocab, int dim, const int32_t* ids, int n, float* y,
+                  void* stream) {
+  clear_error();
+  if (!table || !ids || !y) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (vocab <= 0 || dim <= 0 || n <= 0)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "vocab, dim and n must be positive");
+  cudaError_t e =
+      obn::launch_embed_f16(table, vocab, dim, ids, n, y, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "embedding launch");
   return OBN_OK;
 }
 

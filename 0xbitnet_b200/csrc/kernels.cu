@@ -13,6 +13,8 @@
 //  * The epilogue rounds in the order of the shader the reference would have
 //    dispatched (kernels.h: EpilogueOrder).
 #include "kernels.h"
+
+#include <cuda_fp16.h>
 #include "layout.cuh"
 #include "obn_common.cuh"
 
@@ -697,6 +699,61 @@ __global__ __launch_bounds__(256) void k_relu2_mul(const float4* __restrict__ gu
   }
 }
 }  // namespace
+
+namespace {
+__global__ __launch_bounds__(256) void k_add(const float4* __restrict__ a,
+                                             const float4* __restrict__ b, size_t n4,
+                                             const float* __restrict__ a1,
+                                             const float* __restrict__ b1, size_t count,
+                                             float4* __restrict__ y4, float* __restrict__ y1) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n4) {
+    const float4 u = a[i], v = b[i];
+    y4[i] = make_float4(__fadd_rn(u.x, v.x), __fadd_rn(u.y, v.y), __fadd_rn(u.z, v.z),
+                        __fadd_rn(u.w, v.w));
+  } else if (i - n4 < count - 4 * n4) {  // the tail of a count not divisible by 4
+    const size_t j = 4 * n4 + (i - n4);
+    y1[j] = __fadd_rn(a1[j], b1[j]);
+  }
+}
+
+__global__ __launch_bounds__(256) void k_embed_f16(const unsigned short* __restrict__ table,
+                                                   int vocab, int dim,
+                                                   const int32_t* __restrict__ ids, size_t total,
+                                                   float* __restrict__ y) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const size_t t = i / dim, c = i % dim;
+  const int id = ids[t];
+  y[i] = (id >= 0 && id < vocab)
+             ? __half2float(__ushort_as_half(table[static_cast<size_t>(id) * dim + c]))
+             : 0.0f;
+}
+}  // namespace
+
+cudaError_t launch_add(const float* a, const float* b, size_t count, float* y, cudaStream_t s) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                     reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  const size_t n4 = vec ? count / 4 : 0;
+  const size_t threads = n4 + (count - 4 * n4);
+  if (threads == 0) return cudaSuccess;
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  return launch_pdl(k_add, dim3(blocks), dim3(256), 0, s, reinterpret_cast<const float4*>(a),
+                    reinterpret_cast<const float4*>(b), n4, a, b, count,
+                    reinterpret_cast<float4*>(y), y);
+}
+
+cudaError_t launch_embed_f16(const void* table, int vocab, int dim, const int32_t* ids, int n,
+                             float* y, cudaStream_t s) {
+  const size_t total = static_cast<size_t>(n) * dim;
+  const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
+  return launch_pdl(k_embed_f16, dim3(blocks), dim3(256), 0, s,
+                    static_cast<const unsigned short*>(table), vocab, dim, ids, total, y);
+}
 
 cudaError_t launch_relu2_mul(const float* gu, int n, int d, float* y, cudaStream_t s) {
   const size_t total = static_cast<size_t>(n) * d;

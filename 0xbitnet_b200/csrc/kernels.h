@@ -38,6 +38,14 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int
 // for i < n * d (gu: [n, 2d], y: [n, d]).
 cudaError_t launch_relu2_mul(const float* gu, int n, int d, float* y, cudaStream_t s);
 
+// elementwise.wgsl op 0: y[i] = a[i] + b[i] (residual add), count elements.
+cudaError_t launch_add(const float* a, const float* b, size_t count, float* y, cudaStream_t s);
+
+// embedding.wgsl: y[t, :] = f32(table[ids[t], :]) for t < n (ids >= vocab give 0);
+// table [vocab, dim] binary16.
+cudaError_t launch_embed_f16(const void* table, int vocab, int dim, const int32_t* ids, int n,
+                             float* y, cudaStream_t s);
+
 // Decode-path matmul on CUDA cores (dp4a) for any n (tokens in groups of 8).
 // Writes y (float, `order` rounding) or, when acc != nullptr, exact int32 sums.
 cudaError_t launch_gemv(const WeightView& W, const int8_t* q, const float* s_x,

@@ -106,6 +106,13 @@ OBN_API void obn_bitlinear_free(obn_bitlinear* layer);
 
 /* Shape queries. */
 OBN_API int obn_bitlinear_in_dim(const obn_bitlinear* layer);
+/* obn_bitlinear_load_i2s_gated over device buffers, as obn_bitlinear_create is
+ * BitLinear::new over device buffers: gate / up packed I2_S rows [out_dim, in_dim/4]
+ * and their row scales [out_dim]. Synchronises `stream` before returning. */
+OBN_API int obn_bitlinear_create_gated(const void* gate_packed_dev, const float* gate_scales_dev,
+                                       const void* up_packed_dev, const float* up_scales_dev,
+                                       const float* norm_dev, float eps, int in_dim, int out_dim,
+                                       void* stream, obn_bitlinear** out_layer);
 OBN_API int obn_bitlinear_out_dim(const obn_bitlinear* layer);
 /* Weight rows the matmul entry points compute: out_dim, or 2 * out_dim for a
  * gated layer. */
@@ -201,6 +208,16 @@ OBN_API int obn_attention_decode(const float* q, const void* k_cache, const void
                                  int n, int H, int Hkv, int head_dim, int S_max, int seq_len,
                                  float scale, float* out, void* workspace,
                                  size_t workspace_bytes, void* stream);
+
+/* ---- decoder glue ------------------------------------------------------------- */
+/* Residual add (elementwise.wgsl op 0, TransformerBlock::forward's dispatch_add,
+ * transformer.rs:63,69): y[i] = a[i] + b[i] for i < count (f32; y may alias a or b). */
+OBN_API int obn_add(const float* a, const float* b, size_t count, float* y, void* stream);
+
+/* Token embedding lookup (embedding.wgsl): y[t, :] = f32(table[ids[t], :]) for t < n;
+ * ids outside [0, vocab) give zero rows. table [vocab, dim] binary16; ids int32 (device). */
+OBN_API int obn_embed_f16(const void* table, int vocab, int dim, const int32_t* ids, int n,
+                          float* y, void* stream);
 
 /* ---- kernel-level entry points (one per reference shader) ------------------ */
 
