@@ -55,6 +55,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--prefill", type=str, default="512,2048,8192",
                    help="config-2 token counts for the prefill TOPS block ('' to skip)")
+    p.add_argument("--no-decoder", dest="decoder", action="store_false",
+                   help="skip the config-3 decoder tok/s block")
     p.add_argument("--tp-tokens", type=int, default=16384,
                    help="config-4 tensor-parallel prefill tokens when run on N > 1 GPUs (0 skips)")
     p.add_argument("--case", type=str, default=None,
@@ -543,6 +545,55 @@ def measure_attention(dev, stream, peak, layers):
     return out
 
 
+def measure_decoder(dev, stream, world, rank, ctx=2048, total_batch=64):
+    """Config 3: one decode step of the random-init BitNet-2B-class decoder (30
+    layers, hidden 2560, FFN 6912 ReLU^2-gated, 20/5 heads x 128, RoPE 500000,
+    fp16 KV cache at context `ctx`, tied fp16 embedding / LM head, vocab 128256).
+    Batch 1 on every rank, and `total_batch` sequences sharded over the ranks
+    (total_batch / world each, no collective). tok/s = sequences / step time
+    (max over ranks for the sharded batch)."""
+    import torch
+    import torch.distributed as dist
+    D_ = importlib.import_module("0xbitnet_b200.decoder")
+    cfg = D_.DecoderConfig()
+    out = {"config": "30 layers, hidden 2560, FFN 6912, 20/5 heads x 128, vocab 128256, "
+                     "fp16 KV cache, context %d" % ctx, "per_batch": {}}
+    for B, sharded in ((1, False), (max(1, total_batch // world), True)):
+        m = D_.BitNetDecoder(cfg, B, ctx, device=dev, seed=70_000)
+        m.fill_caches(ctx - 1, seed=70_001)
+        with torch.cuda.stream(stream):
+            m.step(ctx - 1)  # warm-up outside the graph: workspaces
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                m.step(ctx - 1)
+            for _ in range(3):
+                g.replay()
+            stream.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            reps = 10
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+            stream.synchronize()
+            del g
+        ms = e0.elapsed_time(e1) / reps
+        if sharded and world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        key = "sharded_%d_over_%d_gpus" % (B * world, world) if sharded else "1"
+        seqs = B * world if sharded else B
+        out["per_batch"][key] = {"ms_per_step": ms, "tokens_per_s": seqs / (ms / 1e3),
+                                 "sequences": seqs}
+        m.close()
+        del m
+        torch.cuda.synchronize()
+    return out
+
+
 def measure_lm_head(obn, dev, stream, peak):
     """Next-row kernel: the f16 LM head of BitNet-2B (128256 x 2560, 656.7 MB) behind
     the final RMSNorm, one token as the reference runs it; the table exceeds L2, so
@@ -800,6 +851,7 @@ def run_ours(args):
     lm_head = measure_lm_head(obn, dev, stream, peak)
     ffn_gate_up = measure_ffn_gate_up(args, obn, synth, dev, stream, batches)
     attention = measure_attention(dev, stream, peak, min(args.layers, 30))
+    decoder = measure_decoder(dev, stream, world, rank) if args.decoder else None
     tp_prefill = None
     if world > 1 and args.tp_tokens > 0:
         tp_prefill = measure_tp_prefill(args, obn, synth, dev, stream, world, rank)
@@ -830,6 +882,7 @@ def run_ours(args):
             "lm_head": lm_head,
             "ffn_gate_up": ffn_gate_up,
             "attention_decode": attention,
+            "decode_tok_s": decoder,
             "cpu_baseline": cpu,
             "clocks": clock_info,
             "e2e": {"value": e2e_value, "unit": "GB/s",
