@@ -7,9 +7,10 @@ mirror. Import it with ``importlib.import_module("0xbitnet_b200")``.
 """
 from . import i2s
 from ._lib import LIB_PATH, ObnError, lib
-from .bitlinear import BitLinear, check_device_errors, lm_head_f16, rmsnorm, rmsnorm_quantize
+from .bitlinear import (BitLinear, check_device_errors, lm_head_f16, lm_head_f16_batched,
+                        rmsnorm, rmsnorm_quantize)
 
 lib()  # fail loudly at import when the CUDA library has not been built
 
-__all__ = ["BitLinear", "rmsnorm_quantize", "rmsnorm", "lm_head_f16", "check_device_errors", "ObnError",
+__all__ = ["BitLinear", "rmsnorm_quantize", "rmsnorm", "lm_head_f16", "lm_head_f16_batched", "check_device_errors", "ObnError",
            "LIB_PATH", "i2s", "lib"]

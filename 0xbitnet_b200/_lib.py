@@ -41,6 +41,8 @@ SIGNATURES = {
     "obn_bitlinear_forward_noalloc": (_I, [_P, _P, _I, _P, _P]),
     "obn_bitlinear_forward_tp": (_I, [_P, _P, _I, _P, _P, _I, _I, _I, _P, _SZ, _P]),
     "obn_lm_head_f16": (_I, [_P, _I, _I, _P, _P, _F, _I, _P, _P]),
+    "obn_lm_head_workspace_bytes": (_SZ, [_I, _I]),
+    "obn_lm_head_f16_batched": (_I, [_P, _I, _I, _P, _P, _F, _I, _P, _P, _SZ, _P]),
     "obn_rope_kv_append": (_I, [_P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _I, _P]),
     "obn_attention_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "obn_attention_decode": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _SZ, _P]),

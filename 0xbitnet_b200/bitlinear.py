@@ -268,6 +268,27 @@ def lm_head_f16(embed: torch.Tensor, x: torch.Tensor, norm_weight: torch.Tensor 
     return logits
 
 
+def lm_head_f16_batched(embed: torch.Tensor, x: torch.Tensor,
+                        norm_weight: torch.Tensor | None = None, eps: float = 1e-5,
+                        out: torch.Tensor | None = None,
+                        workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """lm_head_f16 for many tokens on the tensor cores (hi/lo f16 split)."""
+    if not (embed.is_cuda and embed.dtype == torch.float16 and embed.is_contiguous()):
+        raise TypeError("embed must be a contiguous float16 CUDA tensor")
+    _require_cuda_f32(x, "x")
+    vocab, dim = embed.shape
+    n = x.numel() // dim
+    logits = out if out is not None else torch.empty((n, vocab), dtype=torch.float32,
+                                                     device=x.device)
+    need = int(lib().obn_lm_head_workspace_bytes(n, dim))
+    ws = workspace if workspace is not None and workspace.numel() >= need else \
+        torch.empty(need, dtype=torch.uint8, device=x.device)
+    check(lib().obn_lm_head_f16_batched(_ptr(embed), vocab, dim, _ptr(x), _ptr(norm_weight),
+                                        ctypes.c_float(eps), n, _ptr(logits), _ptr(ws),
+                                        ws.numel(), _stream(x.device)))
+    return logits
+
+
 def check_device_errors() -> None:
     """Raises ObnError if a bounded in-kernel wait gave up since the last check."""
     check(lib().obn_check_device_errors())

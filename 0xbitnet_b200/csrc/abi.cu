@@ -555,6 +555,36 @@ int obn_lm_head_f16(const void* embed, int vocab, int dim, const float* x,
   return OBN_OK;
 }
 
+size_t obn_lm_head_workspace_bytes(int n, int dim) {
+  if (n <= 0 || dim <= 0) return 0;
+  return obn::lm_head_tc_workspace_bytes(n, dim);
+}
+
+int obn_lm_head_f16_batched(const void* embed, int vocab, int dim, const float* x,
+                            const float* norm_weight, float eps, int n, float* logits,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (!embed || !x || !logits || !workspace)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (vocab <= 0 || dim <= 0 || n <= 0)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "need vocab, dim and n > 0 (got %d, %d, %d)", vocab,
+                dim, n);
+  if (dim % 64 != 0)
+    return fail(OBN_ERR_UNSUPPORTED, "dim must be a multiple of 64 (got %d)", dim);
+  if (workspace_bytes < obn::lm_head_tc_workspace_bytes(n, dim))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than the %zu needed",
+                workspace_bytes, obn::lm_head_tc_workspace_bytes(n, dim));
+  if (!aligned(embed, 16) || !aligned(workspace, 256) || !aligned(x, 4) || !aligned(logits, 4))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "embed 16-byte and workspace 256-byte aligned");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (int rc = check_device(dev)) return rc;
+  cudaError_t e = obn::launch_lm_head_tc(embed, vocab, dim, x, norm_weight, eps, n, logits,
+                                         workspace, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "batched lm head launch");
+  return OBN_OK;
+}
+
 int obn_rope_kv_append(const float* qkv, int B, int n, int H, int Hkv, int head_dim, int pos,
                        float theta_base, float* q_out, void* k_cache, void* v_cache, int S_max,
                        void* stream) {

@@ -1,6 +1,8 @@
 // gemm.h — prefill / batched-decode ternary GEMM on the tcgen05 tensor cores.
 #pragma once
 
+#include <cuda.h>
+
 #include "kernels.h"
 
 namespace obn {
@@ -25,6 +27,13 @@ struct GatherOut {
   int col0 = 0;
   int vec4 = 0;  // ldy, col0, out_dim multiples of 4 and every base 16-byte aligned
 };
+
+// cuTensorMapEncodeTiled from the driver (null when unavailable).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn tensor_map_encoder();
 
 // True when launch_gemm handles this shape (otherwise the dp4a path runs).
 bool gemm_supported(const WeightView& W, int n);

@@ -14,4 +14,12 @@ cudaError_t launch_lm_head_f16(const void* embed, int V, int D, const float* x,
                                const float* gamma, float eps, int n, float* logits,
                                cudaStream_t s);
 
+// The same logits for many tokens on the tensor cores (kind::f16 with the
+// hidden rows split into f16 hi + lo; f32 accumulation in the tensor core's
+// order, not the shader's). workspace: lm_head_tc_workspace_bytes(n, D) bytes,
+// 256-byte aligned; D % 64 == 0.
+size_t lm_head_tc_workspace_bytes(int n, int D);
+cudaError_t launch_lm_head_tc(const void* embed, int V, int D, const float* x, const float* gamma,
+                              float eps, int n, float* logits, void* workspace, cudaStream_t s);
+
 }  // namespace obn

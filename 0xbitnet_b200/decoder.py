@@ -18,8 +18,9 @@ consumes them (numerically the same: rmsnorm then quantize), q/k/v are one
 merged 3840-row BitLinear with a per-row scale table, gate and up are one
 interleaved gated layer, and the KV cache is fp16. Every step is a fixed
 sequence of libobn launches on one stream, so it is captured as a CUDA graph.
-Weights are random (seeded) with the reference's distributions; no checkpoint
-is needed to measure speed.
+Batches above 4 tokens take the tensor-core LM head (f16 hi/lo split, f32
+accumulation) instead of the shader-order one. Weights are random (seeded)
+with the reference's distributions; no checkpoint is needed to measure speed.
 """
 from __future__ import annotations
 
@@ -30,7 +31,7 @@ import torch
 
 from . import attention as att
 from ._lib import check, lib
-from .bitlinear import BitLinear, lm_head_f16
+from .bitlinear import BitLinear, lm_head_f16, lm_head_f16_batched
 
 
 def _ptr(t):
@@ -139,6 +140,9 @@ class BitNetDecoder:
             self.ids = torch.zeros((B,), dtype=torch.int32, device=dev)
             self.attn_ws = torch.empty(max(1, int(lib().obn_attention_workspace_bytes(
                 B, 1, H, d, ctx))), dtype=torch.uint8, device=dev)
+            self.logits = torch.empty((B, cfg.vocab), **f32)
+            self.lm_ws = torch.empty(max(1, int(lib().obn_lm_head_workspace_bytes(B, D))),
+                                     dtype=torch.uint8, device=dev)
 
     def fill_caches(self, seq_len: int, seed: int = 1) -> None:
         """Stands in for a prefill: random fp16 keys/values at positions < seq_len."""
@@ -166,7 +170,10 @@ class BitNetDecoder:
             L.gate_up.forward(self.x, n=B, out=self.ffn_out)
             L.down.forward(self.ffn_out, n=B, out=self.down_out)
             check(lib().obn_add(_ptr(self.x), _ptr(self.down_out), B * D, _ptr(self.x), s))
-        return lm_head_f16(self.embed, self.x, self.final_norm, cfg.eps)
+        if B <= 4:  # the shader's exact order (the reference's own case is one token)
+            return lm_head_f16(self.embed, self.x, self.final_norm, cfg.eps)
+        return lm_head_f16_batched(self.embed, self.x, self.final_norm, cfg.eps,
+                                   out=self.logits, workspace=self.lm_ws)
 
     def close(self) -> None:
         for L in self.layers:

@@ -181,6 +181,17 @@ OBN_API int obn_lm_head_f16(const void* embed, int vocab, int dim, const float* 
                             const float* norm_weight, float eps, int n, float* logits,
                             void* stream);
 
+/* obn_lm_head_f16 for batches of tokens on the tensor cores: the same logits with
+ * the hidden rows split into binary16 hi + lo halves (y = hi + lo to 2^-22 |y|) and
+ * f32 accumulation in the tensor core's order instead of the shader's 256-lane tree
+ * (differences at the 1e-6 relative level; the reference itself only runs n = 1).
+ * dim % 64 == 0. workspace (256-byte aligned) holds obn_lm_head_workspace_bytes(n, dim)
+ * bytes. */
+OBN_API size_t obn_lm_head_workspace_bytes(int n, int dim);
+OBN_API int obn_lm_head_f16_batched(const void* embed, int vocab, int dim, const float* x,
+                                    const float* norm_weight, float eps, int n, float* logits,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- decode attention around the BitLinear path ----------------------------- */
 /* RoPE + KV-cache append (attention.rs:98-104: apply_rope on q and k, then
  * append_to_cache; rope.wgsl). qkv: [B*n, (H + 2*Hkv) * head_dim] f32, the merged QKV

@@ -23,14 +23,17 @@ def dec():
     return importlib.import_module("0xbitnet_b200.decoder")
 
 
-def test_decoder_step_matches_oracle():
+@pytest.mark.parametrize("B", [2, 6])
+def test_decoder_step_matches_oracle(B):
+    # B = 2: the shader-order LM head; B = 6: the tensor-core one
     torch = need_cuda()
     D_ = dec()
     cfg = D_.DecoderConfig(layers=2, hidden=512, ffn=1024, heads=4, kv_heads=2, vocab=1000)
-    B, ctx, pos = 2, 64, 10
+    ctx, pos = 64, 10
+    ids = [7, 999, 0, 5, 500, 123][:B]
     m = D_.BitNetDecoder(cfg, B, ctx, seed=3)
     m.fill_caches(pos, seed=4)
-    m.ids.copy_(torch.tensor([7, 999], dtype=torch.int32))
+    m.ids.copy_(torch.tensor(ids, dtype=torch.int32))
     caches = [(c.k.cpu().numpy().astype(np.float32), c.v.cpu().numpy().astype(np.float32))
               for c in m.caches]
     logits = m.step(pos).cpu().numpy()
@@ -38,7 +41,7 @@ def test_decoder_step_matches_oracle():
 
     H, Hkv, d, D, F = cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.hidden, cfg.ffn
     emb = m.embed.cpu().numpy()
-    x = emb[[7, 999]].astype(np.float32)
+    x = emb[ids].astype(np.float32)
     for L, (kc, vc) in zip(m.layers, caches):
         rows = L.qkv.export_i2s().cpu().numpy()
         sw = np.concatenate([np.full(n_, s_, np.float32) for n_, s_ in

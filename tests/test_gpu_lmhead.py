@@ -50,3 +50,24 @@ def test_lm_head_rejects_bad_dims():
         obn().lm_head_f16(torch.zeros((4, 12), dtype=torch.float16, device="cuda"),
                           torch.zeros((1, 12), device="cuda"))
     assert ei.value.code == E.OBN_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("V,D,n", [(1000, 2560, 8), (1000, 2560, 64), (777, 512, 100),
+                                   (1001, 512, 3), (300, 2560, 130), (128256, 2560, 64)])
+def test_lm_head_batched_tensor_cores(V, D, n):
+    # the tensor-core form: the same logits to f32 rounding (hi/lo f16 split of the
+    # normed hidden rows, tensor-core summation order), checked against the exact
+    # dot products of the oracle's normed rows
+    torch = need_cuda()
+    rng = np.random.default_rng(V + D + n)
+    embed = (rng.standard_normal((V, D)) * 0.05).astype(np.float16)
+    x = rng.standard_normal((n, D)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+    got = obn().lm_head_f16_batched(torch.from_numpy(embed).cuda(), torch.from_numpy(x).cuda(),
+                                    torch.from_numpy(g).cuda(), 1e-5).cpu().numpy()
+    y = orc.rmsnorm(x, g, 1e-5).astype(np.float64)
+    e64 = embed.astype(np.float64)
+    exact = y @ e64.T
+    l1 = np.abs(y) @ np.abs(e64).T
+    assert np.all(np.abs(got - exact) <= 2e-6 * l1 + 1e-7)
+    obn().check_device_errors()
