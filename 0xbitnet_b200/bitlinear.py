@@ -164,6 +164,19 @@ class BitLinear:
 
     __call__ = forward
 
+    def forward_residual(self, input: torch.Tensor, y: torch.Tensor,
+                         n: int | None = None) -> torch.Tensor:
+        """y += forward(input) in the matmul epilogue (the residual add after
+        o_proj / down_proj, transformer.rs:63,69); y [n, out_dim] f32."""
+        _require_cuda_f32(input, "input")
+        _require_cuda_f32(y, "y")
+        if n is None:
+            n = input.numel() // self.in_dim
+        ws = self._workspace(n)
+        check(lib().obn_bitlinear_forward_residual(self._h, _ptr(input), n, _ptr(y), _ptr(ws),
+                                                   ws.numel(), _stream(self.device)))
+        return y
+
     def forward_tp(self, input: torch.Tensor, out_total: int, col0: int,
                    out_mc: int | None = None, out_ranks: list[int] | None = None,
                    n: int | None = None) -> None:

@@ -432,8 +432,31 @@ int obn_rmsnorm(const float* x, const float* w, float eps, int n, int d, float* 
   return OBN_OK;
 }
 
+namespace {
+int forward_impl(const obn_bitlinear* layer, const float* x, int n, float* y, void* workspace,
+                 size_t workspace_bytes, void* stream, int accumulate);
+}  // namespace
+
 int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, int n, float* y,
                           void* workspace, size_t workspace_bytes, void* stream) {
+  return forward_impl(layer, x, n, y, workspace, workspace_bytes, stream, 0);
+}
+
+int obn_bitlinear_forward_residual(const obn_bitlinear* layer, const float* x, int n, float* y,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (layer && layer->gated)
+    return fail(OBN_ERR_UNSUPPORTED, "the residual forward does not take a gated FFN layer");
+  if (x && y && x == y)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "the residual forward needs y distinct from x");
+  return forward_impl(layer, x, n, y, workspace, workspace_bytes, stream, obn::kOutAccumulate);
+}
+
+}  // extern "C"
+
+namespace {
+int forward_impl(const obn_bitlinear* layer, const float* x, int n, float* y, void* workspace,
+                 size_t workspace_bytes, void* stream, int accumulate) {
   clear_error();
   if (int rc = check_layer(layer)) return rc;
   if (!x || !y || !workspace) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
@@ -456,12 +479,13 @@ int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, int n, flo
   auto s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (n == 1 && layer->in_dim <= obn::kGemvMaxK) {  // whole BitLinear in one kernel
-    e = obn::launch_bitlinear_n1(view(layer), layer->norm, layer->eps, x, ym, s);
+    e = obn::launch_bitlinear_n1(view(layer), layer->norm, layer->eps, x, ym, s, accumulate);
     if (e != cudaSuccess) return cuda_fail(e, "bitlinear (n=1) launch");
   } else {
     e = obn::launch_rmsnorm_quant(x, layer->norm, layer->eps, n, layer->in_dim, q, sc, qs, s);
     if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
-    const int order = n == 1 ? obn::kOrderGemv : obn::kOrderGemm;  // bitlinear.rs:90-94
+    const int order =
+        (n == 1 ? obn::kOrderGemv : obn::kOrderGemm) | accumulate;  // bitlinear.rs:90-94
     if (obn::gemm_supported(view(layer), n))
       e = obn::launch_gemm(view(layer), q, sc, qs, n, ym, nullptr, order, s);
     else if (layer->in_dim <= obn::kGemvMaxK)
@@ -476,6 +500,9 @@ int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, int n, flo
   }
   return OBN_OK;
 }
+}  // namespace
+
+extern "C" {
 
 int obn_bitlinear_forward_tp(const obn_bitlinear* layer, const float* x, int n, float* y_mc,
                              float* const* y_ranks, int world, int out_total, int col0,

@@ -340,7 +340,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
             const int qs_j = __shfl_sync(0xffffffffu, qs_l, j);
             const float sx_j = __shfl_sync(0xffffffffu, sx_l, j);
             const float fd = static_cast<float>(static_cast<int>(v[j]) - qs_j);
-            st[j * 32 + lane] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx_j)
+            st[j * 32 + lane] = (order & 1) == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx_j)
                                                     : __fmul_rn(fd, __fmul_rn(sw, sx_j));
           }
           __syncwarp();
@@ -377,10 +377,10 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
               acc_out[o] = d;
             } else {
               const float fd = static_cast<float>(d);
-              const float val = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx_j)
-                                                    : __fmul_rn(fd, __fmul_rn(sw, sx_j));
+              const float val = (order & 1) == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx_j)
+                                                          : __fmul_rn(fd, __fmul_rn(sw, sx_j));
               if constexpr (OUT == kOutLocal) {
-                y[o] = val;
+                y[o] = (order & kOutAccumulate) ? __fadd_rn(y[o], val) : val;
               } else {
                 const size_t og = static_cast<size_t>(n) * go.ldy + go.col0 + m;
                 if constexpr (OUT == kOutMulticast) {
@@ -792,8 +792,9 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
         } else {
           const float fd = static_cast<float>(d);
           const float sx = e_sx[j];
-          y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx)
-                                     : __fmul_rn(fd, __fmul_rn(sw, sx));
+          const float val = (order & 1) == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx)
+                                                      : __fmul_rn(fd, __fmul_rn(sw, sx));
+          y[o] = (order & kOutAccumulate) ? __fadd_rn(y[o], val) : val;
         }
       }
     }

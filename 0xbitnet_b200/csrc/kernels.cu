@@ -412,7 +412,9 @@ __global__ __launch_bounds__(kGemvWarps * 32) void k_gemv(
       } else {
         const float fa = static_cast<float>(a);
         const float sw = s_w[m], sx = sx_s[t];
-        y[o] = order == kOrderGemv ? __fmul_rn(__fmul_rn(fa, sw), sx) : __fmul_rn(fa, __fmul_rn(sw, sx));
+        const float val = (order & 1) == kOrderGemv ? __fmul_rn(__fmul_rn(fa, sw), sx)
+                                                    : __fmul_rn(fa, __fmul_rn(sw, sx));
+        y[o] = (order & kOutAccumulate) ? __fadd_rn(y[o], val) : val;
       }
     }
   }
@@ -437,7 +439,7 @@ template <int EPT>
 __global__ __launch_bounds__(256) void k_bitlinear_n1(
     const uint8_t* __restrict__ W, const float* __restrict__ s_w,
     const float* __restrict__ gamma, float eps, const float* __restrict__ x,
-    float* __restrict__ y, int M, int K) {
+    float* __restrict__ y, int M, int K, int accumulate) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ float shf[256];
@@ -554,7 +556,8 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
 #pragma unroll
     for (int w = 0; w < 4; ++w) a += red[sb * 4 + w][r];
     // ternary_gemv.wgsl:232 order: (f32(acc) * s_w) * s_x
-    y[row] = __fmul_rn(__fmul_rn(static_cast<float>(a), sw), scal[1]);
+    const float val = __fmul_rn(__fmul_rn(static_cast<float>(a), sw), scal[1]);
+    y[row] = accumulate ? __fadd_rn(y[row], val) : val;
   }
 }
 
@@ -598,7 +601,7 @@ cudaError_t gemv_nt(const WeightView& W, const int8_t* q, const float* s_x, cons
 
 template <int EPT>
 cudaError_t bitlinear_n1_ept(const WeightView& W, const float* gamma, float eps, const float* x,
-                             float* y, cudaStream_t s) {
+                             float* y, int accumulate, cudaStream_t s) {
   const int K = W.in_dim;
   const size_t smem =
       2 * static_cast<size_t>(K / kBlockK) * kSubtileBytes + static_cast<size_t>(K) * 5;
@@ -606,7 +609,8 @@ cudaError_t bitlinear_n1_ept(const WeightView& W, const float* gamma, float eps,
   cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return e;
   dim3 grid((W.out_dim + kN1Rows - 1) / kN1Rows);
-  return launch_pdl(kern, grid, dim3(256), smem, s, W.w, W.s_w, gamma, eps, x, y, W.out_dim, K);
+  return launch_pdl(kern, grid, dim3(256), smem, s, W.w, W.s_w, gamma, eps, x, y, W.out_dim, K,
+                    accumulate);
 }
 
 template <bool ACC>
@@ -770,22 +774,22 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int
 }
 
 cudaError_t launch_bitlinear_n1(const WeightView& W, const float* gamma, float eps,
-                                const float* x, float* y, cudaStream_t s) {
+                                const float* x, float* y, cudaStream_t s, int accumulate) {
   const int ept = (W.in_dim + 255) / 256;
-  if (ept <= 1) return bitlinear_n1_ept<1>(W, gamma, eps, x, y, s);
-  if (ept <= 2) return bitlinear_n1_ept<2>(W, gamma, eps, x, y, s);
-  if (ept <= 4) return bitlinear_n1_ept<4>(W, gamma, eps, x, y, s);
-  if (ept <= 8) return bitlinear_n1_ept<8>(W, gamma, eps, x, y, s);
-  if (ept <= 12) return bitlinear_n1_ept<12>(W, gamma, eps, x, y, s);
-  if (ept <= 16) return bitlinear_n1_ept<16>(W, gamma, eps, x, y, s);
-  if (ept <= 20) return bitlinear_n1_ept<20>(W, gamma, eps, x, y, s);
-  if (ept <= 24) return bitlinear_n1_ept<24>(W, gamma, eps, x, y, s);
-  if (ept <= 28) return bitlinear_n1_ept<28>(W, gamma, eps, x, y, s);
-  if (ept <= 32) return bitlinear_n1_ept<32>(W, gamma, eps, x, y, s);
-  if (ept <= 40) return bitlinear_n1_ept<40>(W, gamma, eps, x, y, s);
-  if (ept <= 48) return bitlinear_n1_ept<48>(W, gamma, eps, x, y, s);
-  if (ept <= 56) return bitlinear_n1_ept<56>(W, gamma, eps, x, y, s);
-  if (ept <= 64) return bitlinear_n1_ept<64>(W, gamma, eps, x, y, s);
+  if (ept <= 1) return bitlinear_n1_ept<1>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 2) return bitlinear_n1_ept<2>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 4) return bitlinear_n1_ept<4>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 8) return bitlinear_n1_ept<8>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 12) return bitlinear_n1_ept<12>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 16) return bitlinear_n1_ept<16>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 20) return bitlinear_n1_ept<20>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 24) return bitlinear_n1_ept<24>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 28) return bitlinear_n1_ept<28>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 32) return bitlinear_n1_ept<32>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 40) return bitlinear_n1_ept<40>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 48) return bitlinear_n1_ept<48>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 56) return bitlinear_n1_ept<56>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 64) return bitlinear_n1_ept<64>(W, gamma, eps, x, y, accumulate, s);
   return cudaErrorInvalidValue;
 }
 

@@ -11,6 +11,9 @@ namespace obn {
 enum EpilogueOrder : int {
   kOrderGemv = 0,  // (f32(acc) * s_w[m]) * s_x[t]      ternary_gemv.wgsl:232
   kOrderGemm = 1,  // f32(acc) * (s_w[m] * s_x[t])      ternary_gemm.wgsl:132-133
+  // OR-ed into the order: y += the result (the residual add that follows the
+  // layer in the reference, elementwise.wgsl op 0), y = y + val rounded once.
+  kOutAccumulate = 2,
 };
 
 struct WeightView {
@@ -54,7 +57,8 @@ cudaError_t launch_gemv(const WeightView& W, const int8_t* q, const float* s_x,
 // One-token BitLinear forward in a single kernel (RMSNorm when gamma != null,
 // quantize, GEMV with ternary_gemv.wgsl's epilogue order). K <= kGemvMaxK.
 cudaError_t launch_bitlinear_n1(const WeightView& W, const float* gamma, float eps,
-                                const float* x, float* y, cudaStream_t s);
+                                const float* x, float* y, cudaStream_t s,
+                                int accumulate = 0);
 
 // Largest K the GEMV kernels accept.
 constexpr int kGemvMaxK = 16384;

@@ -14,7 +14,9 @@ model.rs:200-262 and transformer.rs:51-72) for one new token per sequence:
     logits = LM head (tied f16 embedding) of RMSNorm(x; final norm)
 
 B200 form: the block RMSNorms are the fused RMSNorm of the BitLinear that
-consumes them (numerically the same: rmsnorm then quantize), q/k/v are one
+consumes them (numerically the same: rmsnorm then quantize), the residual adds
+happen in the o_proj / down_proj epilogues (x + y rounded once, as the add
+kernel would), q/k/v are one
 merged 3840-row BitLinear with a per-row scale table, gate and up are one
 interleaved gated layer, and the KV cache is fp16. Every step is a fixed
 sequence of libobn launches on one stream, so it is captured as a CUDA graph.
@@ -165,11 +167,9 @@ class BitNetDecoder:
             L.qkv.forward(self.x, n=B, out=self.qkv_out)
             att.rope_kv_append(self.qkv_out, c, H, 1, cfg.rope_theta, q_out=self.q, pos=pos)
             att.attention(self.q, c, H, 1, pos + 1, out=self.attn, workspace=self.attn_ws)
-            L.o.forward(self.attn, n=B, out=self.o_out)
-            check(lib().obn_add(_ptr(self.x), _ptr(self.o_out), B * D, _ptr(self.x), s))
+            L.o.forward_residual(self.attn, self.x, n=B)  # x += o_proj(attn)
             L.gate_up.forward(self.x, n=B, out=self.ffn_out)
-            L.down.forward(self.ffn_out, n=B, out=self.down_out)
-            check(lib().obn_add(_ptr(self.x), _ptr(self.down_out), B * D, _ptr(self.x), s))
+            L.down.forward_residual(self.ffn_out, self.x, n=B)  # x += down(ffn)
         if B <= 4:  # the shader's exact order (the reference's own case is one token)
             return lm_head_f16(self.embed, self.x, self.final_norm, cfg.eps)
         return lm_head_f16_batched(self.embed, self.x, self.final_norm, cfg.eps,

@@ -131,6 +131,15 @@ OBN_API size_t obn_bitlinear_workspace_bytes(const obn_bitlinear* layer, int n);
 OBN_API int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, int n, float* y,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* BitLinear::forward followed by the residual add the reference dispatches after
+ * o_proj and down_proj (TransformerBlock::forward, transformer.rs:63,69;
+ * elementwise.wgsl op 0): y[t, m] = y[t, m] + forward(x)[t, m], the sum rounded
+ * once, in the matmul's epilogue (no separate add kernel). y must not alias x.
+ * Not for gated layers. Same workspace as obn_bitlinear_forward. */
+OBN_API int obn_bitlinear_forward_residual(const obn_bitlinear* layer, const float* x, int n,
+                                           float* y, void* workspace, size_t workspace_bytes,
+                                           void* stream);
+
 /* No counterpart in the reference. obn_bitlinear_forward for callers that cannot
  * allocate device memory: hosts whose device memory is reserved up front by
  * another allocator, and latency-critical threads that must not call

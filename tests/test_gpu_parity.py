@@ -316,3 +316,18 @@ def test_error_paths_on_gpu(torch):
 def test_no_device_wait_gave_up(torch):
     torch.cuda.synchronize()
     obn().check_device_errors()
+
+
+@pytest.mark.parametrize("M,K,n", [(2560, 2560, 1), (2560, 6912, 3), (2560, 2560, 8),
+                                   (2560, 6912, 64), (3000, 512, 300)])
+def test_forward_residual_is_forward_plus_add(M, K, n):
+    # y += forward(x) in the epilogue equals forward(x) then the f32 add, bit for bit
+    torch = need_cuda()
+    L = synth().layer(M + K + n, M, K)
+    layer = obn().BitLinear.from_i2s(L.blob(), K, M, norm_weight=L.gamma)
+    x = torch.from_numpy(synth().activations(n + 1, n, K)).cuda()
+    y0 = torch.from_numpy(synth().activations(n + 2, n, M)).cuda()
+    want = (y0 + layer.forward(x)).cpu().numpy()
+    y = y0.clone()
+    layer.forward_residual(x, y)
+    assert np.array_equal(y.cpu().numpy(), want)
