@@ -61,8 +61,8 @@ def parse_args():
                    help="config-4 tensor-parallel prefill tokens when run on N > 1 GPUs (0 skips)")
     p.add_argument("--case", type=str, default=None,
                    help="SHAPE:B — run a few forwards of one 2B shape (or of 'all' five in "
-                        "turn) at B tokens and exit (a small, self-contained workload for ncu "
-                        "captures)")
+                        "turn; or 'lmhead' / 'attn') at B tokens and exit (a small, "
+                        "self-contained workload for ncu captures)")
     return p.parse_args()
 
 
@@ -906,6 +906,29 @@ def run_case(spec: str):
     synth = importlib.import_module("0xbitnet_b200.synthetic")
     name, B = spec.split(":")
     B = int(B)
+    if name == "lmhead":  # the 128256 x 2560 f16 LM head, B tokens, 3 launches
+        g = torch.Generator(device="cuda")
+        g.manual_seed(5)
+        embed = (torch.randn(128256, 2560, generator=g, device="cuda") * 0.05).half()
+        x = torch.randn(B, 2560, generator=g, device="cuda")
+        gamma = torch.ones(2560, device="cuda")
+        for _ in range(3):
+            (obn.lm_head_f16 if B <= 4 else obn.lm_head_f16_batched)(embed, x, gamma)
+        torch.cuda.synchronize()
+        obn.check_device_errors()
+        print(f"case lmhead B={B}: ok")
+        return
+    if name == "attn":  # decode attention, 5 KV heads, context 2048, B sequences, 3 steps
+        att = importlib.import_module("0xbitnet_b200.attention")
+        cache = att.KVCache(B, 2048, 5, 128)
+        cache.k.normal_()
+        cache.v.normal_()
+        q = torch.randn(B, 20 * 128, device="cuda")
+        for _ in range(3):
+            att.attention(q, cache, 20, 1, 2048)
+        torch.cuda.synchronize()
+        print(f"case attn B={B}: ok")
+        return
     names = list(synth.SHAPES_2B) if name == "all" else [name]
     for nm in names:
         M, K = synth.SHAPES_2B[nm]
