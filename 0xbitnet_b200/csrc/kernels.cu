@@ -427,11 +427,21 @@ __global__ __launch_bounds__(kGemvWarps * 32) void k_gemv(
 // subtiles, 256 threads) normalises and quantizes the token itself; that keeps
 // the whole BitLinear to one launch and one dependent round trip. Before the
 // PDL wait the CTA prefetches everything that does not depend on earlier
-// kernels: its packed weights and the RMSNorm gamma (bulk copies into shared
-// memory) and its row scales. After the wait, thread t loads x[t + 256 j] —
-// exactly the columns lane t of rmsnorm.wgsl / quantize.wgsl owns — so the sum
-// of squares is reduced in the shaders' order (tree_sum_256) and q matches
-// bit for bit. The scalar divisions run once (thread 0) and are broadcast.
+// kernels: its packed weights (one bulk copy into shared memory), its row
+// scales and, in registers, the RMSNorm gamma of the columns each thread owns.
+//
+// After the wait the kernel is latency-bound (a chain of dependent steps that
+// is several times longer than streaming the CTA's weights), so the chain is
+// cut to four block barriers. Thread t owns columns t + 256j, the columns lane
+// t of rmsnorm.wgsl / quantize.wgsl owns, so its sum of squares is that lane's
+// partial (and its loads are coalesced). The partials meet in shared memory
+// once; then every warp finishes the shaders' halving tree by itself: lane l
+// folds strides 128, 64, 32 from eight partials in the tree's order, shuffles
+// do strides 16 .. 1, and every thread computes 1/rms, so no broadcast barrier
+// follows. The absmax takes a second barrier, the quantized row a third, the
+// row sums the last. In the dot product each warp covers both subtiles over
+// every eighth 128-column block, so one q vector read from shared memory feeds
+// two rows.
 // ---------------------------------------------------------------------------
 constexpr int kN1Rows = 32;  // rows per CTA (two subtiles)
 
@@ -442,40 +452,40 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
     float* __restrict__ y, int M, int K, int accumulate) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
-  __shared__ float shf[256];
-  __shared__ float scal[4];  // rms, scale, inv
-  __shared__ int red[8][16];
-  __shared__ int red_q[8];
-  __shared__ int ok_s;
+  __shared__ float sh_ss[256];  // per thread: sum of squares of its columns
+  __shared__ float sh_max[8];  // per warp: max |normalised x|
+  __shared__ int red_q[8];     // per warp: sum of q
+  __shared__ int red[8][2][16];
 
   const int KB = K / kBlockK;
-  const int S0 = blockIdx.x * 2;                  // first subtile
+  const int S0 = blockIdx.x * 2;  // first subtile
   const int nsub = min(2, (M + kSubRows - 1) / kSubRows - S0);
   if (nsub <= 0) return;  // uniform per CTA; the launcher never makes such CTAs
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  uint8_t* w_s = smem;                                                   // nsub * KB * 512
-  float* g_s = reinterpret_cast<float*>(smem + 2 * KB * kSubtileBytes);  // K floats
-  int8_t* q_s = reinterpret_cast<int8_t*>(g_s + K);                      // K bytes
+  uint8_t* w_s = smem;                                                     // 2 * KB * 512
+  int8_t* q_s = reinterpret_cast<int8_t*>(smem + 2 * KB * kSubtileBytes);  // K bytes
 
   if (tid == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  if (warp == 0) {
-    if (lane == 0) {  // both subtiles are one contiguous run in the T16 layout
-      const uint32_t gbytes = gamma ? static_cast<uint32_t>(K) * 4u : 0u;
-      const uint32_t wbytes = static_cast<uint32_t>(nsub * KB) * kSubtileBytes;
-      mbar_arrive_expect_tx(&bar, wbytes + gbytes);
-      bulk_g2s_hint(w_s, W + subtile_offset(S0, 0, KB), wbytes, &bar, policy_evict_first());
-      if (gamma) bulk_g2s(g_s, gamma, gbytes, &bar);
-    }
-    __syncwarp();
+  if (tid == 0) {  // both subtiles are one contiguous run in the T16 layout
+    const uint32_t wbytes = static_cast<uint32_t>(nsub * KB) * kSubtileBytes;
+    mbar_arrive_expect_tx(&bar, wbytes);
+    bulk_g2s_hint(w_s, W + subtile_offset(S0, 0, KB), wbytes, &bar, policy_evict_first());
   }
   const int row = S0 * kSubRows + tid;
-  const float sw = (tid < kN1Rows && row < M) ? s_w[row] : 0.0f;
+  const bool row_thread = tid < kN1Rows && row < M;
+  const float sw = row_thread ? s_w[row] : 0.0f;
+  float gv[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int col = tid + 256 * j;
+    gv[j] = (gamma != nullptr && col < K) ? gamma[col] : 1.0f;
+  }
   pdl_launch_dependents();
-  pdl_wait();  // x may be the previous kernel's output
+  pdl_wait();  // x, and y when accumulating, may be the previous kernel's output
 
   float xv[EPT];
 #pragma unroll
@@ -483,48 +493,41 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
     const int col = tid + 256 * j;
     xv[j] = col < K ? x[col] : 0.0f;
   }
-  if (warp == 0) {
-    if (lane == 0) {
-      bool ok = mbar_wait(&bar, 0);  // weights + gamma (normally landed long ago)
-      if (!ok) mbar_wait(&bar, 0);
-      ok_s = ok;
-    }
-    __syncwarp();
-  }
-  __syncthreads();
+  const float y_old = (accumulate && row_thread) ? y[row] : 0.0f;  // x != y (host check)
+
   float rms = 1.0f;
   if (gamma) {
     float part = 0.0f;
 #pragma unroll
     for (int j = 0; j < EPT; ++j)
       if (tid + 256 * j < K) part = __fadd_rn(part, __fmul_rn(xv[j], xv[j]));
-    const float total = tree_sum_256(part, shf);
-    if (tid == 0)
-      scal[0] =
-          __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), eps)));
+    sh_ss[tid] = part;
     __syncthreads();
-    rms = scal[0];
+    // lane l: strides 128, 64, 32 of the tree for shader lane l, then 16 .. 1
+    const float* p = sh_ss + lane;
+    const float b0 = __fadd_rn(__fadd_rn(p[0], p[128]), __fadd_rn(p[64], p[192]));
+    const float b1 = __fadd_rn(__fadd_rn(p[32], p[160]), __fadd_rn(p[96], p[224]));
+    float tsum = __fadd_rn(b0, b1);
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1)
+      tsum = __fadd_rn(tsum, __shfl_down_sync(0xffffffffu, tsum, s));
+    const float total = __shfl_sync(0xffffffffu, tsum, 0);
+    rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), eps)));
   }
   float lmax = 0.0f;
 #pragma unroll
   for (int j = 0; j < EPT; ++j) {
-    const int col = tid + 256 * j;
-    if (gamma && col < K) xv[j] = norm_mul(xv[j], rms, g_s[col]);
+    if (gamma && tid + 256 * j < K) xv[j] = norm_mul(xv[j], rms, gv[j]);
     lmax = fmaxf(lmax, fabsf(xv[j]));
   }
 #pragma unroll
   for (int s = 16; s >= 1; s >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, s));
-  if (lane == 0) shf[warp] = lmax;
+  if (lane == 0) sh_max[warp] = lmax;
   __syncthreads();
-  if (tid == 0) {
-    float absmax = shf[0];
+  float absmax = sh_max[0];
 #pragma unroll
-    for (int w = 1; w < 8; ++w) absmax = fmaxf(absmax, shf[w]);
-    scal[1] = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
-    scal[2] = absmax == 0.0f ? 0.0f : __fdiv_rn(127.0f, absmax);
-  }
-  __syncthreads();
-  const float inv = scal[2];
+  for (int w = 1; w < 8; ++w) absmax = fmaxf(absmax, sh_max[w]);
+  const float inv = absmax == 0.0f ? 0.0f : __fdiv_rn(127.0f, absmax);
   int qpart = 0;
 #pragma unroll
   for (int j = 0; j < EPT; ++j) {
@@ -538,26 +541,50 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
 #pragma unroll
   for (int s = 16; s >= 1; s >>= 1) qpart += __shfl_xor_sync(0xffffffffu, qpart, s);
   if (lane == 0) red_q[warp] = qpart;
+  const bool ok = mbar_wait(&bar, 0);  // the weights (normally landed long ago)
+  if (!ok) mbar_wait(&bar, 0);         // copies may still be in flight: once more, bounded
   __syncthreads();
 
-  const int sub = warp >> 2;  // warps 0-3: subtile 0, warps 4-7: subtile 1
-  int acc[1] = {0};
-  if (ok_s && sub < nsub)
-    subtile_dot<1>(smem_u32(w_s) + sub * KB * kSubtileBytes, smem_u32(q_s), K, KB, warp & 3,
-                   4, lane, acc);
-  acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 16);
-  if (lane < 16) red[warp][lane] = acc[0];
+  // Subtile 1 of a one-subtile CTA reads allocated but unwritten shared memory;
+  // those rows are >= M and never stored.
+  int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+  if (ok) {
+    const uint32_t w0 = smem_u32(w_s) + lane * 16;
+    const uint32_t w1 = w0 + KB * kSubtileBytes;
+    const uint32_t qb = smem_u32(q_s) + (lane >> 4) * 16;
+#pragma unroll 2
+    for (int b = warp; b < KB; b += 8) {
+      const uint4 wa = lds128(w0 + b * kSubtileBytes);
+      const uint4 wb = lds128(w1 + b * kSubtileBytes);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const uint32_t mask = 0xC0C0C0C0u >> (2 * g);
+        const uint4 xa = lds128(qb + b * kBlockK + 32 * g);
+        a0[g] = dp4a_us(wa.w & mask, xa.w, dp4a_us(wa.z & mask, xa.z,
+                dp4a_us(wa.y & mask, xa.y, dp4a_us(wa.x & mask, xa.x, a0[g]))));
+        a1[g] = dp4a_us(wb.w & mask, xa.w, dp4a_us(wb.z & mask, xa.z,
+                dp4a_us(wb.y & mask, xa.y, dp4a_us(wb.x & mask, xa.x, a1[g]))));
+      }
+    }
+  }
+  int acc0 = (a0[0] >> 6) + (a0[1] >> 4) + (a0[2] >> 2) + a0[3];
+  int acc1 = (a1[0] >> 6) + (a1[1] >> 4) + (a1[2] >> 2) + a1[3];
+  acc0 += __shfl_xor_sync(0xffffffffu, acc0, 16);
+  acc1 += __shfl_xor_sync(0xffffffffu, acc1, 16);
+  if (lane < 16) {
+    red[warp][0][lane] = acc0;
+    red[warp][1][lane] = acc1;
+  }
   __syncthreads();
-  if (tid < kN1Rows && row < M && ok_s) {
+  if (row_thread && ok) {
     const int sb = tid >> 4, r = tid & 15;
     int a = 0;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) a -= red_q[w];
-#pragma unroll
-    for (int w = 0; w < 4; ++w) a += red[sb * 4 + w][r];
+    for (int w = 0; w < 8; ++w) a += red[w][sb][r] - red_q[w];
+    const float scale = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
     // ternary_gemv.wgsl:232 order: (f32(acc) * s_w) * s_x
-    const float val = __fmul_rn(__fmul_rn(static_cast<float>(a), sw), scal[1]);
-    y[row] = accumulate ? __fadd_rn(y[row], val) : val;
+    const float val = __fmul_rn(__fmul_rn(static_cast<float>(a), sw), scale);
+    y[row] = accumulate ? __fadd_rn(y_old, val) : val;
   }
 }
 
@@ -604,7 +631,7 @@ cudaError_t bitlinear_n1_ept(const WeightView& W, const float* gamma, float eps,
                              float* y, int accumulate, cudaStream_t s) {
   const int K = W.in_dim;
   const size_t smem =
-      2 * static_cast<size_t>(K / kBlockK) * kSubtileBytes + static_cast<size_t>(K) * 5;
+      2 * static_cast<size_t>(K / kBlockK) * kSubtileBytes + static_cast<size_t>(K);
   auto kern = k_bitlinear_n1<EPT>;
   cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kern), smem);
   if (e != cudaSuccess) return e;
