@@ -36,6 +36,9 @@ SIGNATURES = {
     "obn_bitlinear_rows": (_I, [_P]),
     "obn_bitlinear_create_gated": (_I, [_P, _P, _P, _P, _P, _F, _I, _I, _P, ctypes.POINTER(_P)]),
     "obn_bitlinear_load_i2s_gated": (_I, [_P, _SZ, _P, _SZ, _I, _I, _P, _F, _I, ctypes.POINTER(_P)]),
+    "obn_bitlinear_load_i2s_concat": (_I, [_I, _P, _P, _P, _I, _P, _F, _I, ctypes.POINTER(_P)]),
+    "obn_bitlinear_set_activation": (_I, [_P, _I]),
+    "obn_activation": (_I, [_P, _SZ, _I, _P, _P]),
     "obn_bitlinear_workspace_bytes": (_SZ, [_P, _I]),
     "obn_bitlinear_forward": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "obn_bitlinear_forward_noalloc": (_I, [_P, _P, _I, _P, _P]),

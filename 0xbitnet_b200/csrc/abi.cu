@@ -22,7 +22,8 @@ struct obn_bitlinear {
   int in_dim = 0;   // K
   int out_dim = 0;  // output features of the forward
   int rows = 0;     // weight rows the matmul computes (2 * out_dim when gated)
-  int gated = 0;    // merged gate|up FFN projection: forward = relu(gate)^2 * up
+  int gated = 0;    // merged gate|up FFN projection: forward = act(gate) * up
+  int act = 0;      // gated activation: 0 = ReLU^2, 1 = SiLU
   int m_pad = 0;
   float eps = 1e-5f;
   uint8_t* w = nullptr;     // T16 layout, m_pad * K / 4 bytes
@@ -195,6 +196,86 @@ int obn_bitlinear_load_i2s(const uint8_t* i2s_tensor, size_t nbytes, int in_dim,
     return cuda_fail(e, "loading I2_S tensor");
   }
   *out_layer = L;
+  return OBN_OK;
+}
+
+int obn_bitlinear_load_i2s_concat(int count, const uint8_t* const* tensors, const size_t* nbytes,
+                                  const int* out_dims, int in_dim, const float* norm_weight,
+                                  float eps, int device, obn_bitlinear** out_layer) {
+  clear_error();
+  if (!tensors || !nbytes || !out_dims || !out_layer)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  *out_layer = nullptr;
+  if (count <= 0 || count > 64) return fail(OBN_ERR_INVALID_ARGUMENT, "count %d out of range", count);
+  const size_t row_bytes = static_cast<size_t>(in_dim) / 4;
+  long long total = 0;
+  for (int t = 0; t < count; ++t) {
+    if (!tensors[t]) return fail(OBN_ERR_INVALID_ARGUMENT, "tensor %d is NULL", t);
+    if (out_dims[t] <= 0) return fail(OBN_ERR_INVALID_ARGUMENT, "out_dims[%d] = %d", t, out_dims[t]);
+    const size_t packed = static_cast<size_t>(out_dims[t]) * row_bytes;
+    if (nbytes[t] < packed + 32)  // loader.rs:109-110: ceil(n/4) + 32 bytes
+      return fail(OBN_ERR_INVALID_ARGUMENT,
+                  "I2_S tensor %d of %dx%d needs %zu bytes (packed + 32-byte scale), got %zu", t,
+                  out_dims[t], in_dim, packed + 32, nbytes[t]);
+    total += out_dims[t];
+  }
+  if (total > (1 << 29)) return fail(OBN_ERR_INVALID_ARGUMENT, "%lld rows too many", total);
+  const int out_dim = static_cast<int>(total);
+  if (int rc = check_dims(in_dim, out_dim)) return rc;
+  if (int rc = check_device(device)) return rc;
+  DeviceGuard g(device);
+  obn_bitlinear* L = nullptr;
+  if (int rc = alloc_layer(in_dim, out_dim, eps, &L)) return rc;
+  uint8_t* staging = nullptr;
+  cudaError_t e = cudaMalloc(&staging, static_cast<size_t>(out_dim) * row_bytes);
+  if (e != cudaSuccess) {
+    free_layer(L);
+    cudaGetLastError();
+    return fail(OBN_ERR_OUT_OF_MEMORY, "cudaMalloc of staging bytes failed");
+  }
+  std::vector<float> table(L->m_pad, 0.0f);
+  size_t row0 = 0;
+  for (int t = 0; t < count && e == cudaSuccess; ++t) {
+    const size_t packed = static_cast<size_t>(out_dims[t]) * row_bytes;
+    float scale;  // loader.rs:129-131: first f32 of the trailing 32 bytes
+    std::memcpy(&scale, tensors[t] + packed, sizeof(float));
+    for (int m = 0; m < out_dims[t]; ++m) table[row0 + m] = scale;
+    e = cudaMemcpy(staging + row0 * row_bytes, tensors[t], packed, cudaMemcpyHostToDevice);
+    row0 += out_dims[t];
+  }
+  if (e == cudaSuccess) e = obn::launch_repack_i2s(staging, L->w, out_dim, in_dim, L->m_pad, 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(L->s_w, table.data(), sizeof(float) * L->m_pad, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && norm_weight) {
+    e = cudaMalloc(&L->norm, sizeof(float) * in_dim);
+    if (e == cudaSuccess)
+      e = cudaMemcpy(L->norm, norm_weight, sizeof(float) * in_dim, cudaMemcpyHostToDevice);
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(staging);
+  if (e != cudaSuccess) {
+    free_layer(L);
+    return cuda_fail(e, "loading concatenated I2_S tensors");
+  }
+  *out_layer = L;
+  return OBN_OK;
+}
+
+int obn_bitlinear_set_activation(obn_bitlinear* layer, int act) {
+  clear_error();
+  if (int rc = check_layer(layer)) return rc;
+  if (!layer->gated) return fail(OBN_ERR_INVALID_ARGUMENT, "only a gated layer has an activation");
+  if (act != 0 && act != 1) return fail(OBN_ERR_INVALID_ARGUMENT, "activation %d is not 0 or 1", act);
+  layer->act = act;
+  return OBN_OK;
+}
+
+int obn_activation(const float* x, size_t count, int act, float* y, void* stream) {
+  clear_error();
+  if ((!x || !y) && count) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (act != 0 && act != 1) return fail(OBN_ERR_INVALID_ARGUMENT, "activation %d is not 0 or 1", act);
+  cudaError_t e = obn::launch_act(x, count, act, y, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "activation launch");
   return OBN_OK;
 }
 
@@ -494,9 +575,9 @@ int forward_impl(const obn_bitlinear* layer, const float* x, int n, float* y, vo
       return fail(OBN_ERR_UNSUPPORTED, "in_dim %d exceeds the kernels' limit", layer->in_dim);
     if (e != cudaSuccess) return cuda_fail(e, "ternary matmul launch");
   }
-  if (layer->gated) {  // ffn.rs:70-79: activation.wgsl (ReLU^2) then elementwise.wgsl (multiply)
-    e = obn::launch_relu2_mul(ym, n, layer->out_dim, y, s);
-    if (e != cudaSuccess) return cuda_fail(e, "relu^2 * up launch");
+  if (layer->gated) {  // ffn.rs:70-79: activation.wgsl then elementwise.wgsl (multiply)
+    e = obn::launch_act_mul(ym, n, layer->out_dim, layer->act, y, s);
+    if (e != cudaSuccess) return cuda_fail(e, "act(gate) * up launch");
   }
   return OBN_OK;
 }

@@ -710,24 +710,43 @@ cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps,
 }
 
 namespace {
-// activation.wgsl:28-33 then elementwise.wgsl:31-32: two outputs per thread from
+// activation.wgsl:28-33 then elementwise.wgsl:31-32: the activation of a gate
+// value, ReLU^2 (act 0: max(0, x)^2) or SiLU (act 1: x / (1 + exp(-x))).
+template <int ACT>
+OBN_DEVINL float activation(float x) {
+  if (ACT == 0) {
+    const float r = fmaxf(0.0f, x);
+    return __fmul_rn(r, r);
+  }
+  return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+}
+
+// act(gate) * up over interleaved (gate, up) pairs: two outputs per thread from
 // one 16-byte load of (gate, up, gate, up).
-__global__ __launch_bounds__(256) void k_relu2_mul(const float4* __restrict__ gu,
-                                                   const float* __restrict__ gu1, size_t pairs2,
-                                                   size_t total, float* __restrict__ y) {
+template <int ACT>
+__global__ __launch_bounds__(256) void k_act_mul(const float4* __restrict__ gu,
+                                                 const float* __restrict__ gu1, size_t pairs2,
+                                                 size_t total, float* __restrict__ y) {
   pdl_launch_dependents();
   pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < pairs2) {
     const float4 v = gu[i];
-    const float r0 = fmaxf(0.0f, v.x), r1 = fmaxf(0.0f, v.z);
-    y[2 * i] = __fmul_rn(__fmul_rn(r0, r0), v.y);
-    y[2 * i + 1] = __fmul_rn(__fmul_rn(r1, r1), v.w);
+    y[2 * i] = __fmul_rn(activation<ACT>(v.x), v.y);
+    y[2 * i + 1] = __fmul_rn(activation<ACT>(v.z), v.w);
   } else if (i == pairs2 && 2 * pairs2 < total) {  // odd element count: the last output
     const size_t j = 2 * pairs2;
-    const float r = fmaxf(0.0f, gu1[2 * j]);
-    y[j] = __fmul_rn(__fmul_rn(r, r), gu1[2 * j + 1]);
+    y[j] = __fmul_rn(activation<ACT>(gu1[2 * j]), gu1[2 * j + 1]);
   }
+}
+
+// activation.wgsl alone (FFN::forward_simple, ffn.rs:82-92): y[i] = act(x[i]).
+template <int ACT>
+__global__ __launch_bounds__(256) void k_act(const float* x, size_t count, float* y) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < count) y[i] = activation<ACT>(x[i]);
 }
 }  // namespace
 
@@ -786,13 +805,25 @@ cudaError_t launch_embed_f16(const void* table, int vocab, int dim, const int32_
                     static_cast<const unsigned short*>(table), vocab, dim, ids, total, y);
 }
 
-cudaError_t launch_relu2_mul(const float* gu, int n, int d, float* y, cudaStream_t s) {
+cudaError_t launch_act_mul(const float* gu, int n, int d, int act, float* y, cudaStream_t s) {
   const size_t total = static_cast<size_t>(n) * d;
   const size_t pairs2 = total / 2;
   const size_t threads = pairs2 + 1;
   const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
-  return launch_pdl(k_relu2_mul, dim3(blocks), dim3(256), 0, s,
-                    reinterpret_cast<const float4*>(gu), gu, pairs2, total, y);
+  auto kern = act == 0 ? k_act_mul<0> : k_act_mul<1>;
+  return launch_pdl(kern, dim3(blocks), dim3(256), 0, s, reinterpret_cast<const float4*>(gu), gu,
+                    pairs2, total, y);
+}
+
+cudaError_t launch_relu2_mul(const float* gu, int n, int d, float* y, cudaStream_t s) {
+  return launch_act_mul(gu, n, d, 0, y, s);
+}
+
+cudaError_t launch_act(const float* x, size_t count, int act, float* y, cudaStream_t s) {
+  if (count == 0) return cudaSuccess;
+  const unsigned blocks = static_cast<unsigned>((count + 255) / 256);
+  auto kern = act == 0 ? k_act<0> : k_act<1>;
+  return launch_pdl(kern, dim3(blocks), dim3(256), 0, s, x, count, y);
 }
 
 cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int d, float* y,

@@ -92,6 +92,26 @@ OBN_API int obn_bitlinear_load_i2s_gated(const uint8_t* gate_i2s, size_t gate_by
                                          int out_dim, const float* norm_weight, float eps,
                                          int device, obn_bitlinear** out_layer);
 
+/* Several GGUF I2_S tensors that read the same input, stacked into one layer
+ * (the merged q|k|v projection: Attention::forward, attention.rs:98-100, runs
+ * three BitLinears on one normed input). Tensor t contributes out_dims[t] rows
+ * scaled by its own per-tensor scale (loader.rs:129-137), so the output row
+ * r of the layer equals row r - (rows before t) of tensor t's BitLinear.
+ * out_dim of the layer = the sum of out_dims. */
+OBN_API int obn_bitlinear_load_i2s_concat(int count, const uint8_t* const* tensors,
+                                          const size_t* nbytes, const int* out_dims, int in_dim,
+                                          const float* norm_weight, float eps, int device,
+                                          obn_bitlinear** out_layer);
+
+/* The activation of a gated layer's gate half: 0 = ReLU^2 (the default; bitnet-25
+ * models), 1 = SiLU x / (1 + exp(-x)) (other architectures; activation.wgsl:28-33,
+ * ffn.rs:64-80). */
+OBN_API int obn_bitlinear_set_activation(obn_bitlinear* layer, int act);
+
+/* activation.wgsl alone: y[i] = act(x[i]) for i < count, act as above (y may alias x).
+ * FFN::forward_simple (ffn.rs:82-92) applies it to up_proj's output. */
+OBN_API int obn_activation(const float* x, size_t count, int act, float* y, void* stream);
+
 /* BitLinear::new(device, packed_weights, weight_scales, norm_weight, in_dim,
  * out_dim) (bitlinear.rs:31-49) over buffers already on the device in the
  * reference's layout: packed [out_dim, in_dim/16] u32, per-row scales
