@@ -8,9 +8,12 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <limits>
+#include <utility>
 
 #include "../../include/obn.h"
 #include "gguf.h"
+#include "sampling.h"
 
 namespace obn {
 
@@ -155,8 +158,12 @@ Model::~Model() {
                   static_cast<void*>(ffn_), static_cast<void*>(lm_in_),
                   static_cast<void*>(logits_d_), static_cast<void*>(ids_d_), ws_, attn_ws_})
     cudaFree(p);
+  cudaFree(recent_d_);
+  cudaFree(sel_d_);
   cudaFreeHost(logits_h_);
   cudaFreeHost(ids_h_);
+  cudaFreeHost(recent_h_);
+  cudaFreeHost(sel_h_);
   if (stream_) cudaStreamDestroy(static_cast<cudaStream_t>(stream_));
   cudaSetDevice(prev);
 }
@@ -396,16 +403,22 @@ std::string Model::build(const gguf::File& f, const uint8_t* data, size_t size,
   attn_ws_bytes_ = std::max<size_t>(obn_attention_workspace_bytes(1, kChunk, H, d, kMaxSeq), 256);
   if ((ce = cudaMalloc(&attn_ws_, attn_ws_bytes_)) != cudaSuccess)
     return cuda_fail(ce, "attention workspace allocation");
+  const size_t sel_bytes = 16 + static_cast<size_t>(kSelCap) * 8;
   if ((ce = cudaMallocHost(&logits_h_, sizeof(float) * c.vocab)) != cudaSuccess ||
-      (ce = cudaMallocHost(&ids_h_, sizeof(int32_t) * kChunk)) != cudaSuccess)
+      (ce = cudaMallocHost(&ids_h_, sizeof(int32_t) * kChunk)) != cudaSuccess ||
+      (ce = cudaMallocHost(&recent_h_, sizeof(uint32_t) * kMaxSeq)) != cudaSuccess ||
+      (ce = cudaMallocHost(&sel_h_, sel_bytes)) != cudaSuccess)
     return cuda_fail(ce, "pinned host buffers");
+  if ((ce = cudaMalloc(&recent_d_, sizeof(uint32_t) * kMaxSeq)) != cudaSuccess ||
+      (ce = cudaMalloc(&sel_d_, sel_bytes)) != cudaSuccess)
+    return cuda_fail(ce, "sampling buffers");
   if ((ce = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(ce, "model upload");
   progress(2, total, total, 1.0);
   log(2, fmt("%llu tensors loaded", static_cast<unsigned long long>(total)));
   return std::string();
 }
 
-std::string Model::forward(const uint32_t* ids, int n) {
+std::string Model::forward(const uint32_t* ids, int n, bool copy_logits) {
   if (n <= 0) return "forward needs at least one token";
   if (pos_ + n > kMaxSeq)
     return fmt("context full: %d positions + %d new tokens exceed the %d-position KV cache", pos_,
@@ -416,14 +429,14 @@ std::string Model::forward(const uint32_t* ids, int n) {
     // Keep every chunk of a multi-token input at >= 2 tokens, so each prompt token
     // takes the n > 1 (GEMM) epilogue order as in one reference forward.
     if (n > 1 && n - done - len == 1) --len;
-    std::string e = run_chunk(ids + done, len, done + len == n);
+    std::string e = run_chunk(ids + done, len, done + len == n, copy_logits);
     if (!e.empty()) return e;
     done += len;
   }
   return std::string();
 }
 
-std::string Model::run_chunk(const uint32_t* ids, int n, bool want_logits) {
+std::string Model::run_chunk(const uint32_t* ids, int n, bool want_logits, bool copy_logits) {
   const ModelConfig& c = cfg_;
   cudaStream_t s = static_cast<cudaStream_t>(stream_);
   int prev = 0;
@@ -479,10 +492,109 @@ std::string Model::run_chunk(const uint32_t* ids, int n, bool want_logits) {
     if (obn_lm_head_f16(table, c.vocab, D, last, final_norm_, c.eps, 1, logits_d_, s) != OBN_OK)
       return obn_fail("LM head");
   }
-  ce = cudaMemcpyAsync(logits_h_, logits_d_, sizeof(float) * c.vocab, cudaMemcpyDeviceToHost, s);
+  if (!copy_logits) return std::string();
+  return logits_to_host();
+}
+
+std::string Model::logits_to_host() {
+  cudaStream_t s = static_cast<cudaStream_t>(stream_);
+  cudaError_t ce = cudaMemcpyAsync(logits_h_, logits_d_, sizeof(float) * cfg_.vocab,
+                                   cudaMemcpyDeviceToHost, s);
   if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
   if (ce != cudaSuccess) return cuda_fail(ce, "logits read-back");
   if (obn_check_device_errors() != OBN_OK) return obn_fail("device-side check");
+  return std::string();
+}
+
+std::string Model::sample(float temperature, size_t top_k, float repeat_penalty,
+                          const uint32_t* recent, size_t n_recent, float u, uint32_t* out) {
+  const size_t V = static_cast<size_t>(cfg_.vocab);
+  const bool greedy = !(temperature > 0.0f);
+  const size_t k = greedy ? 1 : top_k;
+  if (k == 0 || k >= V || k > kSelCap / 2 || n_recent > static_cast<size_t>(kMaxSeq)) {
+    std::string e = logits_to_host();  // the whole vocabulary on the host
+    if (!e.empty()) return e;
+    *out = sample_logits(logits_h_, V, temperature, top_k, repeat_penalty, recent, n_recent, u);
+    return std::string();
+  }
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != device_) cudaSetDevice(device_);
+  struct Restore {
+    int dev, cur;
+    ~Restore() {
+      if (dev != cur) cudaSetDevice(dev);
+    }
+  } restore{prev, device_};
+  cudaStream_t s = static_cast<cudaStream_t>(stream_);
+  cudaError_t ce = cudaSuccess;
+  const bool penalise = repeat_penalty != 1.0f && n_recent > 0;
+  if (penalise) {
+    std::memcpy(recent_h_, recent, sizeof(uint32_t) * n_recent);
+    ce = cudaMemcpyAsync(recent_d_, recent_h_, sizeof(uint32_t) * n_recent,
+                         cudaMemcpyHostToDevice, s);
+    if (ce != cudaSuccess) return cuda_fail(ce, "penalty window upload");
+  }
+  int* count_d = static_cast<int*>(sel_d_);
+  uint2* pairs_d = reinterpret_cast<uint2*>(static_cast<uint8_t*>(sel_d_) + 16);
+  ce = launch_select_topk(logits_d_, cfg_.vocab, recent_d_, penalise ? static_cast<int>(n_recent) : 0,
+                          penalise ? repeat_penalty : 1.0f, temperature, static_cast<int>(k),
+                          pairs_d, kSelCap, count_d, s);
+  if (ce != cudaSuccess) return cuda_fail(ce, "top-k launch");
+  // The count and the first 4k + 256 pairs (ties past that need a second copy).
+  const size_t first = std::min<size_t>(kSelCap, 4 * k + 256);
+  ce = cudaMemcpyAsync(sel_h_, sel_d_, 16 + first * 8, cudaMemcpyDeviceToHost, s);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+  if (ce != cudaSuccess) return cuda_fail(ce, "top-k read-back");
+  const int count = *static_cast<const int*>(sel_h_);
+  if (count > static_cast<int>(first) && count <= kSelCap) {
+    ce = cudaMemcpy(static_cast<uint8_t*>(sel_h_) + 16 + first * 8,
+                    static_cast<uint8_t*>(sel_d_) + 16 + first * 8, (count - first) * 8,
+                    cudaMemcpyDeviceToHost);
+    if (ce != cudaSuccess) return cuda_fail(ce, "top-k read-back");
+  }
+  if (count <= 0 || count > kSelCap) {  // more ties than the buffer holds: host path
+    std::string e = logits_to_host();   // the penalty is already applied
+    if (!e.empty()) return e;
+    *out = sample_logits(logits_h_, V, temperature, top_k, 1.0f, nullptr, 0, u);
+    return std::string();
+  }
+  const uint32_t* pr = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(sel_h_) + 16);
+  std::vector<std::pair<uint32_t, float>> surv(count);
+  for (int i = 0; i < count; ++i) {
+    float v;
+    std::memcpy(&v, pr + 2 * i + 1, 4);
+    surv[i] = {pr[2 * i], v};
+  }
+  std::sort(surv.begin(), surv.end());
+  if (greedy) {  // the first index among the maxima
+    *out = surv.front().first;
+    return std::string();
+  }
+  // sampling.rs:62-76 over the survivors in index order; the masked logits
+  // contribute exp(-inf) = 0 to every sum, which leaves it unchanged.
+  float max_val = -std::numeric_limits<float>::infinity();
+  for (const auto& p : surv) max_val = std::fmax(max_val, p.second);
+  std::vector<float> e(count);
+  float sum = 0.0f;
+  for (int i = 0; i < count; ++i) {
+    e[i] = std::exp(surv[i].second - max_val);
+    sum += e[i];
+  }
+  const float r = u * sum;
+  if (!(r > 0.0f)) {  // r = 0: the running sum reaches it at index 0; NaN: never
+    *out = r == 0.0f ? 0u : static_cast<uint32_t>(V - 1);
+    return std::string();
+  }
+  float cumsum = 0.0f;
+  for (int i = 0; i < count; ++i) {
+    cumsum += e[i];
+    if (cumsum >= r) {
+      *out = surv[i].first;
+      return std::string();
+    }
+  }
+  *out = static_cast<uint32_t>(V - 1);
   return std::string();
 }
 

@@ -73,7 +73,13 @@ class Model {
   // BitNetModel::forward (model.rs:200-262): runs `n` tokens at the current
   // position, appends them to the KV cache and leaves the logits of the last
   // one in logits() (host). Empty string on success.
-  std::string forward(const uint32_t* ids, int n);
+  std::string forward(const uint32_t* ids, int n, bool copy_logits = true);
+  // Next token from the logits of the last forward (sampling.rs:4-77 with the
+  // uniform draw u): the penalty, temperature and top-k cut run on the device
+  // and only the survivors come to the host, which draws in the reference's
+  // order; top_k = 0 or >= vocab takes the whole-vocabulary host path.
+  std::string sample(float temperature, size_t top_k, float repeat_penalty,
+                     const uint32_t* recent, size_t n_recent, float u, uint32_t* out);
   // BitNetModel::reset_kv_cache (model.rs:305-316).
   void reset() { pos_ = 0; }
   int position() const { return pos_; }
@@ -88,7 +94,8 @@ class Model {
   Model() = default;
   std::string build(const gguf::File& f, const uint8_t* data, size_t size,
                     const ProgressFn& progress, const LogFn& log);
-  std::string run_chunk(const uint32_t* ids, int n, bool want_logits);
+  std::string run_chunk(const uint32_t* ids, int n, bool want_logits, bool copy_logits);
+  std::string logits_to_host();
 
   struct Layer {
     obn_bitlinear* qkv = nullptr;     // q|k|v, input_layernorm fused
@@ -119,6 +126,11 @@ class Model {
   size_t attn_ws_bytes_ = 0;
   float* logits_h_ = nullptr;  // pinned [vocab]
   int32_t* ids_h_ = nullptr;   // pinned [kChunk]
+  static constexpr int kSelCap = 4096;  // top-k survivors the device path returns
+  uint32_t* recent_d_ = nullptr;        // [kMaxSeq] penalty window
+  uint32_t* recent_h_ = nullptr;        // pinned [kMaxSeq]
+  void* sel_d_ = nullptr;               // count, then kSelCap ids, then kSelCap values
+  void* sel_h_ = nullptr;               // pinned copy of sel_d_
 };
 
 }  // namespace obn

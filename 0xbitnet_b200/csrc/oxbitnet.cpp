@@ -192,21 +192,23 @@ int32_t run_generation(OxBitNet* h, const std::vector<uint32_t>& ids,
               std::to_string(obn::Model::kMaxSeq) + "-position KV cache");
     return -1;
   }
-  std::string e = m.forward(ids.data(), static_cast<int>(ids.size()));
+  std::string e = m.forward(ids.data(), static_cast<int>(ids.size()), /*copy_logits=*/false);
   if (!e.empty()) {
     set_error(e);
     return -1;
   }
   const obn::BpeTokenizer& tok = m.tokenizer();
-  const size_t vocab = static_cast<size_t>(m.config().vocab);
   std::vector<uint32_t> recent;
   for (size_t step = 0; step < o.max_tokens; ++step) {
     const size_t start =
         o.repeat_last_n > 0 && recent.size() > o.repeat_last_n ? recent.size() - o.repeat_last_n : 0;
-    float* logits = const_cast<float*>(m.logits());  // consumed here, rewritten by the next forward
-    const uint32_t next = m.sampler().sample(logits, vocab, o.temperature, o.top_k,
-                                             o.repeat_penalty, recent.data() + start,
-                                             recent.size() - start);
+    uint32_t next = 0;
+    e = m.sample(o.temperature, o.top_k, o.repeat_penalty, recent.data() + start,
+                 recent.size() - start, m.sampler().uniform(), &next);
+    if (!e.empty()) {
+      set_error(e);
+      return -1;
+    }
     if (next == tok.eos_id() || (tok.has_eot() && next == tok.eot_id()) ||
         (tok.has_im_end() && next == tok.im_end_id()))
       break;
@@ -217,7 +219,7 @@ int32_t run_generation(OxBitNet* h, const std::vector<uint32_t>& ids,
       log_msg(3, "generation stopped: the KV cache is full");
       break;
     }
-    e = m.forward(&next, 1);
+    e = m.forward(&next, 1, /*copy_logits=*/false);
     if (!e.empty()) {
       set_error(e);
       return -1;
@@ -564,6 +566,22 @@ int32_t oxbitnet_token_text(const OxBitNetTokenizer* tok, uint32_t id, char* buf
     return -1;
   }
   return copy_text(tok->tok.decode_one(id), buf, cap, len);
+}
+
+int32_t oxbitnet_sample_next(OxBitNet* model, float temperature, uintptr_t top_k,
+                             float repeat_penalty, const uint32_t* recent, uintptr_t n_recent,
+                             float u, uint32_t* out) {
+  clear_error();
+  if (!model || !model->model || !out || (!recent && n_recent)) {
+    set_error("model and out must not be NULL");
+    return -1;
+  }
+  std::string e = model->model->sample(temperature, top_k, repeat_penalty, recent, n_recent, u, out);
+  if (!e.empty()) {
+    set_error(e);
+    return -1;
+  }
+  return 0;
 }
 
 uint32_t oxbitnet_sample(float* logits, uintptr_t vocab, float temperature, uintptr_t top_k,

@@ -60,29 +60,27 @@ class GGUFWriter:
     def add_tensor(self, name: str, shape, ggml_type: int, data: bytes) -> None:
         self.tensors.append((name, tuple(int(s) for s in shape), ggml_type, bytes(data)))
 
-    def to_bytes(self) -> bytes:
+    def _header(self) -> bytes:
         head = [struct.pack("<IIQQ", 0x46554747, self.version, len(self.tensors),
                             len(self.metadata))]
         for key, vtype, value in self.metadata:
             head.append(_str(key) + struct.pack("<I", vtype) + _value(vtype, value))
-        offsets, off = [], 0
-        for _, _, _, data in self.tensors:
-            offsets.append(off)
-            off += (len(data) + self.alignment - 1) // self.alignment * self.alignment
-        for (name, shape, gtype, _), o in zip(self.tensors, offsets):
+        off = 0
+        for name, shape, gtype, data in self.tensors:
             head.append(_str(name) + struct.pack("<I", len(shape))
                         + b"".join(struct.pack("<Q", s) for s in shape)
-                        + struct.pack("<IQ", gtype, o))
+                        + struct.pack("<IQ", gtype, off))
+            off += (len(data) + self.alignment - 1) // self.alignment * self.alignment
         h = b"".join(head)
-        pad = (-len(h)) % self.alignment
-        body = []
-        for _, _, _, data in self.tensors:
-            body.append(data + b"\0" * ((-len(data)) % self.alignment))
-        return h + b"\0" * pad + b"".join(body)
+        return h + b"\0" * ((-len(h)) % self.alignment)
 
     def write(self, path: str) -> None:
+        """Streams the header, then each tensor padded to the alignment."""
         with open(path, "wb") as f:
-            f.write(self.to_bytes())
+            f.write(self._header())
+            for _, _, _, data in self.tensors:
+                f.write(data)
+                f.write(b"\0" * ((-len(data)) % self.alignment))
 
 
 def pack_i2s(codes: np.ndarray) -> np.ndarray:
@@ -105,6 +103,29 @@ def i2s_tensor(rng: np.random.Generator, M: int, K: int, scale: float | None = N
     return pack_i2s(codes).tobytes() + trailer.tobytes(), codes, scale
 
 
+_FAST_LUT = None
+
+
+def fast_i2s_tensor(rng: np.random.Generator, M: int, K: int) -> bytes:
+    """A random ternary tensor as I2_S bytes without materialising the codes:
+    each packed byte comes from 16 random bits, one nibble per 2-bit code
+    (nibble < 5 -> -1, < 11 -> 0, else +1: P(-1) = P(+1) = 5/16, P(0) = 6/16).
+    For large synthetic models (the 2B shape holds 2.1e9 weights)."""
+    global _FAST_LUT
+    if _FAST_LUT is None:
+        v = np.arange(65536, dtype=np.uint32)
+        lut = np.zeros(65536, np.uint8)
+        for j in range(4):
+            nib = (v >> (4 * j)) & 15
+            code = np.where(nib < 5, 0, np.where(nib < 11, 1, 2)).astype(np.uint8)
+            lut |= (code << (2 * j)).astype(np.uint8)
+        _FAST_LUT = lut
+    r = rng.integers(0, 65536, size=M * K // 4, dtype=np.uint16)
+    trailer = np.zeros(8, dtype=np.float32)
+    trailer[0] = np.float32(0.5 + 1.5 * rng.random())
+    return _FAST_LUT[r].tobytes() + trailer.tobytes()
+
+
 @dataclass
 class BitNetShape:
     vocab: int = 128256
@@ -123,10 +144,12 @@ class BitNetShape:
 
 
 def write_bitnet_model(path: str, shape: BitNetShape, tokens: list, merges: list,
-                       bos: int, eos: int, seed: int = 0, keep: dict | None = None) -> None:
+                       bos: int, eos: int, seed: int = 0, keep: dict | None = None,
+                       fast: bool = False) -> None:
     """Writes a seeded random BitNet model with the given tokenizer vocabulary.
     If `keep` is a dict, the host copies of every tensor go into it (name ->
-    (codes, scale) for I2_S, float32 array otherwise) for reference checks."""
+    (codes, scale) for I2_S, float32 array otherwise) for reference checks.
+    fast=True draws the ternary weights with fast_i2s_tensor (no `keep`)."""
     s = shape
     rng = np.random.default_rng(seed)
     w = GGUFWriter()
@@ -156,12 +179,15 @@ def write_bitnet_model(path: str, shape: BitNetShape, tokens: list, merges: list
             keep[name] = g
 
     def tern(name, M, K):
+        if fast:
+            w.add_tensor(name, (K, M), TYPE_I2_S, fast_i2s_tensor(rng, M, K))
+            return
         data, codes, scale = i2s_tensor(rng, M, K)
         w.add_tensor(name, (K, M), TYPE_I2_S, data)
         if keep is not None:
             keep[name] = (codes, scale)
 
-    emb = (0.02 * rng.standard_normal((s.vocab, s.hidden))).astype(np.float16)
+    emb = (0.02 * rng.standard_normal((s.vocab, s.hidden), dtype=np.float32)).astype(np.float16)
     w.add_tensor("token_embd.weight", (s.hidden, s.vocab), TYPE_F16, emb.tobytes())
     if keep is not None:
         keep["token_embd.weight"] = emb
@@ -190,3 +216,22 @@ def write_bitnet_model(path: str, shape: BitNetShape, tokens: list, merges: list
     elif s.lm_head == "i2s":
         tern("output.weight", s.vocab, s.hidden)
     w.write(path)
+
+
+def synthetic_vocab(n: int) -> tuple:
+    """A vocabulary of n tokens for synthetic models: the 256 byte-alphabet
+    characters, filler tokens, and the LLaMA 3 specials last; no merges.
+    Returns (tokens, merges, bos, eos)."""
+    keep = list(range(33, 127)) + list(range(161, 173)) + list(range(174, 256))
+    chars, k = [], 0
+    for b in range(256):
+        if b in keep:
+            chars.append(chr(b))
+        else:
+            chars.append(chr(256 + k))
+            k += 1
+    specials = ["<|begin_of_text|>", "<|end_of_text|>", "<|start_header_id|>",
+                "<|end_header_id|>", "<|eot_id|>"]
+    filler = [f"<tok{i}>" for i in range(n - 256 - len(specials))]
+    tokens = chars + filler + specials
+    return tokens, [], tokens.index("<|begin_of_text|>"), tokens.index("<|end_of_text|>")

@@ -83,6 +83,8 @@ SIGNATURES = {
     "oxbitnet_detokenize": (_I32, [_P, ctypes.POINTER(_U32), _U, ctypes.c_char_p, _U,
                                    ctypes.POINTER(_U)]),
     "oxbitnet_token_text": (_I32, [_P, _U32, ctypes.c_char_p, _U, ctypes.POINTER(_U)]),
+    "oxbitnet_sample_next": (_I32, [_P, _F, _U, _F, ctypes.POINTER(_U32), _U, _F,
+                                    ctypes.POINTER(_U32)]),
     "oxbitnet_sample": (_U32, [ctypes.POINTER(_F), _U, _F, _U, _F, ctypes.POINTER(_U32), _U, _F]),
     "oxbitnet_gguf_describe": (ctypes.c_char_p, [ctypes.c_char_p]),
     "oxbitnet_cache_path": (_I32, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _U]),
@@ -226,6 +228,16 @@ class BitNet:
                                   out.ctypes.data_as(ctypes.POINTER(_F)), out.size) != 0:
             _raise("forward failed")
         return out
+
+    def sample_next(self, temperature: float, top_k: int, repeat_penalty: float,
+                    recent: Sequence[int], u: float) -> int:
+        """The next token from the last forward's logits (device top-k path)."""
+        arr, n = _ids_array(list(recent))
+        out = _U32(0)
+        if lib().oxbitnet_sample_next(self._handle(), temperature, top_k, repeat_penalty, arr, n,
+                                      u, ctypes.byref(out)) != 0:
+            _raise("sample_next failed")
+        return int(out.value)
 
     def set_seed(self, seed: int) -> None:
         if lib().oxbitnet_set_seed(self._handle(), seed) != 0:

@@ -182,6 +182,14 @@ OXBITNET_API int32_t oxbitnet_detokenize(const struct OxBitNetTokenizer *tok, co
 OXBITNET_API int32_t oxbitnet_token_text(const struct OxBitNetTokenizer *tok, uint32_t id,
                                          char *buf, uintptr_t cap, uintptr_t *len);
 
+/* Samples the next token from the logits of the model's last forward with the
+ * uniform draw `u`, as generation does (penalty, temperature and top-k on the
+ * device, the draw on the host). The penalty modifies the device logits. */
+OXBITNET_API int32_t oxbitnet_sample_next(struct OxBitNet *model, float temperature,
+                                          uintptr_t top_k, float repeat_penalty,
+                                          const uint32_t *recent, uintptr_t n_recent, float u,
+                                          uint32_t *out);
+
 /* One sampling step with the uniform draw `u` in [0, 1) given (logits are
  * modified); returns the id. */
 OXBITNET_API uint32_t oxbitnet_sample(float *logits, uintptr_t vocab, float temperature,

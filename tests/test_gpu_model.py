@@ -173,3 +173,25 @@ def test_errors(tmp_path, vocab):
     p3, _, _ = make(tmp_path, vocab, name="hd64", hidden=256, heads=4, kv_heads=4)
     with pytest.raises(ox().OxBitNetError, match="head_dim 64"):
         ox().BitNet.load_sync(p3)
+
+
+def test_device_sampling_matches_host_sampler(tmp_path, vocab):
+    """The generation loop's sampler (penalty, temperature and top-k on the device,
+    the draw on the host) picks the same id as the whole-vocabulary host sampler
+    (sampling.rs restated in sampler.cpp) on the same logits and draw."""
+    need_cuda()
+    p, _, _ = make(tmp_path, vocab, layers=1, seed=9)
+    m = ox().BitNet.load_sync(p)
+    rng = np.random.default_rng(0)
+    prompt = [vocab["bos"], 3, 4, 5]
+    for trial in range(60):
+        T = float(rng.choice([0.0, 0.5, 1.0, 1.7]))
+        k = int(rng.choice([1, 5, 50, 200, 704, 705, 0]))
+        pen = float(rng.choice([1.0, 1.1, 2.0]))
+        recent = [int(t) for t in rng.integers(0, 705, int(rng.integers(0, 70)))]
+        u = float(rng.random()) if trial % 10 else 0.0
+        logits = m.forward(prompt, reset=True)
+        want = ox().sample(logits, T, k, pen, recent, u)
+        got = m.sample_next(T, k, pen, recent, u)
+        assert got == want, (trial, T, k, pen, u)
+    m.dispose()

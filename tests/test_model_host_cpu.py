@@ -321,7 +321,7 @@ def test_oxbitnet_header_symbols_are_exported():
     import re
     text = open(os.path.join(HERE, "..", "include", "oxbitnet.h")).read()
     syms = sorted(set(re.findall(r"OXBITNET_API\s+[\w\s\*]+?\b(oxbitnet_\w+)\s*\(", text)))
-    assert len(syms) == 21
+    assert len(syms) == 22
     for s in ["oxbitnet_set_logger", "oxbitnet_default_generate_options",
               "oxbitnet_default_load_options", "oxbitnet_load", "oxbitnet_free",
               "oxbitnet_generate", "oxbitnet_chat", "oxbitnet_error_message"]:
