@@ -50,6 +50,9 @@ SIGNATURES = {
     "obn_rope_kv_append": (_I, [_P, _I, _I, _I, _I, _I, _I, _F, _P, _P, _P, _I, _P]),
     "obn_attention_workspace_bytes": (_SZ, [_I, _I, _I, _I, _I]),
     "obn_attention_decode": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _F, _P, _P, _SZ, _P]),
+    "obn_rope_kv_append_at": (_I, [_P, _I, _I, _I, _I, _I, _P, _F, _P, _P, _P, _I, _P]),
+    "obn_attention_decode_at": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _P, _SZ,
+                                     _P]),
     "obn_add": (_I, [_P, _P, _SZ, _P, _P]),
     "obn_embed_f16": (_I, [_P, _I, _I, _P, _I, _P, _P]),
     "obn_rmsnorm_quantize": (_I, [_P, _P, _F, _I, _I, _P, _P, _P, _P]),

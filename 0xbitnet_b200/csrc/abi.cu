@@ -749,6 +749,55 @@ int obn_attention_decode(const float* q, const void* k_cache, const void* v_cach
   return OBN_OK;
 }
 
+int obn_rope_kv_append_at(const float* qkv, int B, int n, int H, int Hkv, int head_dim,
+                          const int* pos_dev, float theta_base, float* q_out, void* k_cache,
+                          void* v_cache, int S_max, void* stream) {
+  clear_error();
+  if (!qkv || !q_out || !k_cache || !v_cache || !pos_dev)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (B <= 0 || n <= 0 || H <= 0 || Hkv <= 0 || S_max <= 0 || n > S_max)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "sizes must be positive, n <= S_max");
+  if (head_dim != obn::kAttnHeadDim)
+    return fail(OBN_ERR_UNSUPPORTED, "head_dim must be %d (got %d)", obn::kAttnHeadDim, head_dim);
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(qkv, 8) || !aligned(q_out, 8) ||
+      !aligned(pos_dev, 4))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "caches must be 16-byte, qkv and q_out 8-byte aligned");
+  cudaError_t e = obn::launch_rope_kv_append(
+      qkv, B, n, H, Hkv, head_dim, 0, theta_base, q_out, static_cast<__half*>(k_cache),
+      static_cast<__half*>(v_cache), S_max, static_cast<cudaStream_t>(stream), pos_dev);
+  if (e != cudaSuccess) return cuda_fail(e, "rope / kv append launch");
+  return OBN_OK;
+}
+
+int obn_attention_decode_at(const float* q, const void* k_cache, const void* v_cache, int B,
+                            int n, int H, int Hkv, int head_dim, int S_max, const int* pos_dev,
+                            float scale, float* out, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  clear_error();
+  if (!q || !k_cache || !v_cache || !out || !workspace || !pos_dev)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (B <= 0 || n <= 0 || H <= 0 || Hkv <= 0 || n > S_max)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "sizes must be positive, n <= S_max");
+  if (head_dim != obn::kAttnHeadDim)
+    return fail(OBN_ERR_UNSUPPORTED, "head_dim must be %d (got %d)", obn::kAttnHeadDim, head_dim);
+  const int G = H % Hkv == 0 ? H / Hkv : 0;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return fail(OBN_ERR_UNSUPPORTED, "H / Hkv must be 1, 2, 4 or 8 (got %d / %d)", H, Hkv);
+  const size_t need = obn::attention_workspace_bytes(B, n, H, head_dim, S_max);
+  if (workspace_bytes < need)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than the %zu needed",
+                workspace_bytes, need);
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(workspace, 256) ||
+      !aligned(q, 4) || !aligned(out, 4) || !aligned(pos_dev, 4))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "caches must be 16-byte, workspace 256-byte aligned");
+  cudaError_t e = obn::launch_attention(q, static_cast<const __half*>(k_cache),
+                                        static_cast<const __half*>(v_cache), B, n, H, Hkv,
+                                        head_dim, S_max, S_max, scale, out, workspace,
+                                        static_cast<cudaStream_t>(stream), pos_dev);
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  return OBN_OK;
+}
+
 int obn_add(const float* a, const float* b, size_t count, float* y, void* stream) {
   clear_error();
   if (!a || !b || !y) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");

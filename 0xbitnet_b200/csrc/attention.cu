@@ -36,6 +36,7 @@ constexpr int kKStride = kAttnHeadDim + 8;  // halves per smem K row: 16-byte ro
 
 __global__ __launch_bounds__(256) void k_rope_kv_append(const float* __restrict__ qkv, int n,
                                                         int H, int Hkv, int d, int pos,
+                                                        const int* __restrict__ pos_dev,
                                                         float theta_base, size_t total,
                                                         float* __restrict__ q_out,
                                                         __half* __restrict__ k_cache,
@@ -54,7 +55,8 @@ __global__ __launch_bounds__(256) void k_rope_kv_append(const float* __restrict_
   const size_t b = r / n;
   const float* src = qkv + (r * slots + j) * d + 2 * i;
   const float x0 = src[0], x1 = src[1];
-  const int p = pos + t;
+  const int p = (pos_dev ? *pos_dev : pos) + t;
+  if (p < 0 || p >= S_max) return;  // a device-side position past the cache writes nothing
   if (j >= H + Hkv) {  // v: stored as is
     __half* dst = v_cache + ((b * S_max + p) * Hkv + (j - H - Hkv)) * d + 2 * i;
     *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(x0, x1);
@@ -105,9 +107,9 @@ OBN_DEVINL float warp_sum(float v) {
 template <int G>
 __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
     const float* __restrict__ q, const __half* __restrict__ k_cache,
-    const __half* __restrict__ v_cache, int n, int H, int Hkv, int S_max, int seq_len, float scale,
-    int nsplit, float* __restrict__ part_acc, float* __restrict__ part_m,
-    float* __restrict__ part_l) {
+    const __half* __restrict__ v_cache, int n, int H, int Hkv, int S_max, int seq_len,
+    const int* __restrict__ pos_dev, float scale, int nsplit, float* __restrict__ part_acc,
+    float* __restrict__ part_m, float* __restrict__ part_l) {
   constexpr int D = kAttnHeadDim;
   extern __shared__ __align__(16) unsigned char smem[];
   __half* sK = reinterpret_cast<__half*>(smem);                       // [128][kKStride]
@@ -122,8 +124,12 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
   const size_t r = blockIdx.z;  // query row b * n + t
   const int t = static_cast<int>(r % n);
   const size_t b = r / n;
-  const int limit = seq_len - n + t + 1;  // keys [0, limit) are visible to this query
   const int s0 = c * kAttnChunk;
+  if (pos_dev) {  // the position lives on the device (graph replay)
+    seq_len = min(*pos_dev + n, S_max);
+    if (s0 >= seq_len) return;  // past every query's keys: the combine skips this split
+  }
+  const int limit = seq_len - n + t + 1;  // keys [0, limit) are visible to this query
   const int cnt = min(kAttnChunk, limit - s0);  // may be <= 0: an empty chunk
   const size_t pbase = (r * H + static_cast<size_t>(kvh) * G) * nsplit + c;
   if (cnt <= 0) {
@@ -231,17 +237,21 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
 __global__ __launch_bounds__(kAttnThreads) void k_attn_combine(const float* __restrict__ part_acc,
                                                                const float* __restrict__ part_m,
                                                                const float* __restrict__ part_l,
-                                                               int nsplit,
+                                                               int nsplit, int n, int S_max,
+                                                               const int* __restrict__ pos_dev,
                                                                float* __restrict__ out) {
   pdl_launch_dependents();
   pdl_wait();
   constexpr int D = kAttnHeadDim;
   const size_t rh = blockIdx.x;  // r * H + h
   const int tid = threadIdx.x;
+  // splits that hold keys (all of them unless the position is read on the device)
+  const int nvalid =
+      pos_dev ? min(nsplit, (min(*pos_dev + n, S_max) + kAttnChunk - 1) / kAttnChunk) : nsplit;
   float M = -FLT_MAX;
-  for (int c = 0; c < nsplit; ++c) M = fmaxf(M, part_m[rh * nsplit + c]);
+  for (int c = 0; c < nvalid; ++c) M = fmaxf(M, part_m[rh * nsplit + c]);
   float L = 0.0f, o = 0.0f;
-  for (int c = 0; c < nsplit; ++c) {
+  for (int c = 0; c < nvalid; ++c) {
     const float l = part_l[rh * nsplit + c];
     if (l == 0.0f) continue;  // an empty chunk
     const float w = expf(part_m[rh * nsplit + c] - M);
@@ -253,8 +263,8 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_combine(const float* __re
 
 template <int G>
 cudaError_t launch_split(const float* q, const __half* k_cache, const __half* v_cache, int B,
-                         int n, int H, int Hkv, int S_max, int seq_len, float scale, int nsplit,
-                         float* pa, float* pm, float* pl, cudaStream_t s) {
+                         int n, int H, int Hkv, int S_max, int seq_len, const int* pos_dev,
+                         float scale, int nsplit, float* pa, float* pm, float* pl, cudaStream_t s) {
   constexpr int D = kAttnHeadDim;
   const size_t smem = static_cast<size_t>(kAttnChunk) * kKStride * 2 +
                       static_cast<size_t>(kAttnChunk) * D * 2 + static_cast<size_t>(G) * D * 4 +
@@ -273,8 +283,8 @@ cudaError_t launch_split(const float* q, const __half* k_cache, const __half* v_
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, q, k_cache, v_cache, n, H, Hkv, S_max, seq_len, scale,
-                            nsplit, pa, pm, pl);
+  return cudaLaunchKernelEx(&cfg, kern, q, k_cache, v_cache, n, H, Hkv, S_max, seq_len, pos_dev,
+                            scale, nsplit, pa, pm, pl);
 }
 
 template <typename... KArgs, typename... Args>
@@ -296,11 +306,11 @@ cudaError_t launch_pdl_attn(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaS
 
 cudaError_t launch_rope_kv_append(const float* qkv, int B, int n, int H, int Hkv, int d, int pos,
                                   float theta_base, float* q_out, __half* k_cache,
-                                  __half* v_cache, int S_max, cudaStream_t s) {
+                                  __half* v_cache, int S_max, cudaStream_t s, const int* pos_dev) {
   const size_t total = static_cast<size_t>(B) * n * (H + 2 * Hkv) * (d / 2);
   const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
   return launch_pdl_attn(k_rope_kv_append, dim3(blocks), dim3(256), s, qkv, n, H, Hkv, d, pos,
-                         theta_base, total, q_out, k_cache, v_cache, S_max);
+                         pos_dev, theta_base, total, q_out, k_cache, v_cache, S_max);
 }
 
 size_t attention_workspace_bytes(int B, int n, int H, int d, int seq_len) {
@@ -310,10 +320,12 @@ size_t attention_workspace_bytes(int B, int n, int H, int d, int seq_len) {
 
 cudaError_t launch_attention(const float* q, const __half* k_cache, const __half* v_cache, int B,
                              int n, int H, int Hkv, int d, int S_max, int seq_len, float scale,
-                             float* out, void* workspace, cudaStream_t s) {
+                             float* out, void* workspace, cudaStream_t s, const int* pos_dev) {
   if (d != kAttnHeadDim || Hkv <= 0 || H % Hkv != 0 || H / Hkv > kAttnMaxGroup)
     return cudaErrorInvalidValue;
-  const int nsplit = (seq_len + kAttnChunk - 1) / kAttnChunk;
+  // With the position on the device the split count covers the whole cache; the
+  // chunks past the visible keys write empty partials.
+  const int nsplit = ((pos_dev ? S_max : seq_len) + kAttnChunk - 1) / kAttnChunk;
   const size_t rows = static_cast<size_t>(B) * n * H * nsplit;
   float* pa = static_cast<float*>(workspace);
   float* pm = pa + rows * d;
@@ -321,17 +333,17 @@ cudaError_t launch_attention(const float* q, const __half* k_cache, const __half
   const int G = H / Hkv;
   cudaError_t e;
   switch (G) {
-    case 1: e = launch_split<1>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, scale, nsplit, pa, pm, pl, s); break;
-    case 2: e = launch_split<2>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, scale, nsplit, pa, pm, pl, s); break;
-    case 4: e = launch_split<4>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, scale, nsplit, pa, pm, pl, s); break;
-    case 8: e = launch_split<8>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, scale, nsplit, pa, pm, pl, s); break;
+    case 1: e = launch_split<1>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, nsplit, pa, pm, pl, s); break;
+    case 2: e = launch_split<2>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, nsplit, pa, pm, pl, s); break;
+    case 4: e = launch_split<4>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, nsplit, pa, pm, pl, s); break;
+    case 8: e = launch_split<8>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, nsplit, pa, pm, pl, s); break;
     default: return cudaErrorInvalidValue;
   }
   if (e != cudaSuccess) return e;
   return launch_pdl_attn(k_attn_combine, dim3(static_cast<unsigned>(B * n * H)),
                          dim3(kAttnThreads), s, static_cast<const float*>(pa),
-                         static_cast<const float*>(pm), static_cast<const float*>(pl), nsplit,
-                         out);
+                         static_cast<const float*>(pm), static_cast<const float*>(pl), nsplit, n,
+                         S_max, pos_dev, out);
 }
 
 }  // namespace obn

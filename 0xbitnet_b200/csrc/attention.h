@@ -17,10 +17,12 @@ constexpr int kAttnMaxGroup = 8;   // query heads per KV head
 // then k heads, then v heads). Rotates q and k of token t of sequence b at
 // position pos + t (rope.wgsl), writes q_out [B*n, H*d] f32, and stores the
 // rotated k and the v of that token into the caches [B][S_max][Hkv][d] (binary16)
-// at position pos + t.
+// at position pos + t. A non-null pos_dev replaces pos by the int it points to
+// (read on the device, so a captured graph serves every position).
 cudaError_t launch_rope_kv_append(const float* qkv, int B, int n, int H, int Hkv, int d, int pos,
                                   float theta_base, float* q_out, __half* k_cache,
-                                  __half* v_cache, int S_max, cudaStream_t s);
+                                  __half* v_cache, int S_max, cudaStream_t s,
+                                  const int* pos_dev = nullptr);
 
 // Scratch of launch_attention: per (query row, head, split) the partial
 // softmax state (max, sum, d unnormalised outputs), f32.
@@ -28,8 +30,11 @@ size_t attention_workspace_bytes(int B, int n, int H, int d, int seq_len);
 
 // Causal GQA attention for the n newest tokens of B sequences whose caches hold
 // seq_len positions (the n new ones last): q [B*n, H*d] f32 -> out [B*n, H*d].
+// A non-null pos_dev makes the visible length *pos_dev + n (read on the device);
+// the workspace must then hold attention_workspace_bytes(B, n, H, d, S_max).
 cudaError_t launch_attention(const float* q, const __half* k_cache, const __half* v_cache, int B,
                              int n, int H, int Hkv, int d, int S_max, int seq_len, float scale,
-                             float* out, void* workspace, cudaStream_t s);
+                             float* out, void* workspace, cudaStream_t s,
+                             const int* pos_dev = nullptr);
 
 }  // namespace obn

@@ -7,6 +7,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <utility>
@@ -158,8 +159,11 @@ Model::~Model() {
                   static_cast<void*>(ffn_), static_cast<void*>(lm_in_),
                   static_cast<void*>(logits_d_), static_cast<void*>(ids_d_), ws_, attn_ws_})
     cudaFree(p);
+  if (decode_exec_) cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(decode_exec_));
   cudaFree(recent_d_);
   cudaFree(sel_d_);
+  cudaFree(step_d_);
+  cudaFreeHost(step_h_);
   cudaFreeHost(logits_h_);
   cudaFreeHost(ids_h_);
   cudaFreeHost(recent_h_);
@@ -410,8 +414,12 @@ std::string Model::build(const gguf::File& f, const uint8_t* data, size_t size,
       (ce = cudaMallocHost(&sel_h_, sel_bytes)) != cudaSuccess)
     return cuda_fail(ce, "pinned host buffers");
   if ((ce = cudaMalloc(&recent_d_, sizeof(uint32_t) * kMaxSeq)) != cudaSuccess ||
-      (ce = cudaMalloc(&sel_d_, sel_bytes)) != cudaSuccess)
+      (ce = cudaMalloc(&sel_d_, sel_bytes)) != cudaSuccess ||
+      (ce = cudaMalloc(&step_d_, 2 * sizeof(int32_t))) != cudaSuccess ||
+      (ce = cudaMallocHost(&step_h_, 2 * sizeof(int32_t))) != cudaSuccess)
     return cuda_fail(ce, "sampling buffers");
+  const char* g = std::getenv("OXBITNET_CUDA_GRAPH");  // "0" runs every step eagerly
+  use_graph_ = !(g && g[0] == '0');
   if ((ce = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(ce, "model upload");
   progress(2, total, total, 1.0);
   log(2, fmt("%llu tensors loaded", static_cast<unsigned long long>(total)));
@@ -436,37 +444,36 @@ std::string Model::forward(const uint32_t* ids, int n, bool copy_logits) {
   return std::string();
 }
 
-std::string Model::run_chunk(const uint32_t* ids, int n, bool want_logits, bool copy_logits) {
+// Enqueues the forward of n tokens whose ids are at ids_dev. pos_dev == nullptr:
+// the first token sits at pos_ (host value); else at *pos_dev (read by the
+// kernels, for the captured decode step). With want_logits the last token's
+// logits land in logits_d_.
+std::string Model::enqueue(int n, const int32_t* ids_dev, const int* pos_dev, bool want_logits) {
   const ModelConfig& c = cfg_;
   cudaStream_t s = static_cast<cudaStream_t>(stream_);
-  int prev = 0;
-  cudaGetDevice(&prev);
-  if (prev != device_) cudaSetDevice(device_);
-  struct Restore {
-    int dev, cur;
-    ~Restore() {
-      if (dev != cur) cudaSetDevice(dev);
-    }
-  } restore{prev, device_};
   const int D = c.hidden, H = c.heads, Hkv = c.kv_heads, d = c.head_dim;
-  cudaError_t ce = cudaStreamSynchronize(s);  // the pinned id buffer is free again
-  if (ce != cudaSuccess) return cuda_fail(ce, "stream");
-  for (int t = 0; t < n; ++t) ids_h_[t] = static_cast<int32_t>(ids[t]);
-  ce = cudaMemcpyAsync(ids_d_, ids_h_, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s);
-  if (ce != cudaSuccess) return cuda_fail(ce, "token upload");
   const float scale = 1.0f / std::sqrt(static_cast<float>(d));  // attention.rs:206
   const int seq = pos_ + n;
-  if (obn_embed_f16(embed_, c.vocab, D, ids_d_, n, x_, s) != OBN_OK) return obn_fail("embedding");
+  if (obn_embed_f16(embed_, c.vocab, D, ids_dev, n, x_, s) != OBN_OK) return obn_fail("embedding");
   for (size_t i = 0; i < layers_.size(); ++i) {
     const Layer& L = layers_[i];
     if (obn_bitlinear_forward(L.qkv, x_, n, qkv_, ws_, ws_bytes_, s) != OBN_OK)
       return obn_fail("q|k|v projection");
-    if (obn_rope_kv_append(qkv_, 1, n, H, Hkv, d, pos_, c.rope_theta, q_, k_cache_[i],
-                           v_cache_[i], kMaxSeq, s) != OBN_OK)
-      return obn_fail("RoPE + KV append");
-    if (obn_attention_decode(q_, k_cache_[i], v_cache_[i], 1, n, H, Hkv, d, kMaxSeq, seq, scale,
-                             attn_, attn_ws_, attn_ws_bytes_, s) != OBN_OK)
-      return obn_fail("attention");
+    if (pos_dev) {
+      if (obn_rope_kv_append_at(qkv_, 1, n, H, Hkv, d, pos_dev, c.rope_theta, q_, k_cache_[i],
+                                v_cache_[i], kMaxSeq, s) != OBN_OK)
+        return obn_fail("RoPE + KV append");
+      if (obn_attention_decode_at(q_, k_cache_[i], v_cache_[i], 1, n, H, Hkv, d, kMaxSeq, pos_dev,
+                                  scale, attn_, attn_ws_, attn_ws_bytes_, s) != OBN_OK)
+        return obn_fail("attention");
+    } else {
+      if (obn_rope_kv_append(qkv_, 1, n, H, Hkv, d, pos_, c.rope_theta, q_, k_cache_[i],
+                             v_cache_[i], kMaxSeq, s) != OBN_OK)
+        return obn_fail("RoPE + KV append");
+      if (obn_attention_decode(q_, k_cache_[i], v_cache_[i], 1, n, H, Hkv, d, kMaxSeq, seq,
+                               scale, attn_, attn_ws_, attn_ws_bytes_, s) != OBN_OK)
+        return obn_fail("attention");
+    }
     if (obn_bitlinear_forward_residual(L.o, attn_, n, x_, ws_, ws_bytes_, s) != OBN_OK)
       return obn_fail("o_proj + residual");
     if (obn_bitlinear_forward(L.ffn_in, x_, n, ffn_, ws_, ws_bytes_, s) != OBN_OK)
@@ -478,7 +485,6 @@ std::string Model::run_chunk(const uint32_t* ids, int n, bool want_logits, bool 
     if (obn_bitlinear_forward_residual(L.down, ffn_, n, x_, ws_, ws_bytes_, s) != OBN_OK)
       return obn_fail("down_proj + residual");
   }
-  pos_ = seq;  // model.rs:231-232: the cache now holds the chunk
   if (!want_logits) return std::string();
   // model.rs:235-262: final RMSNorm and the LM head on the last position only.
   const float* last = x_ + static_cast<size_t>(n - 1) * D;
@@ -492,7 +498,68 @@ std::string Model::run_chunk(const uint32_t* ids, int n, bool want_logits, bool 
     if (obn_lm_head_f16(table, c.vocab, D, last, final_norm_, c.eps, 1, logits_d_, s) != OBN_OK)
       return obn_fail("LM head");
   }
-  if (!copy_logits) return std::string();
+  return std::string();
+}
+
+std::string Model::run_chunk(const uint32_t* ids, int n, bool want_logits, bool copy_logits) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream_);
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != device_) cudaSetDevice(device_);
+  struct Restore {
+    int dev, cur;
+    ~Restore() {
+      if (dev != cur) cudaSetDevice(dev);
+    }
+  } restore{prev, device_};
+  cudaError_t ce = cudaStreamSynchronize(s);  // the pinned input buffers are free again
+  if (ce != cudaSuccess) return cuda_fail(ce, "stream");
+  std::string e;
+  if (n == 1 && want_logits && use_graph_) {
+    // One decode step: the token and its position go to the device, then the
+    // whole step (every layer and the LM head) is one graph launch. The graph
+    // is captured at the second step (the first one, eager, has set up every
+    // kernel's attributes) and serves every later position.
+    step_h_[0] = static_cast<int32_t>(ids[0]);
+    step_h_[1] = pos_;
+    ce = cudaMemcpyAsync(step_d_, step_h_, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    if (ce != cudaSuccess) return cuda_fail(ce, "step upload");
+    if (!decode_exec_ && decode_steps_ >= 1) {
+      // A capture that fails (nothing was enqueued: the stream was capturing)
+      // leaves the model on eager steps.
+      cudaGraph_t g = nullptr;
+      cudaGraphExec_t ge = nullptr;
+      bool ok = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+      if (ok) {
+        ok = enqueue(1, step_d_, step_d_ + 1, true).empty();
+        ok = cudaStreamEndCapture(s, &g) == cudaSuccess && ok;
+        ok = ok && cudaGraphInstantiate(&ge, g, 0) == cudaSuccess;
+        if (g) cudaGraphDestroy(g);
+      }
+      if (ok) {
+        decode_exec_ = ge;
+      } else {
+        use_graph_ = false;
+        cudaGetLastError();
+      }
+    }
+    if (decode_exec_) {
+      ce = cudaGraphLaunch(static_cast<cudaGraphExec_t>(decode_exec_), s);
+      if (ce != cudaSuccess) return cuda_fail(ce, "graph launch");
+    } else {
+      e = enqueue(1, step_d_, step_d_ + 1, true);
+      if (!e.empty()) return e;
+    }
+    ++decode_steps_;
+  } else {
+    for (int t = 0; t < n; ++t) ids_h_[t] = static_cast<int32_t>(ids[t]);
+    ce = cudaMemcpyAsync(ids_d_, ids_h_, sizeof(int32_t) * n, cudaMemcpyHostToDevice, s);
+    if (ce != cudaSuccess) return cuda_fail(ce, "token upload");
+    e = enqueue(n, ids_d_, nullptr, want_logits);
+    if (!e.empty()) return e;
+  }
+  pos_ += n;  // model.rs:231-232: the cache now holds the chunk
+  if (!want_logits || !copy_logits) return std::string();
   return logits_to_host();
 }
 

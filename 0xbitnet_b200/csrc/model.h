@@ -95,6 +95,7 @@ class Model {
   std::string build(const gguf::File& f, const uint8_t* data, size_t size,
                     const ProgressFn& progress, const LogFn& log);
   std::string run_chunk(const uint32_t* ids, int n, bool want_logits, bool copy_logits);
+  std::string enqueue(int n, const int32_t* ids_dev, const int* pos_dev, bool want_logits);
   std::string logits_to_host();
 
   struct Layer {
@@ -131,6 +132,11 @@ class Model {
   uint32_t* recent_h_ = nullptr;        // pinned [kMaxSeq]
   void* sel_d_ = nullptr;               // count, then kSelCap ids, then kSelCap values
   void* sel_h_ = nullptr;               // pinned copy of sel_d_
+  int32_t* step_d_ = nullptr;           // decode step input: token id, position
+  int32_t* step_h_ = nullptr;           // pinned
+  void* decode_exec_ = nullptr;         // cudaGraphExec_t of one decode step
+  bool use_graph_ = true;
+  long long decode_steps_ = 0;
 };
 
 }  // namespace obn

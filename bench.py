@@ -55,6 +55,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--prefill", type=str, default="512,2048,8192",
                    help="config-2 token counts for the prefill TOPS block ('' to skip)")
+    p.add_argument("--no-generate", dest="generate", action="store_false",
+                   help="skip the end-to-end model (GGUF -> oxbitnet_generate_ids) run")
     p.add_argument("--no-decoder", dest="decoder", action="store_false",
                    help="skip the config-3 decoder tok/s block")
     p.add_argument("--tp-tokens", type=int, default=16384,
@@ -594,6 +596,82 @@ def measure_decoder(dev, stream, world, rank, ctx=2048, total_batch=64):
     return out
 
 
+def measure_generate(dev):
+    """Config 3 end to end through the drop-in model ABI (include/oxbitnet.h): a
+    random-init BitNet-2B GGUF (the reference's tensor names, I2_S ternary
+    weights, f16 tied embedding, synthetic 128256-token vocabulary) is written to
+    a temporary file, loaded with oxbitnet_load, and driven with
+    oxbitnet_forward (prefill) and oxbitnet_generate_ids (sampling with the
+    reference's default options: T 1.0, top-k 50, penalty 1.1 over 64 tokens).
+    Decode tok/s = generated tokens / wall time between the first and the last
+    token (host sampling and the per-token callback included)."""
+    import shutil
+    import tempfile
+
+    import numpy as np
+    W = importlib.import_module("0xbitnet_b200.gguf_writer")
+    ox = importlib.import_module("0xbitnet_b200.oxbitnet")
+    tmp = tempfile.mkdtemp(prefix="obn_gguf_")
+    out = {"model": "BitNet-2B shape (30 layers, 2560/6912, 20/5 heads x 128, vocab 128256), "
+                    "random weights, through oxbitnet_load / oxbitnet_forward / "
+                    "oxbitnet_generate_ids"}
+    try:
+        path = os.path.join(tmp, "bitnet2b.gguf")
+        t0 = time.perf_counter()
+        toks, merges, bos, eos = W.synthetic_vocab(128256)
+        W.write_bitnet_model(path, W.BitNetShape(), toks, merges, bos, eos, seed=0, fast=True)
+        out["file_gb"] = os.path.getsize(path) / 1e9
+        t1 = time.perf_counter()
+        m = ox.BitNet.load_sync(path)
+        out["load_s"] = time.perf_counter() - t1
+        out["write_s"] = t1 - t0
+        rng = np.random.default_rng(0)
+        prompt = [bos] + [int(x) for x in rng.integers(0, 128000, 511)]
+        m.forward(prompt, reset=True)
+        ts = []
+        for _ in range(3):
+            t = time.perf_counter()
+            m.forward(prompt, reset=True)
+            ts.append(time.perf_counter() - t)
+        out["prefill_tokens"] = len(prompt)
+        out["prefill_ms"] = min(ts) * 1e3
+        out["prefill_tok_s"] = len(prompt) / min(ts)
+        m.set_seed(1)
+        m.generate_ids(prompt[:16], max_tokens=8)  # warm-up (captures the decode graph)
+        stamps = []
+        n_new = 256
+
+        def timed(ids, max_tokens):
+            got = []
+            L = ox.lib()
+
+            def cb(i, _p, _n, _ud):
+                stamps.append(time.perf_counter())
+                got.append(i)
+                return 0
+            c = ox.TokenIdFn(cb)
+            arr = (ox._U32 * len(ids))(*ids)
+            o = ox.GenerateOptions(max_tokens, 1.0, 50, 1.1, 64)
+            if L.oxbitnet_generate_ids(m._handle(), arr, len(ids), ox.ctypes.byref(o), c,
+                                       None) != 0:
+                raise RuntimeError(ox.error_message())
+            return got
+        best = None
+        for _ in range(2):
+            stamps.clear()
+            got = timed(prompt[:16], n_new)
+            if len(got) > 1:
+                rate = (len(got) - 1) / (stamps[-1] - stamps[0])
+                best = rate if best is None else max(best, rate)
+        out["decode_tokens"] = n_new
+        out["decode_tok_s"] = best
+        out["decode_ms_per_token"] = 1e3 / best if best else None
+        m.dispose()
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    return out
+
+
 def measure_lm_head(obn, dev, stream, peak):
     """Next-row kernel: the f16 LM head of BitNet-2B (128256 x 2560, 656.7 MB) behind
     the final RMSNorm, one token as the reference runs it; the table exceeds L2, so
@@ -852,6 +930,7 @@ def run_ours(args):
     ffn_gate_up = measure_ffn_gate_up(args, obn, synth, dev, stream, batches)
     attention = measure_attention(dev, stream, peak, min(args.layers, 30))
     decoder = measure_decoder(dev, stream, world, rank) if args.decoder else None
+    generate = measure_generate(dev) if (args.generate and world == 1) else None
     tp_prefill = None
     if world > 1 and args.tp_tokens > 0:
         tp_prefill = measure_tp_prefill(args, obn, synth, dev, stream, world, rank)
@@ -883,6 +962,7 @@ def run_ours(args):
             "ffn_gate_up": ffn_gate_up,
             "attention_decode": attention,
             "decode_tok_s": decoder,
+            "generate": generate,
             "cpu_baseline": cpu,
             "clocks": clock_info,
             "e2e": {"value": e2e_value, "unit": "GB/s",

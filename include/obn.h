@@ -249,6 +249,20 @@ OBN_API int obn_attention_decode(const float* q, const void* k_cache, const void
                                  float scale, float* out, void* workspace,
                                  size_t workspace_bytes, void* stream);
 
+/* obn_rope_kv_append / obn_attention_decode with the position in device memory:
+ * `pos_dev` points to the int position of the first new token (the caches then
+ * hold *pos_dev + n positions after the append), read by the kernels, so one
+ * captured CUDA graph serves every decode step. A position with pos + n > S_max
+ * writes nothing and sees at most S_max keys. The attention workspace must hold
+ * obn_attention_workspace_bytes(B, n, H, head_dim, S_max) bytes. */
+OBN_API int obn_rope_kv_append_at(const float* qkv, int B, int n, int H, int Hkv, int head_dim,
+                                  const int* pos_dev, float theta_base, float* q_out,
+                                  void* k_cache, void* v_cache, int S_max, void* stream);
+OBN_API int obn_attention_decode_at(const float* q, const void* k_cache, const void* v_cache,
+                                    int B, int n, int H, int Hkv, int head_dim, int S_max,
+                                    const int* pos_dev, float scale, float* out, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
 /* ---- decoder glue ------------------------------------------------------------- */
 /* Residual add (elementwise.wgsl op 0, TransformerBlock::forward's dispatch_add,
  * transformer.rs:63,69): y[i] = a[i] + b[i] for i < count (f32; y may alias a or b). */
