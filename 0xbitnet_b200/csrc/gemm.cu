@@ -31,6 +31,7 @@
 #include <cuda.h>
 
 #include <cstdlib>
+#include <type_traits>
 
 #include "gemm.h"
 #include "layout.cuh"
@@ -316,9 +317,115 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
       const int mt = t % num_m, nt = t / num_m;
       const int a = ti & 1;
       const uint32_t aph = (ti >> 1) & 1u;
+      const int m = mt * kBM + quarter * 32 + lane;
+      if constexpr (OUT == kOutLocal) {
+        // The tile's per-token code sums and scales are kernel inputs: load them
+        // before waiting for the accumulator, lane l holding columns l, l + 32, ...
+        // (l, l + 16, ... when BN = 16), and broadcast each column by a shuffle.
+        constexpr int kCols = BN < 32 ? BN : 32;  // columns per TMEM load
+        constexpr int kChunks = BN / kCols;
+        int qsr[kChunks];
+        float sxr[kChunks];
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+          const int nl = nt * BN + c * kCols + (lane % kCols);
+          qsr[c] = nl < N ? qsum[nl] : 0;
+          sxr[c] = (nl < N && !acc_out) ? s_x[nl] : 0.0f;
+        }
+        const float sw = (m < M && !acc_out) ? s_w[m] : 0.0f;
+        if (!wait_or_abort(sm, &sm->accf[a], aph)) break;
+        tc_fence_after();
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
+        // Three store kinds, chosen once per tile so the plain store never carries
+        // a (speculated) read of y: int32 accumulators, y = val, y += val.
+        const int kind = acc_out ? 0 : (order & kOutAccumulate) ? 2 : 1;
+        const bool gemv_order = (order & 1) == kOrderGemv;
+        const bool full_tile = (nt + 1) * BN <= N && (mt + 1) * kBM <= M;
+        auto chunk = [&](auto kind_c) {
+          constexpr int K_ = decltype(kind_c)::value;
+          if (full_tile) {
+            // Every column and row in range: branch-free chunks, the 2 * kCols
+            // broadcasts first, so the conversions, products and stores of a
+            // chunk issue back to back instead of one column's chain at a time.
+#pragma unroll
+            for (int c = 0; c < kChunks; ++c) {
+              uint32_t v[kCols];
+              if constexpr (kCols == 32)
+                tmem_ld32(taddr + c * 32, v);
+              else
+                tmem_ld16(taddr + c * 16, v);
+              int qs_v[kCols];
+              float sx_v[kCols];
+#pragma unroll
+              for (int j = 0; j < kCols; ++j) {
+                qs_v[j] = __shfl_sync(0xffffffffu, qsr[c], j);
+                sx_v[j] = __shfl_sync(0xffffffffu, sxr[c], j);
+              }
+              tmem_ld_wait();
+              const size_t o0 = static_cast<size_t>(nt * BN + c * kCols) * M + m;
+#pragma unroll
+              for (int j = 0; j < kCols; ++j) {
+                const int d = static_cast<int>(v[j]) - qs_v[j];
+                const size_t o = o0 + static_cast<size_t>(j) * M;
+                if constexpr (K_ == 0) {
+                  acc_out[o] = d;
+                } else {
+                  const float fd = static_cast<float>(d);
+                  const float val = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx_v[j])
+                                               : __fmul_rn(fd, __fmul_rn(sw, sx_v[j]));
+                  if constexpr (K_ == 2)
+                    y[o] = __fadd_rn(y[o], val);
+                  else
+                    y[o] = val;
+                }
+              }
+            }
+            return;
+          }
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) {
+            uint32_t v[kCols];
+            if constexpr (kCols == 32)
+              tmem_ld32(taddr + c * 32, v);
+            else
+              tmem_ld16(taddr + c * 16, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) {
+              const int n = nt * BN + c * kCols + j;
+              const int qs_j = __shfl_sync(0xffffffffu, qsr[c], j);
+              const float sx_j = __shfl_sync(0xffffffffu, sxr[c], j);
+              if (n < N && m < M) {
+                const int d = static_cast<int>(v[j]) - qs_j;
+                const size_t o = static_cast<size_t>(n) * M + m;
+                if constexpr (K_ == 0) {
+                  acc_out[o] = d;
+                } else {
+                  const float fd = static_cast<float>(d);
+                  const float val = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx_j)
+                                               : __fmul_rn(fd, __fmul_rn(sw, sx_j));
+                  if constexpr (K_ == 2)
+                    y[o] = __fadd_rn(y[o], val);
+                  else
+                    y[o] = val;
+                }
+              }
+            }
+          }
+        };
+        if (kind == 0)
+          chunk(std::integral_constant<int, 0>());
+        else if (kind == 1)
+          chunk(std::integral_constant<int, 1>());
+        else
+          chunk(std::integral_constant<int, 2>());
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm->acce[a]);
+        continue;
+      }
       if (!wait_or_abort(sm, &sm->accf[a], aph)) break;
       tc_fence_after();
-      const int m = mt * kBM + quarter * 32 + lane;
       const float sw = (m < M && !acc_out) ? s_w[m] : 0.0f;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
 #pragma unroll 1
