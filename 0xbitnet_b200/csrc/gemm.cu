@@ -867,7 +867,12 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
   const int nrows = (row0 + RB <= kBM ? RB : kBM - row0);
   const int nrb = (nrows + 31) >> 5;  // 1 or 2 row blocks (RB <= 64)
   const int ngrp = min(BN, N + 3) >> 2;
-  if (ok) {
+  // The store kind (int32 accumulators, y = val, y += val) is fixed per launch and
+  // compiled separately, so a plain store never carries a speculated read of y.
+  const int kind = acc_out ? 0 : (order & kOutAccumulate) ? 2 : 1;
+  const bool gemv_order = (order & 1) == kOrderGemv;
+  auto reduce = [&](auto kind_c) {
+    constexpr int K_ = decltype(kind_c)::value;
     for (int item = warp; item < nrb * ngrp; item += kThreads / 32) {
       const int rb = item % nrb, grp = item / nrb;
       const int rr = rb * 32 + lane;
@@ -894,17 +899,28 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
         if (j >= N) break;
         const int d = sum[c] - e_qs[j];
         const size_t o = static_cast<size_t>(j) * M + m;
-        if (acc_out) {
+        if constexpr (K_ == 0) {
           acc_out[o] = d;
         } else {
           const float fd = static_cast<float>(d);
           const float sx = e_sx[j];
-          const float val = (order & 1) == kOrderGemv ? __fmul_rn(__fmul_rn(fd, sw), sx)
-                                                      : __fmul_rn(fd, __fmul_rn(sw, sx));
-          y[o] = (order & kOutAccumulate) ? __fadd_rn(y[o], val) : val;
+          const float val = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx)
+                                       : __fmul_rn(fd, __fmul_rn(sw, sx));
+          if constexpr (K_ == 2)
+            y[o] = __fadd_rn(y[o], val);
+          else
+            y[o] = val;
         }
       }
     }
+  };
+  if (ok) {
+    if (kind == 0)
+      reduce(std::integral_constant<int, 0>());
+    else if (kind == 1)
+      reduce(std::integral_constant<int, 1>());
+    else
+      reduce(std::integral_constant<int, 2>());
   }
 
   tc_fence_before();

@@ -178,16 +178,19 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant(const float* __restrict__
 
 // Single-pass variant for d <= 256 * EPT: gamma is fetched into registers
 // before the PDL wait (it never depends on earlier kernels), x is loaded once
-// (thread t owns columns t + 256 j, the shaders' lane mapping), and the scalar
-// divisions run in one thread and are broadcast.
+// (thread t owns columns t + 256 j, the shaders' lane mapping), and the chain
+// after the wait has three block barriers: the per-thread sums of squares meet
+// in shared memory once and every warp finishes the shaders' halving tree and
+// the scalar divisions itself (as k_bitlinear_n1 does), the warp maxima meet
+// once and every thread derives the scale, the warp code sums meet once.
 template <int EPT, bool NORM>
 __global__ __launch_bounds__(256) void k_rmsnorm_quant_reg(const float* __restrict__ x,
                                                            const float* __restrict__ w, float eps,
                                                            int d, int8_t* __restrict__ q,
                                                            float* __restrict__ scales,
                                                            int32_t* __restrict__ qsum) {
-  __shared__ float shf[256];
-  __shared__ float scal[3];
+  __shared__ float sh_ss[256];
+  __shared__ float sh_max[8];
   __shared__ int shi[8];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float g[EPT];
@@ -211,11 +214,19 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant_reg(const float* __restri
 #pragma unroll
     for (int j = 0; j < EPT; ++j)
       if (tid + 256 * j < d) part = __fadd_rn(part, __fmul_rn(xv[j], xv[j]));
-    const float total = tree_sum_256(part, shf);
-    if (tid == 0)
-      scal[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(d)), eps)));
+    sh_ss[tid] = part;
     __syncthreads();
-    const float rms = scal[0];
+    // lane l: strides 128, 64, 32 of the tree for shader lane l, then 16 .. 1
+    const float* p = sh_ss + lane;
+    const float b0 = __fadd_rn(__fadd_rn(p[0], p[128]), __fadd_rn(p[64], p[192]));
+    const float b1 = __fadd_rn(__fadd_rn(p[32], p[160]), __fadd_rn(p[96], p[224]));
+    float tsum = __fadd_rn(b0, b1);
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1)
+      tsum = __fadd_rn(tsum, __shfl_down_sync(0xffffffffu, tsum, s));
+    const float total = __shfl_sync(0xffffffffu, tsum, 0);
+    const float rms =
+        __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(d)), eps)));
 #pragma unroll
     for (int j = 0; j < EPT; ++j)
       if (tid + 256 * j < d) xv[j] = norm_mul(xv[j], rms, g[j]);
@@ -225,17 +236,12 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant_reg(const float* __restri
   for (int j = 0; j < EPT; ++j) lmax = fmaxf(lmax, fabsf(xv[j]));
 #pragma unroll
   for (int s = 16; s >= 1; s >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, s));
-  if (lane == 0) shf[warp] = lmax;
+  if (lane == 0) sh_max[warp] = lmax;
   __syncthreads();
-  if (tid == 0) {
-    float absmax = shf[0];
+  float absmax = sh_max[0];
 #pragma unroll
-    for (int i = 1; i < 8; ++i) absmax = fmaxf(absmax, shf[i]);
-    scal[1] = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
-    scal[2] = absmax == 0.0f ? 0.0f : __fdiv_rn(127.0f, absmax);
-  }
-  __syncthreads();
-  const float inv = scal[2];
+  for (int i = 1; i < 8; ++i) absmax = fmaxf(absmax, sh_max[i]);
+  const float inv = absmax == 0.0f ? 0.0f : __fdiv_rn(127.0f, absmax);
   int8_t* qr = q + row * d;
   int lsum = 0;
 #pragma unroll
@@ -255,7 +261,7 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant_reg(const float* __restri
     int t = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) t += shi[i];
-    scales[row] = scal[1];
+    scales[row] = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
     if (qsum) qsum[row] = t;
   }
 }
