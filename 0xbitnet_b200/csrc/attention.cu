@@ -32,6 +32,7 @@ namespace obn {
 namespace {
 
 constexpr int kAttnThreads = 128;
+constexpr int kMaxSplits = 4096 / kAttnChunk;  // combine: splits held in registers
 constexpr int kKStride = kAttnHeadDim + 8;  // halves per smem K row: 16-byte rows, no conflicts
 
 __global__ __launch_bounds__(256) void k_rope_kv_append(const float* __restrict__ qkv, int n,
@@ -112,10 +113,10 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
     float* __restrict__ part_m, float* __restrict__ part_l) {
   constexpr int D = kAttnHeadDim;
   extern __shared__ __align__(16) unsigned char smem[];
-  __half* sK = reinterpret_cast<__half*>(smem);                       // [128][kKStride]
-  __half* sV = sK + kAttnChunk * kKStride;                            // [128][D]
-  float* sQ = reinterpret_cast<float*>(sV + kAttnChunk * D);          // [G][D]
-  float* sP = sQ + G * D;                                             // [G][128]
+  __half* sK = reinterpret_cast<__half*>(smem);                       // [chunk][kKStride]
+  __half* sV = sK + kAttnChunk * kKStride;                            // [chunk][D]
+  float* sQ = reinterpret_cast<float*>(sV + kAttnChunk * D);          // [D][G]
+  float* sP = sQ + G * D;                                             // [chunk keys][G]
   __shared__ float red[G][kAttnThreads / 32];
   pdl_launch_dependents();
   pdl_wait();
@@ -144,8 +145,10 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
     return;
   }
   // q rows of the group's heads, and the chunk's K and V rows (16-byte loads).
-  for (int e = tid; e < G * D; e += kAttnThreads)
-    sQ[e] = q[(r * H + static_cast<size_t>(kvh) * G) * D + e];
+  for (int e = tid; e < G * D; e += kAttnThreads) {  // e = g * D + dim -> sQ[dim][g]
+    const int g = e / D, dim = e % D;
+    sQ[dim * G + g] = q[(r * H + static_cast<size_t>(kvh) * G) * D + e];
+  }
   // Asynchronous 16-byte copies (no register held): K in one group, V in a second
   // one that lands while the scores are computed.
 #pragma unroll 4
@@ -171,10 +174,28 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
   cp_async_wait_group<1>();  // K landed (V may still be in flight)
   __syncthreads();
   // Scores: thread = key, the dot sequential over d (attention.wgsl:48-51).
+  static_assert(kAttnThreads == kAttnChunk, "one thread per key");
   float sc[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) sc[g] = 0.0f;
   const __half* krow = sK + tid * kKStride;
+  // q of dims d and d + 1 for every head: G floats each, read as one broadcast
+  // (16-byte words for G >= 4).
+  auto qload = [&](int dim, float (&qv)[G]) {
+    if constexpr (G % 4 == 0) {
+#pragma unroll
+      for (int g4 = 0; g4 < G; g4 += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(sQ + dim * G + g4);
+        qv[g4] = t.x;
+        qv[g4 + 1] = t.y;
+        qv[g4 + 2] = t.z;
+        qv[g4 + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; ++g) qv[g] = sQ[dim * G + g];
+    }
+  };
 #pragma unroll 4
   for (int d8 = 0; d8 < D; d8 += 8) {
     const uint4 w = *reinterpret_cast<const uint4*>(krow + d8);
@@ -182,10 +203,13 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float2 kf = __half22float2(h2[e]);
+      float q0[G], q1[G];
+      qload(d8 + 2 * e, q0);
+      qload(d8 + 2 * e + 1, q1);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        sc[g] = __fadd_rn(sc[g], __fmul_rn(sQ[g * D + d8 + 2 * e], kf.x));
-        sc[g] = __fadd_rn(sc[g], __fmul_rn(sQ[g * D + d8 + 2 * e + 1], kf.y));
+        sc[g] = __fadd_rn(sc[g], __fmul_rn(q0[g], kf.x));
+        sc[g] = __fadd_rn(sc[g], __fmul_rn(q1[g], kf.y));
       }
     }
   }
@@ -206,7 +230,7 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     const float p = valid ? expf(sc[g] - mg[g]) : 0.0f;
-    sP[g * kAttnChunk + tid] = p;
+    sP[tid * G + g] = p;
     const float ws = warp_sum(p);
     if (lane == 0) red[g][warp] = ws;
   }
@@ -219,8 +243,22 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
   for (int g = 0; g < G; ++g) acc[g] = 0.0f;
   for (int key = 0; key < cnt; ++key) {
     const float v = __half2float(sV[key * D + tid]);
+    float pk[G];
+    if constexpr (G % 4 == 0) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = __fadd_rn(acc[g], __fmul_rn(sP[g * kAttnChunk + key], v));
+      for (int g4 = 0; g4 < G; g4 += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(sP + key * G + g4);
+        pk[g4] = t.x;
+        pk[g4 + 1] = t.y;
+        pk[g4 + 2] = t.z;
+        pk[g4 + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; ++g) pk[g] = sP[key * G + g];
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = __fadd_rn(acc[g], __fmul_rn(pk[g], v));
   }
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -248,12 +286,35 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_combine(const float* __re
   // splits that hold keys (all of them unless the position is read on the device)
   const int nvalid =
       pos_dev ? min(nsplit, (min(*pos_dev + n, S_max) + kAttnChunk - 1) / kAttnChunk) : nsplit;
+  // Every split's (m, l) in shared memory, every thread's accumulator values in
+  // flight before the first dependent step; then the rescaling in split order.
+  __shared__ float s_m[kMaxSplits], s_l[kMaxSplits];
+  const int nfast = min(nvalid, kMaxSplits);  // longer caches: the rest one by one
+  for (int c = tid; c < nfast; c += kAttnThreads) {
+    s_m[c] = part_m[rh * nsplit + c];
+    s_l[c] = part_l[rh * nsplit + c];
+  }
+  float av[kMaxSplits];
+#pragma unroll
+  for (int c = 0; c < kMaxSplits; ++c)
+    av[c] = c < nfast ? part_acc[(rh * nsplit + c) * D + tid] : 0.0f;
+  __syncthreads();
   float M = -FLT_MAX;
-  for (int c = 0; c < nvalid; ++c) M = fmaxf(M, part_m[rh * nsplit + c]);
+  for (int c = 0; c < nfast; ++c) M = fmaxf(M, s_m[c]);
+  for (int c = nfast; c < nvalid; ++c) M = fmaxf(M, part_m[rh * nsplit + c]);
   float L = 0.0f, o = 0.0f;
-  for (int c = 0; c < nvalid; ++c) {
-    const float l = part_l[rh * nsplit + c];
+#pragma unroll
+  for (int c = 0; c < kMaxSplits; ++c) {
+    if (c >= nfast) break;
+    const float l = s_l[c];
     if (l == 0.0f) continue;  // an empty chunk
+    const float w = expf(s_m[c] - M);
+    L = fmaf(w, l, L);
+    o = fmaf(w, av[c], o);
+  }
+  for (int c = nfast; c < nvalid; ++c) {
+    const float l = part_l[rh * nsplit + c];
+    if (l == 0.0f) continue;
     const float w = expf(part_m[rh * nsplit + c] - M);
     L = fmaf(w, l, L);
     o = fmaf(w, part_acc[(rh * nsplit + c) * D + tid], o);

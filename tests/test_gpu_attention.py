@@ -51,7 +51,8 @@ def test_rope_kv_append(B, n, H, Hkv, pos):
 
 @pytest.mark.parametrize("B,n,H,Hkv,S", [(1, 1, 20, 5, 1), (1, 1, 20, 5, 2048), (3, 1, 20, 5, 700),
                                          (2, 5, 20, 5, 300), (1, 7, 8, 8, 7), (2, 1, 16, 2, 129),
-                                         (1, 130, 4, 1, 260)])
+                                         (1, 130, 4, 1, 260), (1, 1, 20, 5, 5000),
+                                         (1, 1, 16, 8, 4096), (2, 1, 4, 4, 33)])
 def test_attention_matches_oracle(B, n, H, Hkv, S):
     torch = need_cuda()
     S_max = S + 3
