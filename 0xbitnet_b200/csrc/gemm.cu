@@ -866,7 +866,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
   const int row0 = static_cast<int>(rank) * RB;
   const int nrows = (row0 + RB <= kBM ? RB : kBM - row0);
   const int nrb = (nrows + 31) >> 5;  // 1 or 2 row blocks (RB <= 64)
-  const int ngrp = min(BN, N + 3) >> 2;
+  const int ngrp = (min(BN, N) + 7) >> 3;  // 8-column groups
   // The store kind (int32 accumulators, y = val, y += val) is fixed per launch and
   // compiled separately, so a plain store never carries a speculated read of y.
   const int kind = acc_out ? 0 : (order & kOutAccumulate) ? 2 : 1;
@@ -874,43 +874,59 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
   auto reduce = [&](auto kind_c) {
     constexpr int K_ = decltype(kind_c)::value;
     for (int item = warp; item < nrb * ngrp; item += kThreads / 32) {
-      const int rb = item % nrb, grp = item / nrb;
+      const int rb = item & (nrb - 1), grp = item >> (nrb - 1);  // nrb is 1 or 2
       const int rr = rb * 32 + lane;
       const int m = mt * kBM + row0 + rr;
       if (rr >= nrows || m >= M) continue;
-      const int j0 = 4 * grp;
-      uint4 pv[8];
-#pragma unroll
-      for (uint32_t src = 0; src < 8; ++src)
-        if (src < S) pv[src] = *reinterpret_cast<const uint4*>(red + (src * RB + rr) * BNP + j0);
-      int sum[4] = {0, 0, 0, 0};
+      const int j0 = 8 * grp;
+      // Every source rank's two 16-byte runs and the column scalars in flight
+      // before the first sum.
+      uint4 pa[8], pb[8];
 #pragma unroll
       for (uint32_t src = 0; src < 8; ++src)
         if (src < S) {
-          sum[0] += static_cast<int>(pv[src].x);
-          sum[1] += static_cast<int>(pv[src].y);
-          sum[2] += static_cast<int>(pv[src].z);
-          sum[3] += static_cast<int>(pv[src].w);
+          const int32_t* rp = red + (src * RB + rr) * BNP + j0;
+          pa[src] = *reinterpret_cast<const uint4*>(rp);
+          pb[src] = *reinterpret_cast<const uint4*>(rp + 4);
         }
+      const int4 qa = *reinterpret_cast<const int4*>(e_qs + j0);
+      const int4 qb = *reinterpret_cast<const int4*>(e_qs + j0 + 4);
+      const float4 xa = *reinterpret_cast<const float4*>(e_sx + j0);
+      const float4 xb = *reinterpret_cast<const float4*>(e_sx + j0 + 4);
       const float sw = e_sw[row0 + rr];
+      int sum[8] = {-qa.x, -qa.y, -qa.z, -qa.w, -qb.x, -qb.y, -qb.z, -qb.w};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int j = j0 + c;
-        if (j >= N) break;
-        const int d = sum[c] - e_qs[j];
-        const size_t o = static_cast<size_t>(j) * M + m;
+      for (uint32_t src = 0; src < 8; ++src)
+        if (src < S) {
+          sum[0] += static_cast<int>(pa[src].x);
+          sum[1] += static_cast<int>(pa[src].y);
+          sum[2] += static_cast<int>(pa[src].z);
+          sum[3] += static_cast<int>(pa[src].w);
+          sum[4] += static_cast<int>(pb[src].x);
+          sum[5] += static_cast<int>(pb[src].y);
+          sum[6] += static_cast<int>(pb[src].z);
+          sum[7] += static_cast<int>(pb[src].w);
+        }
+      const float sx[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+      auto put = [&](int c) {
+        const size_t o = static_cast<size_t>(j0 + c) * M + m;
         if constexpr (K_ == 0) {
-          acc_out[o] = d;
+          acc_out[o] = sum[c];
         } else {
-          const float fd = static_cast<float>(d);
-          const float sx = e_sx[j];
-          const float val = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx)
-                                       : __fmul_rn(fd, __fmul_rn(sw, sx));
+          const float fd = static_cast<float>(sum[c]);
+          const float val = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx[c])
+                                       : __fmul_rn(fd, __fmul_rn(sw, sx[c]));
           if constexpr (K_ == 2)
             y[o] = __fadd_rn(y[o], val);
           else
             y[o] = val;
         }
+      };
+      if (j0 + 8 <= N) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) put(c);
+      } else {
+        for (int c = 0; c < 8 && j0 + c < N; ++c) put(c);
       }
     }
   };
