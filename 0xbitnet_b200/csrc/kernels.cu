@@ -183,10 +183,14 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant(const float* __restrict__
 // in shared memory once and every warp finishes the shaders' halving tree and
 // the scalar divisions itself (as k_bitlinear_n1 does), the warp maxima meet
 // once and every thread derives the scale, the warp code sums meet once.
+// Persistent over tokens (row, row + gridDim.x, ...): the next token's x is in
+// flight while the current one is reduced, and gamma is loaded once per CTA.
+// The shared slots need no extra barrier between tokens: each is rewritten only
+// after a barrier that every reader of its previous contents has passed.
 template <int EPT, bool NORM>
 __global__ __launch_bounds__(256) void k_rmsnorm_quant_reg(const float* __restrict__ x,
                                                            const float* __restrict__ w, float eps,
-                                                           int d, int8_t* __restrict__ q,
+                                                           int d, int n, int8_t* __restrict__ q,
                                                            float* __restrict__ scales,
                                                            int32_t* __restrict__ qsum) {
   __shared__ float sh_ss[256];
@@ -201,13 +205,22 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant_reg(const float* __restri
   }
   pdl_launch_dependents();
   pdl_wait();  // x may be the previous kernel's output
-  const size_t row = blockIdx.x;
-  const float* xr = x + row * d;
+  size_t row = blockIdx.x;
+  if (row >= static_cast<size_t>(n)) return;  // uniform per CTA
   float xv[EPT];
 #pragma unroll
   for (int j = 0; j < EPT; ++j) {
     const int col = tid + 256 * j;
-    xv[j] = col < d ? xr[col] : 0.0f;
+    xv[j] = col < d ? x[row * d + col] : 0.0f;
+  }
+  for (;;) {
+  const size_t next = row + gridDim.x;
+  const bool more = next < static_cast<size_t>(n);
+  float xn[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int col = tid + 256 * j;
+    xn[j] = (more && col < d) ? x[next * d + col] : 0.0f;
   }
   if (NORM) {
     float part = 0.0f;  // rmsnorm.wgsl:41-45
@@ -263,6 +276,11 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant_reg(const float* __restri
     for (int i = 0; i < 8; ++i) t += shi[i];
     scales[row] = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
     if (qsum) qsum[row] = t;
+  }
+  if (!more) break;
+  row = next;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) xv[j] = xn[j];
   }
 }
 
@@ -686,14 +704,31 @@ cudaError_t launch_export_i2s(const uint8_t* t256, uint8_t* rows, int M, int K, 
   return cudaGetLastError();
 }
 
+// SM count of the current device (cached per device).
+int num_sms_cached() {
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  return sms[dev] ? sms[dev] : 148;
+}
+
 template <int EPT>
 cudaError_t rmsnorm_quant_ept(const float* x, const float* norm_w, float eps, int n, int d,
                               int8_t* q, float* scales, int32_t* qsum, cudaStream_t s) {
-  if (norm_w)
-    return launch_pdl(k_rmsnorm_quant_reg<EPT, true>, dim3(n), dim3(256), 0, s, x, norm_w, eps, d,
-                      q, scales, qsum);
-  return launch_pdl(k_rmsnorm_quant_reg<EPT, false>, dim3(n), dim3(256), 0, s, x, norm_w, eps, d,
-                    q, scales, qsum);
+  auto kern = norm_w ? k_rmsnorm_quant_reg<EPT, true> : k_rmsnorm_quant_reg<EPT, false>;
+  // One CTA per token up to the resident capacity, then persistent CTAs.
+  static int cap[2] = {0, 0};
+  int& c = cap[norm_w ? 1 : 0];
+  if (c == 0) {
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0);
+    if (e != cudaSuccess) return e;
+    c = (per_sm > 0 ? per_sm : 1) * num_sms_cached();
+  }
+  const int grid = n < c ? n : c;
+  return launch_pdl(kern, dim3(grid), dim3(256), 0, s, x, norm_w, eps, d, n, q, scales, qsum);
 }
 
 cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps, int n, int d,
