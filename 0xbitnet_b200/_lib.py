@@ -53,6 +53,10 @@ SIGNATURES = {
     "obn_rope_kv_append_at": (_I, [_P, _I, _I, _I, _I, _I, _P, _F, _P, _P, _P, _I, _P]),
     "obn_attention_decode_at": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _P, _F, _P, _P, _SZ,
                                      _P]),
+    "obn_attention_decode_rope": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _F, _F, _P, _P, _SZ,
+                                       _P]),
+    "obn_attention_decode_rope_at": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _F, _F, _P, _P,
+                                          _SZ, _P]),
     "obn_add": (_I, [_P, _P, _SZ, _P, _P]),
     "obn_embed_f16": (_I, [_P, _I, _I, _P, _I, _P, _P]),
     "obn_rmsnorm_quantize": (_I, [_P, _P, _F, _I, _I, _P, _P, _P, _P]),

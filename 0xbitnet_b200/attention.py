@@ -70,3 +70,25 @@ def attention(q: torch.Tensor, cache: KVCache, H: int, n: int, seq_len: int,
                                      cache.Hkv, d, cache.S_max, seq_len, ctypes.c_float(sc),
                                      _ptr(out), _ptr(ws), ws.numel(), _stream(q.device)))
     return out
+
+
+def attention_rope(qkv: torch.Tensor, cache: KVCache, H: int, pos: int,
+                   theta_base: float = 500000.0, scale: float | None = None,
+                   out: torch.Tensor | None = None,
+                   workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode token per sequence: RoPE + KV append + attention in one pass
+    (bit-identical to rope_kv_append then attention with n = 1). qkv [B,
+    (H + 2*Hkv) * d] unrotated -> out [B, H*d]; the token sits at position pos."""
+    d = cache.head_dim
+    sc = float(np.float32(1.0) / np.sqrt(np.float32(d))) if scale is None else scale
+    out = out if out is not None else torch.empty((cache.B, H * d), dtype=torch.float32,
+                                                  device=qkv.device)
+    need = int(lib().obn_attention_workspace_bytes(cache.B, 1, H, d, pos + 1))
+    ws = workspace if workspace is not None and workspace.numel() >= need else \
+        torch.empty(max(need, 1), dtype=torch.uint8, device=qkv.device)
+    check(lib().obn_attention_decode_rope(_ptr(qkv), _ptr(cache.k), _ptr(cache.v), cache.B, H,
+                                          cache.Hkv, d, cache.S_max, pos,
+                                          ctypes.c_float(theta_base), ctypes.c_float(sc),
+                                          _ptr(out), _ptr(ws), ws.numel(), _stream(qkv.device)))
+    cache.seq_len = max(cache.seq_len, pos + 1)
+    return out

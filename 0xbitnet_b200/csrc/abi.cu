@@ -798,6 +798,55 @@ int obn_attention_decode_at(const float* q, const void* k_cache, const void* v_c
   return OBN_OK;
 }
 
+namespace {
+int attention_rope_common(const float* qkv, void* k_cache, void* v_cache, int B, int H, int Hkv,
+                          int head_dim, int S_max, int pos, const int* pos_dev, float theta_base,
+                          float scale, float* out, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  if (!qkv || !k_cache || !v_cache || !out || !workspace)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (B <= 0 || H <= 0 || Hkv <= 0 || S_max <= 0 || (!pos_dev && (pos < 0 || pos >= S_max)))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "need B, H, Hkv > 0 and 0 <= pos < S_max");
+  if (head_dim != obn::kAttnHeadDim)
+    return fail(OBN_ERR_UNSUPPORTED, "head_dim must be %d (got %d)", obn::kAttnHeadDim, head_dim);
+  const int G = H % Hkv == 0 ? H / Hkv : 0;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return fail(OBN_ERR_UNSUPPORTED, "H / Hkv must be 1, 2, 4 or 8 (got %d / %d)", H, Hkv);
+  const size_t need =
+      obn::attention_workspace_bytes(B, 1, H, head_dim, pos_dev ? S_max : pos + 1);
+  if (workspace_bytes < need)
+    return fail(OBN_ERR_INVALID_ARGUMENT, "workspace of %zu bytes is smaller than the %zu needed",
+                workspace_bytes, need);
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(workspace, 256) ||
+      !aligned(qkv, 8) || !aligned(out, 4) || (pos_dev && !aligned(pos_dev, 4)))
+    return fail(OBN_ERR_INVALID_ARGUMENT, "caches must be 16-byte, workspace 256-byte aligned");
+  cudaError_t e = obn::launch_attention_rope(
+      qkv, static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), B, H, Hkv, head_dim,
+      S_max, pos, theta_base, scale, out, workspace, static_cast<cudaStream_t>(stream), pos_dev);
+  if (e != cudaSuccess) return cuda_fail(e, "fused rope + attention launch");
+  return OBN_OK;
+}
+}  // namespace
+
+int obn_attention_decode_rope(const float* qkv, void* k_cache, void* v_cache, int B, int H,
+                              int Hkv, int head_dim, int S_max, int pos, float theta_base,
+                              float scale, float* out, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  clear_error();
+  return attention_rope_common(qkv, k_cache, v_cache, B, H, Hkv, head_dim, S_max, pos, nullptr,
+                               theta_base, scale, out, workspace, workspace_bytes, stream);
+}
+
+int obn_attention_decode_rope_at(const float* qkv, void* k_cache, void* v_cache, int B, int H,
+                                 int Hkv, int head_dim, int S_max, const int* pos_dev,
+                                 float theta_base, float scale, float* out, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  clear_error();
+  if (!pos_dev) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
+  return attention_rope_common(qkv, k_cache, v_cache, B, H, Hkv, head_dim, S_max, 0, pos_dev,
+                               theta_base, scale, out, workspace, workspace_bytes, stream);
+}
+
 int obn_add(const float* a, const float* b, size_t count, float* y, void* stream) {
   clear_error();
   if (!a || !b || !y) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");

@@ -35,6 +35,19 @@ constexpr int kAttnThreads = 128;
 constexpr int kMaxSplits = 4096 / kAttnChunk;  // combine: splits held in registers
 constexpr int kKStride = kAttnHeadDim + 8;  // halves per smem K row: 16-byte rows, no conflicts
 
+// rope.wgsl:41-55 for the pair (x0, x1) = dims (2i, 2i + 1) of a head at
+// position p: theta = p * base^(-2i/d), then the rotation with products and
+// sums rounded as written.
+OBN_DEVINL void rope_pair(float x0, float x1, int i, int d, int p, float theta_base, float* y0,
+                          float* y1) {
+  const float freq_exp = __fdiv_rn(__fmul_rn(-2.0f, static_cast<float>(i)), static_cast<float>(d));
+  const float theta = __fmul_rn(static_cast<float>(p), powf(theta_base, freq_exp));
+  float sn, c;
+  sincosf(theta, &sn, &c);
+  *y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+  *y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+}
+
 __global__ __launch_bounds__(256) void k_rope_kv_append(const float* __restrict__ qkv, int n,
                                                         int H, int Hkv, int d, int pos,
                                                         const int* __restrict__ pos_dev,
@@ -63,13 +76,8 @@ __global__ __launch_bounds__(256) void k_rope_kv_append(const float* __restrict_
     *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(x0, x1);
     return;
   }
-  // rope.wgsl:41-55
-  const float freq_exp = __fdiv_rn(__fmul_rn(-2.0f, static_cast<float>(i)), static_cast<float>(d));
-  const float theta = __fmul_rn(static_cast<float>(p), powf(theta_base, freq_exp));
-  float sn, c;
-  sincosf(theta, &sn, &c);
-  const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
-  const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+  float y0, y1;
+  rope_pair(x0, x1, i, d, p, theta_base, &y0, &y1);
   if (j < H) {
     float* dst = q_out + (r * H + j) * d + 2 * i;
     dst[0] = y0;
@@ -105,12 +113,17 @@ OBN_DEVINL float warp_sum(float v) {
 
 // Partials layout (workspace): for row r, head h, split c:
 //   acc[((r * H + h) * nsplit + c) * D + dim], then m[...] and l[...] after all acc.
-template <int G>
+// ROPE (decode, n = 1): q is the merged QKV row instead of rotated q; the CTA
+// rotates its group's q heads itself (the same rope_pair as k_rope_kv_append),
+// and the CTA whose chunk holds the new position also rotates the new key,
+// stores key and value into the caches and places them in its shared tiles
+// directly. That removes the separate RoPE launch from every decode step.
+template <int G, bool ROPE = false>
 __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
     const float* __restrict__ q, const __half* __restrict__ k_cache,
     const __half* __restrict__ v_cache, int n, int H, int Hkv, int S_max, int seq_len,
     const int* __restrict__ pos_dev, float scale, int nsplit, float* __restrict__ part_acc,
-    float* __restrict__ part_m, float* __restrict__ part_l) {
+    float* __restrict__ part_m, float* __restrict__ part_l, float theta_base) {
   constexpr int D = kAttnHeadDim;
   extern __shared__ __align__(16) unsigned char smem[];
   __half* sK = reinterpret_cast<__half*>(smem);                       // [chunk][kKStride]
@@ -145,9 +158,45 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
     return;
   }
   // q rows of the group's heads, and the chunk's K and V rows (16-byte loads).
-  for (int e = tid; e < G * D; e += kAttnThreads) {  // e = g * D + dim -> sQ[dim][g]
-    const int g = e / D, dim = e % D;
-    sQ[dim * G + g] = q[(r * H + static_cast<size_t>(kvh) * G) * D + e];
+  // ROPE: the new token's position (n = 1); one past the cache appends nothing
+  const int p_new = ROPE ? (pos_dev ? *pos_dev : seq_len - 1) : 0;
+  const int new_row =
+      (ROPE && p_new < S_max && p_new >= s0 && p_new < s0 + kAttnChunk) ? p_new - s0 : -1;
+  if constexpr (ROPE) {
+    const int slots = H + 2 * Hkv;
+    const float* qrow = q + r * static_cast<size_t>(slots) * D;
+    for (int e = tid; e < G * (D / 2); e += kAttnThreads) {
+      const int g = e / (D / 2), i = e % (D / 2);
+      const float* src = qrow + (static_cast<size_t>(kvh) * G + g) * D + 2 * i;
+      float y0, y1;
+      rope_pair(src[0], src[1], i, D, p_new, theta_base, &y0, &y1);
+      sQ[(2 * i) * G + g] = y0;
+      sQ[(2 * i + 1) * G + g] = y1;
+    }
+    if (new_row >= 0) {  // append the new key (rotated) and value, keep them in the tiles
+      __half* kc = const_cast<__half*>(k_cache);
+      __half* vc = const_cast<__half*>(v_cache);
+      const size_t cache_off = ((b * S_max + p_new) * Hkv + kvh) * D;
+      if (tid < D / 2) {
+        const float* src = qrow + (static_cast<size_t>(H) + kvh) * D + 2 * tid;
+        float y0, y1;
+        rope_pair(src[0], src[1], tid, D, p_new, theta_base, &y0, &y1);
+        const __half2 h = __floats2half2_rn(y0, y1);
+        *reinterpret_cast<__half2*>(kc + cache_off + 2 * tid) = h;
+        *reinterpret_cast<__half2*>(sK + new_row * kKStride + 2 * tid) = h;
+      } else {
+        const int i = tid - D / 2;
+        const float* src = qrow + (static_cast<size_t>(H) + Hkv + kvh) * D + 2 * i;
+        const __half2 h = __floats2half2_rn(src[0], src[1]);
+        *reinterpret_cast<__half2*>(vc + cache_off + 2 * i) = h;
+        *reinterpret_cast<__half2*>(sV + new_row * D + 2 * i) = h;
+      }
+    }
+  } else {
+    for (int e = tid; e < G * D; e += kAttnThreads) {  // e = g * D + dim -> sQ[dim][g]
+      const int g = e / D, dim = e % D;
+      sQ[dim * G + g] = q[(r * H + static_cast<size_t>(kvh) * G) * D + e];
+    }
   }
   // Asynchronous 16-byte copies (no register held): K in one group, V in a second
   // one that lands while the scores are computed.
@@ -155,6 +204,7 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
   for (int e = tid; e < kAttnChunk * (D / 8); e += kAttnThreads) {
     const int key = e / (D / 8), part = e % (D / 8);
     __half* dk = sK + key * kKStride + part * 8;
+    if (key == new_row) continue;  // ROPE: written above
     if (key < cnt)
       cp_async16(dk, k_cache + ((b * S_max + s0 + key) * Hkv + kvh) * D + part * 8);
     else
@@ -165,6 +215,7 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
   for (int e = tid; e < kAttnChunk * (D / 8); e += kAttnThreads) {
     const int key = e / (D / 8), part = e % (D / 8);
     __half* dv = sV + key * D + part * 8;
+    if (key == new_row) continue;
     if (key < cnt)
       cp_async16(dv, v_cache + ((b * S_max + s0 + key) * Hkv + kvh) * D + part * 8);
     else
@@ -322,15 +373,16 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_combine(const float* __re
   out[rh * D + tid] = o / L;
 }
 
-template <int G>
+template <int G, bool ROPE>
 cudaError_t launch_split(const float* q, const __half* k_cache, const __half* v_cache, int B,
                          int n, int H, int Hkv, int S_max, int seq_len, const int* pos_dev,
-                         float scale, int nsplit, float* pa, float* pm, float* pl, cudaStream_t s) {
+                         float scale, int nsplit, float* pa, float* pm, float* pl, cudaStream_t s,
+                         float theta_base) {
   constexpr int D = kAttnHeadDim;
   const size_t smem = static_cast<size_t>(kAttnChunk) * kKStride * 2 +
                       static_cast<size_t>(kAttnChunk) * D * 2 + static_cast<size_t>(G) * D * 4 +
                       static_cast<size_t>(G) * kAttnChunk * 4;
-  auto kern = k_attn_split<G>;
+  auto kern = k_attn_split<G, ROPE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
@@ -345,7 +397,7 @@ cudaError_t launch_split(const float* q, const __half* k_cache, const __half* v_
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, q, k_cache, v_cache, n, H, Hkv, S_max, seq_len, pos_dev,
-                            scale, nsplit, pa, pm, pl);
+                            scale, nsplit, pa, pm, pl, theta_base);
 }
 
 template <typename... KArgs, typename... Args>
@@ -379,13 +431,16 @@ size_t attention_workspace_bytes(int B, int n, int H, int d, int seq_len) {
   return static_cast<size_t>(B) * n * H * nsplit * (d + 2) * sizeof(float);
 }
 
-cudaError_t launch_attention(const float* q, const __half* k_cache, const __half* v_cache, int B,
-                             int n, int H, int Hkv, int d, int S_max, int seq_len, float scale,
-                             float* out, void* workspace, cudaStream_t s, const int* pos_dev) {
+namespace {
+cudaError_t attention_impl(const float* q, const __half* k_cache, const __half* v_cache, int B,
+                           int n, int H, int Hkv, int d, int S_max, int seq_len, float scale,
+                           float* out, void* workspace, cudaStream_t s, const int* pos_dev,
+                           bool rope, float theta_base) {
   if (d != kAttnHeadDim || Hkv <= 0 || H % Hkv != 0 || H / Hkv > kAttnMaxGroup)
     return cudaErrorInvalidValue;
+  if (rope && n != 1) return cudaErrorInvalidValue;
   // With the position on the device the split count covers the whole cache; the
-  // chunks past the visible keys write empty partials.
+  // chunks past the visible keys write nothing and the combine skips them.
   const int nsplit = ((pos_dev ? S_max : seq_len) + kAttnChunk - 1) / kAttnChunk;
   const size_t rows = static_cast<size_t>(B) * n * H * nsplit;
   float* pa = static_cast<float*>(workspace);
@@ -393,18 +448,40 @@ cudaError_t launch_attention(const float* q, const __half* k_cache, const __half
   float* pl = pm + rows;
   const int G = H / Hkv;
   cudaError_t e;
+#define OBN_SPLIT(GG)                                                                           \
+  (rope ? launch_split<GG, true>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev,  \
+                                 scale, nsplit, pa, pm, pl, s, theta_base)                     \
+        : launch_split<GG, false>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, \
+                                  scale, nsplit, pa, pm, pl, s, theta_base))
   switch (G) {
-    case 1: e = launch_split<1>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, nsplit, pa, pm, pl, s); break;
-    case 2: e = launch_split<2>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, nsplit, pa, pm, pl, s); break;
-    case 4: e = launch_split<4>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, nsplit, pa, pm, pl, s); break;
-    case 8: e = launch_split<8>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, nsplit, pa, pm, pl, s); break;
+    case 1: e = OBN_SPLIT(1); break;
+    case 2: e = OBN_SPLIT(2); break;
+    case 4: e = OBN_SPLIT(4); break;
+    case 8: e = OBN_SPLIT(8); break;
     default: return cudaErrorInvalidValue;
   }
+#undef OBN_SPLIT
   if (e != cudaSuccess) return e;
   return launch_pdl_attn(k_attn_combine, dim3(static_cast<unsigned>(B * n * H)),
                          dim3(kAttnThreads), s, static_cast<const float*>(pa),
                          static_cast<const float*>(pm), static_cast<const float*>(pl), nsplit, n,
                          S_max, pos_dev, out);
+}
+}  // namespace
+
+cudaError_t launch_attention(const float* q, const __half* k_cache, const __half* v_cache, int B,
+                             int n, int H, int Hkv, int d, int S_max, int seq_len, float scale,
+                             float* out, void* workspace, cudaStream_t s, const int* pos_dev) {
+  return attention_impl(q, k_cache, v_cache, B, n, H, Hkv, d, S_max, seq_len, scale, out,
+                        workspace, s, pos_dev, false, 0.0f);
+}
+
+cudaError_t launch_attention_rope(const float* qkv, __half* k_cache, __half* v_cache, int B, int H,
+                                  int Hkv, int d, int S_max, int pos, float theta_base,
+                                  float scale, float* out, void* workspace, cudaStream_t s,
+                                  const int* pos_dev) {
+  return attention_impl(qkv, k_cache, v_cache, B, 1, H, Hkv, d, S_max, pos + 1, scale, out,
+                        workspace, s, pos_dev, true, theta_base);
 }
 
 }  // namespace obn

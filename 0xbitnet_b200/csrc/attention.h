@@ -37,4 +37,16 @@ cudaError_t launch_attention(const float* q, const __half* k_cache, const __half
                              float* out, void* workspace, cudaStream_t s,
                              const int* pos_dev = nullptr);
 
+// One decode token per sequence (n = 1) with the RoPE + KV append fused in:
+// qkv [B, (H + 2*Hkv) * d] is the merged QKV projection output (unrotated); the
+// new token sits at position pos (or *pos_dev), its rotated key and its value
+// are stored into the caches, and out [B, H*d] is the attention of the rotated
+// q over positions [0, pos]. Equal, bit for bit, to launch_rope_kv_append
+// followed by launch_attention. Workspace as launch_attention with n = 1 and
+// seq_len = pos + 1 (S_max when pos_dev is given).
+cudaError_t launch_attention_rope(const float* qkv, __half* k_cache, __half* v_cache, int B, int H,
+                                  int Hkv, int d, int S_max, int pos, float theta_base,
+                                  float scale, float* out, void* workspace, cudaStream_t s,
+                                  const int* pos_dev = nullptr);
+
 }  // namespace obn

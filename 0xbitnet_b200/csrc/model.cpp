@@ -459,7 +459,16 @@ std::string Model::enqueue(int n, const int32_t* ids_dev, const int* pos_dev, bo
     const Layer& L = layers_[i];
     if (obn_bitlinear_forward(L.qkv, x_, n, qkv_, ws_, ws_bytes_, s) != OBN_OK)
       return obn_fail("q|k|v projection");
-    if (pos_dev) {
+    if (n == 1) {  // decode: RoPE + KV append fused into the attention pass
+      const int rc =
+          pos_dev ? obn_attention_decode_rope_at(qkv_, k_cache_[i], v_cache_[i], 1, H, Hkv, d,
+                                                 kMaxSeq, pos_dev, c.rope_theta, scale, attn_,
+                                                 attn_ws_, attn_ws_bytes_, s)
+                  : obn_attention_decode_rope(qkv_, k_cache_[i], v_cache_[i], 1, H, Hkv, d,
+                                              kMaxSeq, pos_, c.rope_theta, scale, attn_,
+                                              attn_ws_, attn_ws_bytes_, s);
+      if (rc != OBN_OK) return obn_fail("RoPE + attention");
+    } else if (pos_dev) {
       if (obn_rope_kv_append_at(qkv_, 1, n, H, Hkv, d, pos_dev, c.rope_theta, q_, k_cache_[i],
                                 v_cache_[i], kMaxSeq, s) != OBN_OK)
         return obn_fail("RoPE + KV append");

@@ -18,7 +18,8 @@ consumes them (numerically the same: rmsnorm then quantize), the residual adds
 happen in the o_proj / down_proj epilogues (x + y rounded once, as the add
 kernel would), q/k/v are one
 merged 3840-row BitLinear with a per-row scale table, gate and up are one
-interleaved gated layer, and the KV cache is fp16. Every step is a fixed
+interleaved gated layer, and the KV cache is fp16; small batches rotate q and
+append k/v inside the attention pass (one launch fewer). Every step is a fixed
 sequence of libobn launches on one stream, so it is captured as a CUDA graph.
 Batches above 4 tokens take the tensor-core LM head (f16 hi/lo split, f32
 accumulation) instead of the shader-order one. Weights are random (seeded)
@@ -34,6 +35,11 @@ import torch
 from . import attention as att
 from ._lib import check, lib
 from .bitlinear import BitLinear, lm_head_f16, lm_head_f16_batched
+
+
+# Batches up to this size take the fused RoPE + attention pass (one launch fewer);
+# larger ones rotate q once in a separate pass instead of once per KV chunk.
+FUSED_ROPE_MAX_BATCH = 8
 
 
 def _ptr(t):
@@ -165,8 +171,12 @@ class BitNetDecoder:
                                   _ptr(self.x), s))
         for L, c in zip(self.layers, self.caches):
             L.qkv.forward(self.x, n=B, out=self.qkv_out)
-            att.rope_kv_append(self.qkv_out, c, H, 1, cfg.rope_theta, q_out=self.q, pos=pos)
-            att.attention(self.q, c, H, 1, pos + 1, out=self.attn, workspace=self.attn_ws)
+            if B <= FUSED_ROPE_MAX_BATCH:  # RoPE + KV append + attention in one pass
+                att.attention_rope(self.qkv_out, c, H, pos, cfg.rope_theta, out=self.attn,
+                                   workspace=self.attn_ws)
+            else:  # every split CTA would rotate its q heads again: rotate once first
+                att.rope_kv_append(self.qkv_out, c, H, 1, cfg.rope_theta, q_out=self.q, pos=pos)
+                att.attention(self.q, c, H, 1, pos + 1, out=self.attn, workspace=self.attn_ws)
             L.o.forward_residual(self.attn, self.x, n=B)  # x += o_proj(attn)
             L.gate_up.forward(self.x, n=B, out=self.ffn_out)
             L.down.forward_residual(self.ffn_out, self.x, n=B)  # x += down(ffn)

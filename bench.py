@@ -500,7 +500,9 @@ def measure_ffn_gate_up(args, obn, synth, dev, stream, batches):
 def measure_attention(dev, stream, peak, layers):
     """Next-row kernels: one decode step's attention for BitNet-2B (20 heads, 5 KV
     heads, head_dim 128) at context 2048 over `layers` layers, fp16 KV: RoPE + KV
-    append of the new token, then split-KV attention + combine. Bytes per layer and
+    append of the new token fused into the split-KV attention for small batches
+    (obn_attention_decode_rope), a separate RoPE pass before it for large ones, then
+    the combine. Bytes per layer and
     sequence = the K and V cache read (2 * 2048 * 5 * 128 * 2) + q, out, new k/v."""
     import torch
     att = importlib.import_module("0xbitnet_b200.attention")
@@ -515,10 +517,15 @@ def measure_attention(dev, stream, peak, layers):
             c.seq_len = ctx - 1
         qkv = torch.randn(B, (H + 2 * Hkv) * Dh, device=dev)
 
-        def step():
+        fused = B <= importlib.import_module("0xbitnet_b200.decoder").FUSED_ROPE_MAX_BATCH
+
+        def step():  # the decoder's path for this batch size
             for c in caches:
-                q = att.rope_kv_append(qkv, c, H, 1)
-                att.attention(q, c, H, 1, ctx)
+                if fused:
+                    att.attention_rope(qkv, c, H, ctx - 1)
+                else:
+                    q = att.rope_kv_append(qkv, c, H, 1)
+                    att.attention(q, c, H, 1, ctx)
         with torch.cuda.stream(stream):
             step()
             stream.synchronize()

@@ -263,6 +263,24 @@ OBN_API int obn_attention_decode_at(const float* q, const void* k_cache, const v
                                     const int* pos_dev, float scale, float* out, void* workspace,
                                     size_t workspace_bytes, void* stream);
 
+/* One decode token per sequence with RoPE + KV append fused into the attention:
+ * qkv [B, (H + 2*Hkv) * head_dim] f32 is the merged QKV projection output (q, k, v
+ * unrotated); the token sits at position pos (the _at form reads it from pos_dev),
+ * its rotated key and its value are stored into the caches at that position and
+ * out [B, H * head_dim] is its attention over positions [0, pos]. Bit-identical to
+ * obn_rope_kv_append followed by obn_attention_decode (n = 1) and one launch fewer.
+ * Workspace: obn_attention_workspace_bytes(B, 1, H, head_dim, pos + 1), or with
+ * S_max in place of pos + 1 for the _at form. */
+OBN_API int obn_attention_decode_rope(const float* qkv, void* k_cache, void* v_cache, int B, int H,
+                                      int Hkv, int head_dim, int S_max, int pos, float theta_base,
+                                      float scale, float* out, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+OBN_API int obn_attention_decode_rope_at(const float* qkv, void* k_cache, void* v_cache, int B,
+                                         int H, int Hkv, int head_dim, int S_max,
+                                         const int* pos_dev, float theta_base, float scale,
+                                         float* out, void* workspace, size_t workspace_bytes,
+                                         void* stream);
+
 /* ---- decoder glue ------------------------------------------------------------- */
 /* Residual add (elementwise.wgsl op 0, TransformerBlock::forward's dispatch_add,
  * transformer.rs:63,69): y[i] = a[i] + b[i] for i < count (f32; y may alias a or b). */

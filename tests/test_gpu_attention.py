@@ -93,3 +93,27 @@ def test_attention_decode_step_end_to_end():
         want = orc.attention(qn[b:b + 1], kc[b, :S].reshape(S, -1).astype(np.float32),
                              vc[b, :S].reshape(S, -1).astype(np.float32), H, Hkv, D)
         np.testing.assert_allclose(out[b:b + 1], want, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("B,H,Hkv,S_prev", [(1, 20, 5, 2047), (3, 20, 5, 127), (2, 16, 2, 128),
+                                             (1, 8, 8, 0), (2, 32, 4, 300)])
+def test_fused_rope_attention_is_bit_identical(B, H, Hkv, S_prev):
+    """obn_attention_decode_rope == obn_rope_kv_append + obn_attention_decode (n = 1):
+    same output bits, same cache contents."""
+    torch = need_cuda()
+    S_max = S_prev + 9
+    rng = np.random.default_rng(B * 7 + H + S_prev)
+    k = torch.from_numpy(rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16))
+    v = torch.from_numpy(rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16))
+    qkv = torch.from_numpy(rng.standard_normal((B, (H + 2 * Hkv) * D)).astype(np.float32)).cuda()
+    c1, c2 = att().KVCache(B, S_max, Hkv, D), att().KVCache(B, S_max, Hkv, D)
+    for c in (c1, c2):
+        c.k.copy_(k)
+        c.v.copy_(v)
+        c.seq_len = S_prev
+    q = att().rope_kv_append(qkv, c1, H, 1, pos=S_prev)
+    want = att().attention(q, c1, H, 1, S_prev + 1).cpu()
+    got = att().attention_rope(qkv, c2, H, S_prev).cpu()
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert torch.equal(c1.k.cpu(), c2.k.cpu()) and torch.equal(c1.v.cpu(), c2.v.cpu())
