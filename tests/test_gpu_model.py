@@ -215,3 +215,23 @@ def test_graph_and_eager_decode_agree(tmp_path, vocab, monkeypatch):
         assert np.array_equal(g.forward([t]), e.forward([t]))
     g.dispose()
     e.dispose()
+
+
+def test_url_source_loads_from_the_cache(tmp_path, vocab):
+    """loader.rs:366-384: a URL source is served from <cache_dir>/<sha256(url)> when
+    that file exists (nothing is downloaded)."""
+    need_cuda()
+    import hashlib
+    import shutil
+    p, shape, keep = make(tmp_path, vocab, layers=1)
+    url = "https://example.com/bitnet/ggml-model-i2_s.gguf"
+    cache = tmp_path / "cache"
+    cache.mkdir()
+    shutil.copy(p, cache / hashlib.sha256(url.encode()).hexdigest())
+    phases = []
+    m = ox().BitNet.load_sync(url, on_progress=lambda *a: phases.append(a[0]),
+                              cache_dir=str(cache))
+    ref = model_ref.RefModel(keep, shape)
+    check_steps(m, ref, [vocab["bos"], 5, 6], [7])
+    assert phases[0] == 0 and 1 in phases and phases[-1] == 2
+    m.dispose()
