@@ -12,9 +12,10 @@
 //    reference's f32 cache: the decode step streams the cache).
 //  * k_attn_split: one CTA per (128-key chunk, KV head, query row) — the G query
 //    heads of a KV group share each K/V chunk load. Thread = key for the scores
-//    (the dot over d is sequential in d, as attention.wgsl's, then * scale),
-//    thread = dimension for P.V (sequential over the chunk's keys); the chunk
-//    keeps its own max and sum (online softmax), written as partials.
+//    (the dot over d is sequential in d, as attention.wgsl's, one fused
+//    multiply-add per step, then * scale), thread = dimension for P.V
+//    (sequential over the chunk's keys, fused multiply-adds); the chunk keeps
+//    its own max and sum (online softmax), written as partials.
 //  * k_attn_combine: per (query row, head) rescales the chunks' partials to the
 //    global max and divides by the global sum.
 //
@@ -224,7 +225,8 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
   cp_async_commit();
   cp_async_wait_group<1>();  // K landed (V may still be in flight)
   __syncthreads();
-  // Scores: thread = key, the dot sequential over d (attention.wgsl:48-51).
+  // Scores: thread = key, the dot sequential over d (attention.wgsl:48-51), each
+  // step one fused multiply-add (the shader's q * k + sum, contracted).
   static_assert(kAttnThreads == kAttnChunk, "one thread per key");
   float sc[G];
 #pragma unroll
@@ -258,9 +260,9 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
       qload(d8 + 2 * e, q0);
       qload(d8 + 2 * e + 1, q1);
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        sc[g] = __fadd_rn(sc[g], __fmul_rn(q0[g], kf.x));
-        sc[g] = __fadd_rn(sc[g], __fmul_rn(q1[g], kf.y));
+      for (int g = 0; g < G; ++g) {  // fused multiply-adds, in the shader's order over d
+        sc[g] = fmaf(q0[g], kf.x, sc[g]);
+        sc[g] = fmaf(q1[g], kf.y, sc[g]);
       }
     }
   }
@@ -309,7 +311,7 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
       for (int g = 0; g < G; ++g) pk[g] = sP[key * G + g];
     }
 #pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = __fadd_rn(acc[g], __fmul_rn(pk[g], v));
+    for (int g = 0; g < G; ++g) acc[g] = fmaf(pk[g], v, acc[g]);
   }
 #pragma unroll
   for (int g = 0; g < G; ++g) {
