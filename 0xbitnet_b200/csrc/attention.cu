@@ -28,6 +28,7 @@
 #include "obn_common.cuh"
 
 #include <cfloat>
+#include <cstdlib>
 
 namespace obn {
 namespace {
@@ -324,6 +325,262 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
   }
 }
 
+// ---- tensor-core split pass ------------------------------------------------
+// The same partials as k_attn_split, with the two contractions on the tensor
+// cores (mma.sync m16n8k16, f16 x f16 -> f32): scores S[key][head] = K . q over
+// the chunk's 128 keys and P.V out[dim][head] = sum over keys of V[key][dim] P.
+// K and V are binary16 already (exact as MMA operands); q and P are f32, so each
+// is split into a binary16 high part and the binary16 rounding of the remainder
+// and both halves are multiplied (x = hi + lo to about 2^-22 |x|), which keeps
+// the contractions at f32 accuracy. The G query heads of the KV group are the
+// MMA's N = 8 columns (zero-padded above G). 4 warps: warp w takes keys
+// 32w .. 32w + 31 for the scores and dimensions 32w .. 32w + 31 for P.V.
+OBN_DEVINL void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+OBN_DEVINL void ldsm_x4(uint32_t addr, uint32_t (&a)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+               : "r"(addr));
+}
+OBN_DEVINL void ldsm_x4_t(uint32_t addr, uint32_t (&a)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+               : "r"(addr));
+}
+// (x0, x1) -> binary16 pairs hi and lo with x = hi + lo to about 2^-22 |x|.
+OBN_DEVINL void split_h2(float x0, float x1, uint32_t* hi, uint32_t* lo) {
+  const __half2 h = __floats2half2_rn(x0, x1);
+  const __half2 l = __floats2half2_rn(x0 - __low2float(h), x1 - __high2float(h));
+  *hi = *reinterpret_cast<const uint32_t*>(&h);
+  *lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+constexpr int kVStride = kAttnHeadDim + 8;  // halves per smem V row (ldmatrix.trans, no conflicts)
+
+template <int G, bool ROPE = false>
+__global__ __launch_bounds__(kAttnThreads) void k_attn_split_tc(
+    const float* __restrict__ q, const __half* __restrict__ k_cache,
+    const __half* __restrict__ v_cache, int n, int H, int Hkv, int S_max, int seq_len,
+    const int* __restrict__ pos_dev, float scale, int nsplit, float* __restrict__ part_acc,
+    float* __restrict__ part_m, float* __restrict__ part_l, float theta_base) {
+  constexpr int D = kAttnHeadDim;
+  constexpr int C = kAttnChunk;
+  static_assert(C == 128 && D == 128 && kAttnThreads == 128 && G <= 8, "tile shape");
+  extern __shared__ __align__(16) unsigned char smem[];
+  __half* sK = reinterpret_cast<__half*>(smem);                 // [C][kKStride]
+  __half* sV = sK + C * kKStride;                               // [C][kVStride]
+  float* sQ = reinterpret_cast<float*>(sV + C * kVStride);      // [G][D] rotated q (f32)
+  float* sP = sQ + G * D;                                       // [C][G] probabilities
+  __shared__ float red_m[8][4], red_l[8][4];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = lane >> 2, qd = lane & 3;  // MMA fragment coordinates
+  const int c = blockIdx.x, kvh = blockIdx.y;
+  const size_t r = blockIdx.z;  // query row b * n + t
+  const int t = static_cast<int>(r % n);
+  const size_t b = r / n;
+  const int s0 = c * C;
+  if (pos_dev) {
+    seq_len = min(*pos_dev + n, S_max);
+    if (s0 >= seq_len) return;
+  }
+  const int limit = seq_len - n + t + 1;
+  const int cnt = min(C, limit - s0);
+  const size_t pbase = (r * H + static_cast<size_t>(kvh) * G) * nsplit + c;
+  if (cnt <= 0) {
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      part_acc[(pbase + static_cast<size_t>(g) * nsplit) * D + tid] = 0.0f;
+      if (tid == 0) {
+        part_m[pbase + static_cast<size_t>(g) * nsplit] = -FLT_MAX;
+        part_l[pbase + static_cast<size_t>(g) * nsplit] = 0.0f;
+      }
+    }
+    return;
+  }
+  const int p_new = ROPE ? (pos_dev ? *pos_dev : seq_len - 1) : 0;
+  const int new_row = (ROPE && p_new < S_max && p_new >= s0 && p_new < s0 + C) ? p_new - s0 : -1;
+  // K in one copy group, V in a second one that lands while the scores run.
+#pragma unroll 4
+  for (int e = tid; e < C * (D / 8); e += kAttnThreads) {
+    const int key = e / (D / 8), part = e % (D / 8);
+    __half* dk = sK + key * kKStride + part * 8;
+    if (key == new_row) continue;
+    if (key < cnt)
+      cp_async16(dk, k_cache + ((b * S_max + s0 + key) * Hkv + kvh) * D + part * 8);
+    else
+      *reinterpret_cast<uint4*>(dk) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  cp_async_commit();
+#pragma unroll 4
+  for (int e = tid; e < C * (D / 8); e += kAttnThreads) {
+    const int key = e / (D / 8), part = e % (D / 8);
+    __half* dv = sV + key * kVStride + part * 8;
+    if (key == new_row) continue;
+    if (key < cnt)
+      cp_async16(dv, v_cache + ((b * S_max + s0 + key) * Hkv + kvh) * D + part * 8);
+    else
+      *reinterpret_cast<uint4*>(dv) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  cp_async_commit();
+  // q of the group's heads (rotated here for ROPE), f32, heads above G zero.
+  if constexpr (ROPE) {
+    const int slots = H + 2 * Hkv;
+    const float* qrow = q + r * static_cast<size_t>(slots) * D;
+    for (int e = tid; e < G * (D / 2); e += kAttnThreads) {
+      const int g = e / (D / 2), i = e % (D / 2);
+      const float* src = qrow + (static_cast<size_t>(kvh) * G + g) * D + 2 * i;
+      float y0, y1;
+      rope_pair(src[0], src[1], i, D, p_new, theta_base, &y0, &y1);
+      sQ[g * D + 2 * i] = y0;
+      sQ[g * D + 2 * i + 1] = y1;
+    }
+    if (new_row >= 0) {
+      __half* kc = const_cast<__half*>(k_cache);
+      __half* vc = const_cast<__half*>(v_cache);
+      const size_t cache_off = ((b * S_max + p_new) * Hkv + kvh) * D;
+      if (tid < D / 2) {
+        const float* src = qrow + (static_cast<size_t>(H) + kvh) * D + 2 * tid;
+        float y0, y1;
+        rope_pair(src[0], src[1], tid, D, p_new, theta_base, &y0, &y1);
+        const __half2 h = __floats2half2_rn(y0, y1);
+        *reinterpret_cast<__half2*>(kc + cache_off + 2 * tid) = h;
+        *reinterpret_cast<__half2*>(sK + new_row * kKStride + 2 * tid) = h;
+      } else {
+        const int i = tid - D / 2;
+        const float* src = qrow + (static_cast<size_t>(H) + Hkv + kvh) * D + 2 * i;
+        const __half2 h = __floats2half2_rn(src[0], src[1]);
+        *reinterpret_cast<__half2*>(vc + cache_off + 2 * i) = h;
+        *reinterpret_cast<__half2*>(sV + new_row * kVStride + 2 * i) = h;
+      }
+    }
+  } else {
+    for (int e = tid; e < G * D; e += kAttnThreads)
+      sQ[e] = q[(r * H + static_cast<size_t>(kvh) * G) * D + e];
+  }
+  __syncthreads();
+  // B fragments of q (column = head grp, rows = dims), split hi / lo.
+  uint32_t qh[8][2], ql[8][2];
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    if (grp < G) {
+      const float* qc = sQ + grp * D + ks * 16 + 2 * qd;
+      split_h2(qc[0], qc[1], &qh[ks][0], &ql[ks][0]);
+      split_h2(qc[8], qc[9], &qh[ks][1], &ql[ks][1]);
+    } else {  // padding columns
+      qh[ks][0] = qh[ks][1] = ql[ks][0] = ql[ks][1] = 0u;
+    }
+  }
+  cp_async_wait_group<1>();  // K landed
+  __syncthreads();
+  // Scores: warp w, keys 32w + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1.
+  float sc[2][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sc[mt][i] = 0.0f;
+    const int krow = 32 * warp + 16 * mt + (lane & 15);
+    const uint32_t abase = smem_u32(sK + krow * kKStride + ((lane >> 4) << 3));
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(abase + ks * 32, a);
+      mma_16816(sc[mt], a, qh[ks][0], qh[ks][1]);
+      mma_16816(sc[mt], a, ql[ks][0], ql[ks][1]);
+    }
+  }
+  // Scale, causal validity, per-head max over the chunk.
+  float mx[2] = {-FLT_MAX, -FLT_MAX};
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int key = 32 * warp + 16 * mt + grp + (i >= 2 ? 8 : 0);
+      sc[mt][i] = key < cnt ? __fmul_rn(sc[mt][i], scale) : -FLT_MAX;
+      mx[i & 1] = fmaxf(mx[i & 1], sc[mt][i]);
+    }
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int sft = 4; sft <= 16; sft <<= 1) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], sft));
+  if (grp == 0) {
+    red_m[2 * qd][warp] = mx[0];
+    red_m[2 * qd + 1][warp] = mx[1];
+  }
+  __syncthreads();
+  float mg[2], ls[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    mg[h] = fmaxf(fmaxf(red_m[2 * qd + h][0], red_m[2 * qd + h][1]),
+                  fmaxf(red_m[2 * qd + h][2], red_m[2 * qd + h][3]));
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int key = 32 * warp + 16 * mt + grp + (i >= 2 ? 8 : 0);
+      const int h = i & 1;
+      const float pv = key < cnt ? expf(sc[mt][i] - mg[h]) : 0.0f;
+      ls[h] += pv;
+      if (2 * qd + h < G) sP[key * G + 2 * qd + h] = pv;
+    }
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int sft = 4; sft <= 16; sft <<= 1) ls[h] += __shfl_xor_sync(0xffffffffu, ls[h], sft);
+  if (grp == 0) {
+    red_l[2 * qd][warp] = ls[0];
+    red_l[2 * qd + 1][warp] = ls[1];
+  }
+  cp_async_wait_group<0>();  // V landed
+  __syncthreads();
+  // P.V: warp w, dims 32w + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1.
+  float o[2][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[mt][i] = 0.0f;
+  // ldmatrix.trans row addresses: lanes 0-7 keys 0-7 / dims d0.., 8-15 keys 0-7 / dims
+  // d0 + 8.., 16-23 keys 8-15 / d0.., 24-31 keys 8-15 / d0 + 8..
+  const int vkey = (lane & 7) + ((lane >> 4) << 3);
+  const int vdim = ((lane >> 3) & 1) << 3;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    uint32_t ph0 = 0u, pl0 = 0u, ph1 = 0u, pl1 = 0u;
+    if (grp < G) {
+      const float* pc = sP + (ks * 16 + 2 * qd) * G + grp;
+      split_h2(pc[0], pc[G], &ph0, &pl0);          // keys 2qd, 2qd + 1
+      split_h2(pc[8 * G], pc[9 * G], &ph1, &pl1);  // keys 2qd + 8, 2qd + 9
+    }
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      uint32_t a[4];
+      ldsm_x4_t(smem_u32(sV + (ks * 16 + vkey) * kVStride + 32 * warp + 16 * mt + vdim), a);
+      mma_16816(o[mt], a, ph0, ph1);
+      mma_16816(o[mt], a, pl0, pl1);
+    }
+  }
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int dim = 32 * warp + 16 * mt + grp + (i >= 2 ? 8 : 0);
+      const int h = 2 * qd + (i & 1);
+      if (h < G) part_acc[(pbase + static_cast<size_t>(h) * nsplit) * D + dim] = o[mt][i];
+    }
+  if (tid < G) {
+    part_m[pbase + static_cast<size_t>(tid) * nsplit] =
+        fmaxf(fmaxf(red_m[tid][0], red_m[tid][1]), fmaxf(red_m[tid][2], red_m[tid][3]));
+    part_l[pbase + static_cast<size_t>(tid) * nsplit] =
+        (red_l[tid][0] + red_l[tid][1]) + (red_l[tid][2] + red_l[tid][3]);
+  }
+}
+
 // One CTA per (query row, head): thread = dimension.
 __global__ __launch_bounds__(kAttnThreads) void k_attn_combine(const float* __restrict__ part_acc,
                                                                const float* __restrict__ part_m,
@@ -381,10 +638,17 @@ cudaError_t launch_split(const float* q, const __half* k_cache, const __half* v_
                          float scale, int nsplit, float* pa, float* pm, float* pl, cudaStream_t s,
                          float theta_base) {
   constexpr int D = kAttnHeadDim;
-  const size_t smem = static_cast<size_t>(kAttnChunk) * kKStride * 2 +
-                      static_cast<size_t>(kAttnChunk) * D * 2 + static_cast<size_t>(G) * D * 4 +
-                      static_cast<size_t>(G) * kAttnChunk * 4;
-  auto kern = k_attn_split<G, ROPE>;
+  // The tensor-core pass unless OBN_ATTN_TC=0 selects the CUDA-core one.
+  static const bool tc = [] {
+    const char* v = std::getenv("OBN_ATTN_TC");
+    return !(v && v[0] == '0');
+  }();
+  const size_t smem =
+      tc ? static_cast<size_t>(kAttnChunk) * kKStride * 2 + static_cast<size_t>(kAttnChunk) * kVStride * 2 +
+               static_cast<size_t>(G) * D * 4 + static_cast<size_t>(kAttnChunk) * G * 4
+         : static_cast<size_t>(kAttnChunk) * kKStride * 2 + static_cast<size_t>(kAttnChunk) * D * 2 +
+               static_cast<size_t>(G) * D * 4 + static_cast<size_t>(G) * kAttnChunk * 4;
+  auto kern = tc ? k_attn_split_tc<G, ROPE> : k_attn_split<G, ROPE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
