@@ -16,6 +16,9 @@
 //    multiply-add per step, then * scale), thread = dimension for P.V
 //    (sequential over the chunk's keys, fused multiply-adds); the chunk keeps
 //    its own max and sum (online softmax), written as partials.
+//  * k_attn_split_tc (the default): the same partials with K.q and P.V on the
+//    tensor cores (mma.sync m16n8k16, binary16 operands, f32 accumulation; q
+//    and P split into binary16 hi + lo so nothing is lost against f32).
 //  * k_attn_combine: per (query row, head) rescales the chunks' partials to the
 //    global max and divides by the global sum.
 //
