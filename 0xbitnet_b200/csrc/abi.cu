@@ -560,8 +560,12 @@ int forward_impl(const obn_bitlinear* layer, const float* x, int n, float* y, vo
   auto s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (n == 1 && layer->in_dim <= obn::kGemvMaxK) {  // whole BitLinear in one kernel
-    e = obn::launch_bitlinear_n1(view(layer), layer->norm, layer->eps, x, ym, s, accumulate);
+    // (a gated layer's activation included: the kernel writes y directly)
+    e = obn::launch_bitlinear_n1(view(layer), layer->norm, layer->eps, x,
+                                 layer->gated ? y : ym, s, accumulate,
+                                 layer->gated ? layer->act : -1);
     if (e != cudaSuccess) return cuda_fail(e, "bitlinear (n=1) launch");
+    return OBN_OK;
   } else {
     e = obn::launch_rmsnorm_quant(x, layer->norm, layer->eps, n, layer->in_dim, q, sc, qs, s);
     if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");

@@ -469,11 +469,20 @@ __global__ __launch_bounds__(kGemvWarps * 32) void k_gemv(
 // ---------------------------------------------------------------------------
 constexpr int kN1Rows = 32;  // rows per CTA (two subtiles)
 
+// activation.wgsl:28-33 for a gated layer's gate value: 0 = ReLU^2, 1 = SiLU.
+OBN_DEVINL float gate_act(int act, float x) {
+  if (act == 0) {
+    const float r = fmaxf(0.0f, x);
+    return __fmul_rn(r, r);
+  }
+  return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+}
+
 template <int EPT>
 __global__ __launch_bounds__(256) void k_bitlinear_n1(
     const uint8_t* __restrict__ W, const float* __restrict__ s_w,
     const float* __restrict__ gamma, float eps, const float* __restrict__ x,
-    float* __restrict__ y, int M, int K, int accumulate) {
+    float* __restrict__ y, int M, int K, int accumulate, int act) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
   __shared__ float sh_ss[256];  // per thread: sum of squares of its columns
@@ -600,15 +609,25 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
     red[warp][1][lane] = acc1;
   }
   __syncthreads();
-  if (row_thread && ok) {
-    const int sb = tid >> 4, r = tid & 15;
-    int a = 0;
+  if (warp == 0) {
+    float val = 0.0f;
+    if (row_thread && ok) {
+      const int sb = tid >> 4, r = tid & 15;
+      int a = 0;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) a += red[w][sb][r] - red_q[w];
-    const float scale = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
-    // ternary_gemv.wgsl:232 order: (f32(acc) * s_w) * s_x
-    const float val = __fmul_rn(__fmul_rn(static_cast<float>(a), sw), scale);
-    y[row] = accumulate ? __fadd_rn(y_old, val) : val;
+      for (int w = 0; w < 8; ++w) a += red[w][sb][r] - red_q[w];
+      const float scale = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
+      // ternary_gemv.wgsl:232 order: (f32(acc) * s_w) * s_x
+      val = __fmul_rn(__fmul_rn(static_cast<float>(a), sw), scale);
+    }
+    if (act < 0) {
+      if (row_thread && ok) y[row] = accumulate ? __fadd_rn(y_old, val) : val;
+    } else {
+      // Gated layer (rows 2i = gate, 2i + 1 = up of feature i, an even row count):
+      // the even lane forms act(gate) * up as the separate activation pass would.
+      const float up = __shfl_down_sync(0xffffffffu, val, 1);
+      if (row_thread && ok && (tid & 1) == 0) y[row >> 1] = __fmul_rn(gate_act(act, val), up);
+    }
   }
 }
 
@@ -652,7 +671,7 @@ cudaError_t gemv_nt(const WeightView& W, const int8_t* q, const float* s_x, cons
 
 template <int EPT>
 cudaError_t bitlinear_n1_ept(const WeightView& W, const float* gamma, float eps, const float* x,
-                             float* y, int accumulate, cudaStream_t s) {
+                             float* y, int accumulate, int act, cudaStream_t s) {
   const int K = W.in_dim;
   const size_t smem =
       2 * static_cast<size_t>(K / kBlockK) * kSubtileBytes + static_cast<size_t>(K);
@@ -661,7 +680,7 @@ cudaError_t bitlinear_n1_ept(const WeightView& W, const float* gamma, float eps,
   if (e != cudaSuccess) return e;
   dim3 grid((W.out_dim + kN1Rows - 1) / kN1Rows);
   return launch_pdl(kern, grid, dim3(256), smem, s, W.w, W.s_w, gamma, eps, x, y, W.out_dim, K,
-                    accumulate);
+                    accumulate, act);
 }
 
 template <bool ACC>
@@ -873,22 +892,23 @@ cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int
 }
 
 cudaError_t launch_bitlinear_n1(const WeightView& W, const float* gamma, float eps,
-                                const float* x, float* y, cudaStream_t s, int accumulate) {
+                                const float* x, float* y, cudaStream_t s, int accumulate,
+                                int act) {
   const int ept = (W.in_dim + 255) / 256;
-  if (ept <= 1) return bitlinear_n1_ept<1>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 2) return bitlinear_n1_ept<2>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 4) return bitlinear_n1_ept<4>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 8) return bitlinear_n1_ept<8>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 12) return bitlinear_n1_ept<12>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 16) return bitlinear_n1_ept<16>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 20) return bitlinear_n1_ept<20>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 24) return bitlinear_n1_ept<24>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 28) return bitlinear_n1_ept<28>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 32) return bitlinear_n1_ept<32>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 40) return bitlinear_n1_ept<40>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 48) return bitlinear_n1_ept<48>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 56) return bitlinear_n1_ept<56>(W, gamma, eps, x, y, accumulate, s);
-  if (ept <= 64) return bitlinear_n1_ept<64>(W, gamma, eps, x, y, accumulate, s);
+  if (ept <= 1) return bitlinear_n1_ept<1>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 2) return bitlinear_n1_ept<2>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 4) return bitlinear_n1_ept<4>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 8) return bitlinear_n1_ept<8>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 12) return bitlinear_n1_ept<12>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 16) return bitlinear_n1_ept<16>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 20) return bitlinear_n1_ept<20>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 24) return bitlinear_n1_ept<24>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 28) return bitlinear_n1_ept<28>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 32) return bitlinear_n1_ept<32>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 40) return bitlinear_n1_ept<40>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 48) return bitlinear_n1_ept<48>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 56) return bitlinear_n1_ept<56>(W, gamma, eps, x, y, accumulate, act, s);
+  if (ept <= 64) return bitlinear_n1_ept<64>(W, gamma, eps, x, y, accumulate, act, s);
   return cudaErrorInvalidValue;
 }
 

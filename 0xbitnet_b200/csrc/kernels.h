@@ -60,9 +60,11 @@ cudaError_t launch_gemv(const WeightView& W, const int8_t* q, const float* s_x,
                         cudaStream_t s);
 // One-token BitLinear forward in a single kernel (RMSNorm when gamma != null,
 // quantize, GEMV with ternary_gemv.wgsl's epilogue order). K <= kGemvMaxK.
+// act >= 0: W is a gated layer (rows 2i gate, 2i + 1 up) and y[i] = act(gate) * up
+// (0 = ReLU^2, 1 = SiLU) is written instead of the rows.
 cudaError_t launch_bitlinear_n1(const WeightView& W, const float* gamma, float eps,
                                 const float* x, float* y, cudaStream_t s,
-                                int accumulate = 0);
+                                int accumulate = 0, int act = -1);
 
 // Largest K the GEMV kernels accept.
 constexpr int kGemvMaxK = 16384;
