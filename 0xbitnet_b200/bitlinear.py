@@ -135,6 +135,11 @@ class BitLinear:
     def handle(self) -> ctypes.c_void_p:
         return self._h
 
+    def set_activation(self, act: int) -> None:
+        """A gated layer's activation of the gate: 0 = ReLU^2 (the default), 1 = SiLU
+        (the "bitnet" architecture's FFN, ffn.rs:70-79)."""
+        check(lib().obn_bitlinear_set_activation(self._h, act))
+
     def workspace_bytes(self, n: int) -> int:
         return int(lib().obn_bitlinear_workspace_bytes(self._h, n))
 

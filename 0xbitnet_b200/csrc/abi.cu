@@ -571,6 +571,13 @@ int forward_impl(const obn_bitlinear* layer, const float* x, int n, float* y, vo
     if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
     const int order =
         (n == 1 ? obn::kOrderGemv : obn::kOrderGemm) | accumulate;  // bitlinear.rs:90-94
+    if (obn::gemm_supported(view(layer), n) && layer->gated) {
+      // the GEMM epilogue forms act(gate) * up itself
+      e = obn::launch_gemm(view(layer), q, sc, qs, n, y, nullptr,
+                           order | obn::kOutGated | (layer->act ? obn::kOutSilu : 0), s);
+      if (e != cudaSuccess) return cuda_fail(e, "ternary matmul launch");
+      return OBN_OK;
+    }
     if (obn::gemm_supported(view(layer), n))
       e = obn::launch_gemm(view(layer), q, sc, qs, n, ym, nullptr, order, s);
     else if (layer->in_dim <= obn::kGemvMaxK)

@@ -336,10 +336,17 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
         if (!wait_or_abort(sm, &sm->accf[a], aph)) break;
         tc_fence_after();
         const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
-        // Three store kinds, chosen once per tile so the plain store never carries
-        // a (speculated) read of y: int32 accumulators, y = val, y += val.
-        const int kind = acc_out ? 0 : (order & kOutAccumulate) ? 2 : 1;
+        // Five store kinds, chosen once per tile so the plain store never carries
+        // a (speculated) read of y: int32 accumulators, y = val, y += val, and
+        // gated pairs with ReLU^2 (3) or SiLU (4) compiled in (rows 2i, 2i + 1 in
+        // lanes 2i, 2i + 1: the even lane writes act(gate) * up to y[t, i], y being
+        // [N][M / 2]).
+        const int kind = acc_out                  ? 0
+                         : (order & kOutGated)    ? ((order & kOutSilu) ? 4 : 3)
+                         : (order & kOutAccumulate) ? 2
+                                                    : 1;
         const bool gemv_order = (order & 1) == kOrderGemv;
+        const size_t Mh = static_cast<size_t>(M) >> 1;
         const bool full_tile = (nt + 1) * BN <= N && (mt + 1) * kBM <= M;
         auto chunk = [&](auto kind_c) {
           constexpr int K_ = decltype(kind_c)::value;
@@ -362,6 +369,30 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                 sx_v[j] = __shfl_sync(0xffffffffu, sxr[c], j);
               }
               tmem_ld_wait();
+              if constexpr (K_ >= 3) {
+                // Gated pairs: lanes 2i (gate row) and 2i + 1 (up row) swap one
+                // value per column pair (2k, 2k + 1), so the even lane forms
+                // column 2k and the odd lane column 2k + 1: every lane stores.
+                float val[kCols];
+#pragma unroll
+                for (int j = 0; j < kCols; ++j) {
+                  const float fd = static_cast<float>(static_cast<int>(v[j]) - qs_v[j]);
+                  val[j] = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx_v[j])
+                                      : __fmul_rn(fd, __fmul_rn(sw, sx_v[j]));
+                }
+                const bool odd = (m & 1) != 0;
+                float* yb = y + static_cast<size_t>(nt * BN + c * kCols + (odd ? 1 : 0)) * Mh +
+                            (m >> 1);
+#pragma unroll
+                for (int k = 0; k < kCols / 2; ++k) {
+                  const float r =
+                      __shfl_xor_sync(0xffffffffu, odd ? val[2 * k] : val[2 * k + 1], 1);
+                  const float g = odd ? r : val[2 * k];
+                  const float u = odd ? val[2 * k + 1] : r;
+                  yb[static_cast<size_t>(2 * k) * Mh] = __fmul_rn(gate_act(K_ - 3, g), u);
+                }
+                continue;
+              }
               const size_t o0 = static_cast<size_t>(nt * BN + c * kCols) * M + m;
 #pragma unroll
               for (int j = 0; j < kCols; ++j) {
@@ -395,7 +426,14 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
               const int n = nt * BN + c * kCols + j;
               const int qs_j = __shfl_sync(0xffffffffu, qsr[c], j);
               const float sx_j = __shfl_sync(0xffffffffu, sxr[c], j);
-              if (n < N && m < M) {
+              if constexpr (K_ >= 3) {  // the pair's shuffle runs in every lane
+                const float fd = static_cast<float>(static_cast<int>(v[j]) - qs_j);
+                const float val = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx_j)
+                                             : __fmul_rn(fd, __fmul_rn(sw, sx_j));
+                const float up = __shfl_down_sync(0xffffffffu, val, 1);
+                if (n < N && m < M && (m & 1) == 0)
+                  y[static_cast<size_t>(n) * Mh + (m >> 1)] = __fmul_rn(gate_act(K_ - 3, val), up);
+              } else if (n < N && m < M) {
                 const int d = static_cast<int>(v[j]) - qs_j;
                 const size_t o = static_cast<size_t>(n) * M + m;
                 if constexpr (K_ == 0) {
@@ -417,8 +455,12 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
           chunk(std::integral_constant<int, 0>());
         else if (kind == 1)
           chunk(std::integral_constant<int, 1>());
-        else
+        else if (kind == 2)
           chunk(std::integral_constant<int, 2>());
+        else if (kind == 3)
+          chunk(std::integral_constant<int, 3>());
+        else
+          chunk(std::integral_constant<int, 4>());
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm->acce[a]);
@@ -533,7 +575,8 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
 // Each CTA accumulates its partial in its own TMEM. The reduction is a
 // reduce-scatter over distributed shared memory driven by the bulk-copy engine:
 // each CTA stages its partial tile in its own shared memory, then one thread
-// sends every owner rank o the rows [o*RB, o*RB+RB) (RB = ceil(128/S)) with one
+// sends every owner rank o the rows [o*RB, o*RB+RB) (RB = ceil(128/S) rounded up
+// to even, so a gated layer's gate|up row pair has one owner) with one
 // cp.async.bulk shared::cta -> shared::cluster copy into slot [src] of the
 // owner's buffer, completing as transaction bytes on the owner's mbarrier; the
 // owner sums its S slots in rank order (integers: exact) and writes the outputs.
@@ -585,7 +628,7 @@ OBN_DEVINL bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-constexpr int kRedRows = 136;  // >= S * ceil(128 / S) for every S <= 8
+constexpr int kRedRows = 140;  // >= S * RB for every S <= 8 (7 * 20)
 constexpr int kSplitKDefaultCtas = 148;
 constexpr size_t kSkMinSmem = 120 * 1024;
 
@@ -697,7 +740,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
   const int b0 = static_cast<int>(rank * KB / S);
   const int nb_slice = static_cast<int>((rank + 1) * KB / S) - b0;
   const int nb = min(nb_slice, NB);  // the host keeps every slice within NB blocks
-  const int RB = (kBM + static_cast<int>(S) - 1) / static_cast<int>(S);
+  const int RB = (((kBM + static_cast<int>(S) - 1) / static_cast<int>(S)) + 1) & ~1;
   if (tid == 0 && (nb_slice > NB || S > 8)) record_error(DEVERR_BAD_LAUNCH);
 
   const int ng = (nb + kSkGroup - 1) / kSkGroup;
@@ -867,17 +910,28 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
   const int nrows = (row0 + RB <= kBM ? RB : kBM - row0);
   const int nrb = (nrows + 31) >> 5;  // 1 or 2 row blocks (RB <= 64)
   const int ngrp = (min(BN, N) + 7) >> 3;  // 8-column groups
-  // The store kind (int32 accumulators, y = val, y += val) is fixed per launch and
-  // compiled separately, so a plain store never carries a speculated read of y.
-  const int kind = acc_out ? 0 : (order & kOutAccumulate) ? 2 : 1;
+  // The store kind (int32 accumulators, y = val, y += val, gated pairs) is fixed
+  // per launch and compiled separately, so a plain store never carries a
+  // speculated read of y. Gated pairs: row blocks start on even rows (RB is
+  // even), so rows 2i and 2i + 1 sit in lanes 2i and 2i + 1 of one warp.
+  const int kind = acc_out                    ? 0
+                   : (order & kOutGated)      ? ((order & kOutSilu) ? 4 : 3)
+                   : (order & kOutAccumulate) ? 2
+                                              : 1;
   const bool gemv_order = (order & 1) == kOrderGemv;
+  const size_t Mh = static_cast<size_t>(M) >> 1;
   auto reduce = [&](auto kind_c) {
     constexpr int K_ = decltype(kind_c)::value;
     for (int item = warp; item < nrb * ngrp; item += kThreads / 32) {
       const int rb = item & (nrb - 1), grp = item >> (nrb - 1);  // nrb is 1 or 2
-      const int rr = rb * 32 + lane;
+      int rr = rb * 32 + lane;
       const int m = mt * kBM + row0 + rr;
-      if (rr >= nrows || m >= M) continue;
+      const bool valid = rr < nrows && m < M;
+      if constexpr (K_ >= 3) {
+        rr = valid ? rr : 0;  // every lane reaches the pair shuffle, on a real row
+      } else {
+        if (!valid) continue;
+      }
       const int j0 = 8 * grp;
       // Every source rank's two 16-byte runs and the column scalars in flight
       // before the first sum.
@@ -922,7 +976,27 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
             y[o] = val;
         }
       };
-      if (j0 + 8 <= N) {
+      if constexpr (K_ >= 3) {
+        // lanes 2i (gate) and 2i + 1 (up) swap one value per column pair: the even
+        // lane forms column 2k, the odd lane column 2k + 1
+        float val[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float fd = static_cast<float>(sum[c]);
+          val[c] = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx[c])
+                              : __fmul_rn(fd, __fmul_rn(sw, sx[c]));
+        }
+        const int odd = m & 1;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float r = __shfl_xor_sync(0xffffffffu, odd ? val[2 * k] : val[2 * k + 1], 1);
+          const float g = odd ? r : val[2 * k];
+          const float u = odd ? val[2 * k + 1] : r;
+          const int col = j0 + 2 * k + odd;
+          if (valid && col < N)
+            y[static_cast<size_t>(col) * Mh + (m >> 1)] = __fmul_rn(gate_act(K_ - 3, g), u);
+        }
+      } else if (j0 + 8 <= N) {
 #pragma unroll
         for (int c = 0; c < 8; ++c) put(c);
       } else {
@@ -935,8 +1009,12 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
       reduce(std::integral_constant<int, 0>());
     else if (kind == 1)
       reduce(std::integral_constant<int, 1>());
-    else
+    else if (kind == 2)
       reduce(std::integral_constant<int, 2>());
+    else if (kind == 3)
+      reduce(std::integral_constant<int, 3>());
+    else
+      reduce(std::integral_constant<int, 4>());
   }
 
   tc_fence_before();

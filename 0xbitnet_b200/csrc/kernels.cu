@@ -469,14 +469,6 @@ __global__ __launch_bounds__(kGemvWarps * 32) void k_gemv(
 // ---------------------------------------------------------------------------
 constexpr int kN1Rows = 32;  // rows per CTA (two subtiles)
 
-// activation.wgsl:28-33 for a gated layer's gate value: 0 = ReLU^2, 1 = SiLU.
-OBN_DEVINL float gate_act(int act, float x) {
-  if (act == 0) {
-    const float r = fmaxf(0.0f, x);
-    return __fmul_rn(r, r);
-  }
-  return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
-}
 
 template <int EPT>
 __global__ __launch_bounds__(256) void k_bitlinear_n1(
@@ -774,11 +766,7 @@ namespace {
 // value, ReLU^2 (act 0: max(0, x)^2) or SiLU (act 1: x / (1 + exp(-x))).
 template <int ACT>
 OBN_DEVINL float activation(float x) {
-  if (ACT == 0) {
-    const float r = fmaxf(0.0f, x);
-    return __fmul_rn(r, r);
-  }
-  return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+  return gate_act(ACT, x);
 }
 
 // act(gate) * up over interleaved (gate, up) pairs: two outputs per thread from

@@ -14,6 +14,11 @@ enum EpilogueOrder : int {
   // OR-ed into the order: y += the result (the residual add that follows the
   // layer in the reference, elementwise.wgsl op 0), y = y + val rounded once.
   kOutAccumulate = 2,
+  // OR-ed into the order (k_gemm only): the weight rows are gated pairs (2i gate,
+  // 2i + 1 up) and y[t, i] = act(gate) * up is written, [n, rows / 2]; the
+  // activation is ReLU^2, or SiLU with kOutSilu.
+  kOutGated = 4,
+  kOutSilu = 8,
 };
 
 struct WeightView {

@@ -166,4 +166,14 @@ OBN_DEVINL float tree_sum_256(float v, float* sh) {
 }
 
 
+// activation.wgsl:28-33 for a gated layer's gate value: 0 = ReLU^2 (max(0, x)^2),
+// 1 = SiLU (x / (1 + exp(-x))).
+OBN_DEVINL float gate_act(int act, float x) {
+  if (act == 0) {
+    const float r = fmaxf(0.0f, x);
+    return __fmul_rn(r, r);
+  }
+  return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+}
+
 }  // namespace obn

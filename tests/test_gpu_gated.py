@@ -4,7 +4,7 @@ forward(x) must equal, bit for bit, the reference's FFN::forward_gated front:
 two BitLinear forwards (gate, up) on the same input followed by ReLU^2 on gate
 and an elementwise multiply by up (oracle: bitlinear twice + relu2_mul), for
 every matmul path: the fused single-token kernel, the dp4a GEMV, the split-K
-and persistent tensor-core GEMMs. The interleaved rows are also checked through
+and persistent tensor-core GEMMs (whose epilogues form act(gate) * up). The interleaved rows are also checked through
 the exact accumulators.
 """
 import numpy as np
@@ -24,7 +24,9 @@ def layers(M, K, seed):
 
 @pytest.mark.parametrize("M,K,n", [(6912, 2560, 1), (6912, 2560, 2), (6912, 2560, 8),
                                    (6912, 2560, 64), (1000, 384, 3), (300, 256, 40),
-                                   (6912, 2560, 300), (513, 640, 17)])
+                                   (6912, 2560, 300), (513, 640, 17),
+                                   # split-K over 3 and 7 CTAs (owner row blocks 44, 20)
+                                   (2560, 2560, 4), (1280, 2560, 9), (1280, 2560, 40)])
 def test_gated_forward_matches_two_bitlinears(M, K, n):
     torch = need_cuda()
     gate, up = layers(M, K, 100 + n)
@@ -35,6 +37,26 @@ def test_gated_forward_matches_two_bitlinears(M, K, n):
     g, _, _ = orc.bitlinear(x, gate.packed, gate.row_scales(), M, K, norm_w=gate.gamma)
     u, _, _ = orc.bitlinear(x, up.packed, up.row_scales(), M, K, norm_w=gate.gamma)
     assert np.array_equal(y, orc.relu2_mul(g, u))
+    L.close()
+
+
+@pytest.mark.parametrize("M,K,n", [(6912, 2560, 1), (6912, 2560, 2), (6912, 2560, 64),
+                                   (300, 256, 3), (6912, 2560, 300), (513, 640, 17),
+                                   (1280, 2560, 9)])
+def test_gated_silu_forward(M, K, n):
+    """SiLU gate (x / (1 + exp(-x)), activation.wgsl): every matmul path within the
+    error of the device's expf (a few ulp) of silu(gate) * up."""
+    torch = need_cuda()
+    gate, up = layers(M, K, 300 + n)
+    L = obn().BitLinear.from_i2s_gated(gate.blob(), up.blob(), K, M, norm_weight=gate.gamma)
+    L.set_activation(1)
+    x = synth().activations(400 + n, n, K)
+    y = L.forward(torch.from_numpy(x).cuda()).cpu().numpy()
+    g, _, _ = orc.bitlinear(x, gate.packed, gate.row_scales(), M, K, norm_w=gate.gamma)
+    u, _, _ = orc.bitlinear(x, up.packed, up.row_scales(), M, K, norm_w=gate.gamma)
+    with np.errstate(over="ignore"):
+        want = (g / (np.float32(1) + np.exp(-g))).astype(np.float32) * u
+    np.testing.assert_allclose(y, want, rtol=1e-6, atol=1e-30)
     L.close()
 
 
