@@ -63,8 +63,8 @@ def parse_args():
                    help="config-4 tensor-parallel prefill tokens when run on N > 1 GPUs (0 skips)")
     p.add_argument("--case", type=str, default=None,
                    help="SHAPE:B — run a few forwards of one 2B shape (or of 'all' five in "
-                        "turn; or 'lmhead' / 'attn') at B tokens and exit (a small, "
-                        "self-contained workload for ncu captures)")
+                        "turn; or 'lmhead' / 'attn' / 'gateup') at B tokens and exit (a "
+                        "small, self-contained workload for ncu captures)")
     return p.parse_args()
 
 
@@ -1015,6 +1015,23 @@ def run_case(spec: str):
             att.attention(q, cache, 20, 1, 2048)
         torch.cuda.synchronize()
         print(f"case attn B={B}: ok")
+        return
+    if name == "gateup":  # merged 6912 x 2560 gate|up layer, ReLU^2 x up in the matmul epilogue
+        M, K = synth.SHAPES_2B["gate"]
+        layers = []
+        for i in range(4):
+            gp, gs, gamma = synth.layer_device(91 + 2 * i, M, K)
+            up, us, _ = synth.layer_device(92 + 2 * i, M, K)
+            layers.append(obn.BitLinear.create_gated(gp, gs, up, us, gamma, K, M))
+        x = torch.randn(B, K, device="cuda")
+        for _ in range(3):
+            for L in layers:
+                L.forward(x)
+        torch.cuda.synchronize()
+        obn.check_device_errors()
+        for L in layers:
+            L.close()
+        print(f"case gateup {M}x{K} B={B}: ok")
         return
     names = list(synth.SHAPES_2B) if name == "all" else [name]
     for nm in names:
