@@ -350,11 +350,77 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
         const bool full_tile = (nt + 1) * BN <= N && (mt + 1) * kBM <= M;
         auto chunk = [&](auto kind_c) {
           constexpr int K_ = decltype(kind_c)::value;
-          if (full_tile) {
+          if constexpr (K_ >= 3) {
+            if (full_tile) {
+              // Gated pairs: lanes 2i (gate row) and 2i + 1 (up row) swap one
+              // value per column pair (2k, 2k + 1), so the even lane forms column
+              // 2k and the odd lane column 2k + 1: every lane stores. The chunk
+              // loop stays rolled (the column scalars shift down one chunk per
+              // pass) to keep the epilogue's code small next to the other roles'.
+              int qr[kChunks];
+              float xr[kChunks];
+#pragma unroll
+              for (int c = 0; c < kChunks; ++c) {
+                qr[c] = qsr[c];
+                xr[c] = sxr[c];
+              }
+              const bool odd = (m & 1) != 0;
+              float* yb = y + static_cast<size_t>(nt * BN + (odd ? 1 : 0)) * Mh + (m >> 1);
+#pragma unroll 1
+              for (int c = 0; c < kChunks; ++c) {
+                uint32_t v[kCols];
+                if constexpr (kCols == 32)
+                  tmem_ld32(taddr + c * 32, v);
+                else
+                  tmem_ld16(taddr + c * 16, v);
+                int qs_v[kCols];
+                float sx_v[kCols];
+#pragma unroll
+                for (int j = 0; j < kCols; ++j) {
+                  qs_v[j] = __shfl_sync(0xffffffffu, qr[0], j);
+                  sx_v[j] = __shfl_sync(0xffffffffu, xr[0], j);
+                }
+                tmem_ld_wait();
+                float val[kCols];
+#pragma unroll
+                for (int j = 0; j < kCols; ++j) {
+                  const float fd = static_cast<float>(static_cast<int>(v[j]) - qs_v[j]);
+                  val[j] = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx_v[j])
+                                      : __fmul_rn(fd, __fmul_rn(sw, sx_v[j]));
+                }
+#pragma unroll
+                for (int k = 0; k < kCols / 2; ++k) {
+                  const float r =
+                      __shfl_xor_sync(0xffffffffu, odd ? val[2 * k] : val[2 * k + 1], 1);
+                  const float g = odd ? r : val[2 * k];
+                  const float u = odd ? val[2 * k + 1] : r;
+                  yb[static_cast<size_t>(2 * k) * Mh] = __fmul_rn(gate_act(K_ - 3, g), u);
+                }
+                yb += static_cast<size_t>(kCols) * Mh;
+#pragma unroll
+                for (int k = 0; k + 1 < kChunks; ++k) {
+                  qr[k] = qr[k + 1];
+                  xr[k] = xr[k + 1];
+                }
+              }
+              return;
+            }
+          }
+          if (K_ < 3 && full_tile) {
             // Every column and row in range: branch-free chunks, the 2 * kCols
             // broadcasts first, so the conversions, products and stores of a
             // chunk issue back to back instead of one column's chain at a time.
+            // The chunk loop stays rolled (column scalars shifted down a chunk
+            // per pass): the unrolled epilogue's code crowded the instruction
+            // cache the producer, expansion and MMA warps share.
+            int qr[kChunks];
+            float xr[kChunks];
 #pragma unroll
+            for (int c = 0; c < kChunks; ++c) {
+              qr[c] = qsr[c];
+              xr[c] = sxr[c];
+            }
+#pragma unroll 1
             for (int c = 0; c < kChunks; ++c) {
               uint32_t v[kCols];
               if constexpr (kCols == 32)
@@ -365,34 +431,15 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
               float sx_v[kCols];
 #pragma unroll
               for (int j = 0; j < kCols; ++j) {
-                qs_v[j] = __shfl_sync(0xffffffffu, qsr[c], j);
-                sx_v[j] = __shfl_sync(0xffffffffu, sxr[c], j);
+                qs_v[j] = __shfl_sync(0xffffffffu, qr[0], j);
+                sx_v[j] = __shfl_sync(0xffffffffu, xr[0], j);
+              }
+#pragma unroll
+              for (int k = 0; k + 1 < kChunks; ++k) {
+                qr[k] = qr[k + 1];
+                xr[k] = xr[k + 1];
               }
               tmem_ld_wait();
-              if constexpr (K_ >= 3) {
-                // Gated pairs: lanes 2i (gate row) and 2i + 1 (up row) swap one
-                // value per column pair (2k, 2k + 1), so the even lane forms
-                // column 2k and the odd lane column 2k + 1: every lane stores.
-                float val[kCols];
-#pragma unroll
-                for (int j = 0; j < kCols; ++j) {
-                  const float fd = static_cast<float>(static_cast<int>(v[j]) - qs_v[j]);
-                  val[j] = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx_v[j])
-                                      : __fmul_rn(fd, __fmul_rn(sw, sx_v[j]));
-                }
-                const bool odd = (m & 1) != 0;
-                float* yb = y + static_cast<size_t>(nt * BN + c * kCols + (odd ? 1 : 0)) * Mh +
-                            (m >> 1);
-#pragma unroll
-                for (int k = 0; k < kCols / 2; ++k) {
-                  const float r =
-                      __shfl_xor_sync(0xffffffffu, odd ? val[2 * k] : val[2 * k + 1], 1);
-                  const float g = odd ? r : val[2 * k];
-                  const float u = odd ? val[2 * k + 1] : r;
-                  yb[static_cast<size_t>(2 * k) * Mh] = __fmul_rn(gate_act(K_ - 3, g), u);
-                }
-                continue;
-              }
               const size_t o0 = static_cast<size_t>(nt * BN + c * kCols) * M + m;
 #pragma unroll
               for (int j = 0; j < kCols; ++j) {

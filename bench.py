@@ -453,7 +453,8 @@ def measure_ffn_gate_up(args, obn, synth, dev, stream, batches):
         merged.append(obn.BitLinear.from_i2s_gated(g.blob(), u.blob(), K, M, norm_weight=g.gamma,
                                                    device=dev.index))
     out = {"shape": [M, K], "layers": nl, "per_batch": {}}
-    for B in batches:
+    # the decode batches, then two prefill chunk sizes (tensor-core GEMM epilogue)
+    for B in list(batches) + [512, 2048]:
         x = torch.randn(B, K, device=dev)
         yg, yu, ym = (torch.empty(B, M, device=dev) for _ in range(3))
 
