@@ -460,19 +460,34 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
             }
             return;
           }
+          // Partial tiles: per-column bounds checks, the chunk loop rolled as above.
+          int qr[kChunks];
+          float xr[kChunks];
 #pragma unroll
+          for (int c = 0; c < kChunks; ++c) {
+            qr[c] = qsr[c];
+            xr[c] = sxr[c];
+          }
+#pragma unroll 1
           for (int c = 0; c < kChunks; ++c) {
             uint32_t v[kCols];
             if constexpr (kCols == 32)
               tmem_ld32(taddr + c * 32, v);
             else
               tmem_ld16(taddr + c * 16, v);
+            const int qs_c = qr[0];
+            const float sx_c = xr[0];
+#pragma unroll
+            for (int k = 0; k + 1 < kChunks; ++k) {
+              qr[k] = qr[k + 1];
+              xr[k] = xr[k + 1];
+            }
             tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < kCols; ++j) {
               const int n = nt * BN + c * kCols + j;
-              const int qs_j = __shfl_sync(0xffffffffu, qsr[c], j);
-              const float sx_j = __shfl_sync(0xffffffffu, sxr[c], j);
+              const int qs_j = __shfl_sync(0xffffffffu, qs_c, j);
+              const float sx_j = __shfl_sync(0xffffffffu, sx_c, j);
               if constexpr (K_ >= 3) {  // the pair's shuffle runs in every lane
                 const float fd = static_cast<float>(static_cast<int>(v[j]) - qs_j);
                 const float val = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx_j)
