@@ -19,6 +19,11 @@
 // The MMA accumulates sum_k c q = sum_k w q + sum_k q; the epilogue subtracts
 // the per-token code sum qsum[n] (exact, integer).
 //
+// Gated layers (rows 2i = gate row i, 2i + 1 = up row i, order | kOutGated):
+// the epilogue writes act(gate) * up to Out[n, i] ([N][M / 2]); the two lanes of
+// a row pair swap one value per column pair, so each lane stores one column of
+// the pair (64-byte runs over i per column).
+//
 // Warp roles (384 threads, one persistent CTA per SM):
 //   warp 0      TMA / bulk-copy producer
 //   warp 1      MMA issuer (one thread)
