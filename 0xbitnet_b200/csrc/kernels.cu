@@ -863,10 +863,6 @@ cudaError_t launch_act_mul(const float* gu, int n, int d, int act, float* y, cud
                     pairs2, total, y);
 }
 
-cudaError_t launch_relu2_mul(const float* gu, int n, int d, float* y, cudaStream_t s) {
-  return launch_act_mul(gu, n, d, 0, y, s);
-}
-
 cudaError_t launch_act(const float* x, size_t count, int act, float* y, cudaStream_t s) {
   if (count == 0) return cudaSuccess;
   const unsigned blocks = static_cast<unsigned>((count + 255) / 256);

@@ -41,11 +41,9 @@ cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps,
 cudaError_t launch_rmsnorm(const float* x, const float* w, float eps, int n, int d, float* y,
                            cudaStream_t s);
 
-// Gated FFN activation over interleaved gate|up outputs (activation.wgsl ReLU^2,
-// then elementwise.wgsl multiply): y[i] = (r * r) * gu[2i + 1], r = max(0, gu[2i]),
-// for i < n * d (gu: [n, 2d], y: [n, d]).
-cudaError_t launch_relu2_mul(const float* gu, int n, int d, float* y, cudaStream_t s);
-// act(gate) * up over interleaved pairs; act 0 = ReLU^2, 1 = SiLU.
+// Gated FFN activation over interleaved gate|up outputs (activation.wgsl, then
+// elementwise.wgsl multiply): y[i] = act(gu[2i]) * gu[2i + 1] for i < n * d
+// (gu: [n, 2d], y: [n, d]); act 0 = ReLU^2 (max(0, g)^2), 1 = SiLU.
 cudaError_t launch_act_mul(const float* gu, int n, int d, int act, float* y, cudaStream_t s);
 // y[i] = act(x[i]) for i < count (y may alias x).
 cudaError_t launch_act(const float* x, size_t count, int act, float* y, cudaStream_t s);
