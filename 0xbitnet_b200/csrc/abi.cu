@@ -552,8 +552,10 @@ int forward_impl(const obn_bitlinear* layer, const float* x, int n, float* y, vo
   auto* q = reinterpret_cast<int8_t*>(base);
   auto* sc = reinterpret_cast<float*>(base + align256(static_cast<size_t>(n) * layer->in_dim));
   auto* qs = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(sc) + align256(sizeof(float) * n));
-  // Gated layers: the matmul writes the interleaved [n, 2*out_dim] gate|up outputs
-  // here, and relu(gate)^2 * up goes to y.
+  // Gated layers on the dp4a GEMV path (2-3 tokens): the matmul writes the
+  // interleaved [n, 2*out_dim] gate|up outputs here and act(gate) * up goes to y.
+  // The single-token kernel and the tensor-core GEMMs write act(gate) * up to y
+  // from their epilogues.
   float* ym = layer->gated ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(qs) +
                                                       align256(sizeof(float) * n))
                            : y;
