@@ -138,6 +138,15 @@ int check_layer(const obn_bitlinear* L) {
   return OBN_OK;
 }
 
+// A gated layer whose n-token forward runs the dp4a GEMV (not the single-token
+// kernel, not the tensor-core GEMM): only then are the interleaved gate|up rows
+// stored in the workspace before k_act_mul forms act(gate) * up.
+bool gated_gemv_path(const obn_bitlinear* L, int n) {
+  if (!L->gated) return false;
+  if (n == 1 && L->in_dim <= obn::kGemvMaxK) return false;
+  return !obn::gemm_supported(view(L), n);
+}
+
 }  // namespace
 
 namespace obn {
@@ -443,8 +452,12 @@ int obn_bitlinear_rows(const obn_bitlinear* layer) { return layer ? layer->rows 
 
 size_t obn_bitlinear_workspace_bytes(const obn_bitlinear* layer, int n) {
   if (!layer || n <= 0) return 0;
-  const size_t pre = layer->gated ? align256(sizeof(float) * n * static_cast<size_t>(layer->rows))
-                                  : 0;  // interleaved gate|up outputs before the activation
+  // interleaved gate|up outputs before the activation: only the dp4a GEMV path of
+  // a gated layer stores them (the single-token kernel and the tensor-core GEMM
+  // epilogues write act(gate) * up straight to y)
+  const size_t pre = gated_gemv_path(layer, n)
+                         ? align256(sizeof(float) * n * static_cast<size_t>(layer->rows))
+                         : 0;
   return align256(static_cast<size_t>(n) * layer->in_dim) + 2 * align256(sizeof(float) * n) + pre;
 }
 
@@ -556,9 +569,9 @@ int forward_impl(const obn_bitlinear* layer, const float* x, int n, float* y, vo
   // interleaved [n, 2*out_dim] gate|up outputs here and act(gate) * up goes to y.
   // The single-token kernel and the tensor-core GEMMs write act(gate) * up to y
   // from their epilogues.
-  float* ym = layer->gated ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(qs) +
-                                                      align256(sizeof(float) * n))
-                           : y;
+  float* ym = gated_gemv_path(layer, n) ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(qs) +
+                                                                  align256(sizeof(float) * n))
+                                       : y;
   auto s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (n == 1 && layer->in_dim <= obn::kGemvMaxK) {  // whole BitLinear in one kernel

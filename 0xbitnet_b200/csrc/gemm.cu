@@ -808,7 +808,10 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
   const int nb_slice = static_cast<int>((rank + 1) * KB / S) - b0;
   const int nb = min(nb_slice, NB);  // the host keeps every slice within NB blocks
   const int RB = (((kBM + static_cast<int>(S) - 1) / static_cast<int>(S)) + 1) & ~1;
-  if (tid == 0 && (nb_slice > NB || S > 8)) record_error(DEVERR_BAD_LAUNCH);
+  // The owner reduce below decodes row blocks for 1 or 2 blocks of 32 rows (RB <= 64),
+  // which holds for 2 <= S <= 8; any other launch records an error and skips it.
+  const bool geom_ok = nb_slice <= NB && S >= 2 && S <= 8 && RB <= 64;
+  if (tid == 0 && !geom_ok) record_error(DEVERR_BAD_LAUNCH);
 
   const int ng = (nb + kSkGroup - 1) / kSkGroup;
   if (tid == 0) {
@@ -1071,7 +1074,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
       }
     }
   };
-  if (ok) {
+  if (ok && geom_ok) {
     if (kind == 0)
       reduce(std::integral_constant<int, 0>());
     else if (kind == 1)

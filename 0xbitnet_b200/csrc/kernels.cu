@@ -6,8 +6,8 @@
 //    nvcc cannot contract them into FMAs; rms = 1 / sqrt(mean + eps) with IEEE
 //    sqrt and division; y = (x * rms) * w (rmsnorm.wgsl:57-61).
 //  * Quantization: absmax (order-free), scale/inv with IEEE division and the
-//    absmax == 0 selects of quantize.wgsl:122,131, q = clamp(rint(y * inv))
-//    with round-half-even (WGSL round(), quantize.wgsl:134).
+//    absmax == 0 selects of quantize.wgsl:59,68, q = clamp(rint(y * inv))
+//    with round-half-even (WGSL round(), quantize.wgsl:71).
 //  * The matmul is integer: sum_k c[m,k] q[t,k] - sum_k q[t,k] with codes
 //    c = w + 1 in {0,1,2}, which equals sum_k w[m,k] q[t,k] exactly (any order).
 //  * The epilogue rounds in the order of the shader the reference would have
@@ -609,7 +609,7 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
 #pragma unroll
       for (int w = 0; w < 8; ++w) a += red[w][sb][r] - red_q[w];
       const float scale = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
-      // ternary_gemv.wgsl:232 order: (f32(acc) * s_w) * s_x
+      // ternary_gemv.wgsl:95 order: (f32(acc) * s_w) * s_x
       val = __fmul_rn(__fmul_rn(static_cast<float>(a), sw), scale);
     }
     if (act < 0) {

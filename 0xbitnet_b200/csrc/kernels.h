@@ -9,7 +9,7 @@ namespace obn {
 
 // Epilogue rounding order, as the two reference shaders write it.
 enum EpilogueOrder : int {
-  kOrderGemv = 0,  // (f32(acc) * s_w[m]) * s_x[t]      ternary_gemv.wgsl:232
+  kOrderGemv = 0,  // (f32(acc) * s_w[m]) * s_x[t]      ternary_gemv.wgsl:95
   kOrderGemm = 1,  // f32(acc) * (s_w[m] * s_x[t])      ternary_gemm.wgsl:132-133
   // OR-ed into the order: y += the result (the residual add that follows the
   // layer in the reference, elementwise.wgsl op 0), y = y + val rounded once.

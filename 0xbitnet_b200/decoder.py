@@ -82,13 +82,20 @@ def _gamma(g: torch.Generator, K: int, device) -> torch.Tensor:
 
 
 class DecoderLayer:
-    """One transformer block's weights on the device, as libobn layers."""
+    """One transformer block's weights on the device, as libobn layers. With
+    keep_source, the generated I2_S rows are also kept on the host (`source`:
+    name -> uint8 [rows, in/4]) as they were before the device repack, so a
+    checker can rebuild the block from them."""
 
-    def __init__(self, cfg: DecoderConfig, g: torch.Generator, device):
+    def __init__(self, cfg: DecoderConfig, g: torch.Generator, device,
+                 keep_source: bool = False):
         D, F, H, Hkv, d = cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.head_dim
         nq, nk = H * d, Hkv * d
+        self.source = {} if keep_source else None
         # q, k, v: three ternary tensors with their own scales -> one layer
         rows = [_ternary_rows(g, m, D, device) for m in (nq, nk, nk)]
+        if keep_source:
+            self.source["qkv"] = torch.cat(rows).cpu().numpy()
         scales = [_scale(g, device) for _ in range(3)]
         self.qkv_scales = scales  # per-tensor scales of q, k, v (kept for checks)
         s_w = torch.cat([torch.full((m,), s, dtype=torch.float32, device=device)
@@ -98,11 +105,15 @@ class DecoderLayer:
         del rows
         self.attn_sub_norm = _gamma(g, nq, device)
         o = _ternary_rows(g, D, nq, device)
+        if keep_source:
+            self.source["o"] = o.cpu().numpy()
         self.o_scale = _scale(g, device)
         self.o = BitLinear(o, torch.full((D,), self.o_scale, device=device),
                            self.attn_sub_norm, nq, D, cfg.eps)
         self.ffn_norm = _gamma(g, D, device)
         gate, up = _ternary_rows(g, F, D, device), _ternary_rows(g, F, D, device)
+        if keep_source:
+            self.source["gate"], self.source["up"] = gate.cpu().numpy(), up.cpu().numpy()
         self.gate_scale, self.up_scale = _scale(g, device), _scale(g, device)
         self.gate_up = BitLinear.create_gated(
             gate, torch.full((F,), self.gate_scale, device=device),
@@ -110,6 +121,8 @@ class DecoderLayer:
         del gate, up
         self.ffn_sub_norm = _gamma(g, F, device)
         dn = _ternary_rows(g, D, F, device)
+        if keep_source:
+            self.source["down"] = dn.cpu().numpy()
         self.down_scale = _scale(g, device)
         self.down = BitLinear(dn, torch.full((D,), self.down_scale, device=device),
                               self.ffn_sub_norm, F, D, cfg.eps)
@@ -122,7 +135,8 @@ class DecoderLayer:
 class BitNetDecoder:
     """B sequences decoding one token per step, KV caches of `ctx` positions."""
 
-    def __init__(self, cfg: DecoderConfig, B: int, ctx: int, device=None, seed: int = 0):
+    def __init__(self, cfg: DecoderConfig, B: int, ctx: int, device=None, seed: int = 0,
+                 keep_source: bool = False):
         self.cfg, self.B, self.ctx = cfg, B, ctx
         self.device = device if device is not None else torch.device(
             "cuda", torch.cuda.current_device())
@@ -130,7 +144,7 @@ class BitNetDecoder:
         g = torch.Generator(device=dev)
         g.manual_seed(seed)
         with torch.cuda.device(dev):
-            self.layers = [DecoderLayer(cfg, g, dev) for _ in range(cfg.layers)]
+            self.layers = [DecoderLayer(cfg, g, dev, keep_source) for _ in range(cfg.layers)]
             self.embed = (0.02 * torch.randn((cfg.vocab, cfg.hidden), generator=g,
                                              device=dev)).to(torch.float16)
             self.final_norm = _gamma(g, cfg.hidden, dev)

@@ -68,9 +68,31 @@ def parse_args():
     return p.parse_args()
 
 
+def synthetic_standalone():
+    """The package's pure-numpy generators (0xbitnet_b200/synthetic.py and i2s.py),
+    loaded by file path under a private package name so that the CPU legs never run
+    the package __init__, which maps libobn.so."""
+    import importlib.util
+    import types
+    name = "_obn_synthetic_pkg"
+    if name + ".synthetic" in sys.modules:
+        return sys.modules[name + ".synthetic"]
+    pkg_dir = os.path.join(ROOT, "0xbitnet_b200")
+    pkg = types.ModuleType(name)
+    pkg.__path__ = [pkg_dir]
+    sys.modules[name] = pkg
+    for sub in ("i2s", "synthetic"):
+        spec = importlib.util.spec_from_file_location(f"{name}.{sub}",
+                                                      os.path.join(pkg_dir, sub + ".py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[spec.name] = mod
+        spec.loader.exec_module(mod)
+        setattr(pkg, sub, mod)
+    return sys.modules[name + ".synthetic"]
+
+
 def shapes():
-    synth = importlib.import_module("0xbitnet_b200.synthetic")
-    return list(synth.SHAPES_2B.items())
+    return list(synthetic_standalone().SHAPES_2B.items())
 
 
 def fwd_bytes(M: int, K: int, B: int) -> int:
@@ -158,25 +180,33 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_sample(args, min_seconds=10.0, max_reps=50):
-    """Times the oracle (OpenMP, all host threads) on 1 layer x 5 shapes x every B."""
-    import numpy as np
-    import oracle as orc
-    synth = importlib.import_module("0xbitnet_b200.synthetic")
+def reference_sample(args):
+    """1 layer x 5 shapes x every B of the sweep, seeded; numpy only (no libobn)."""
+    synth = synthetic_standalone()
     batches = [int(b) for b in args.batches.split(",")]
     data = []
     for i, (name, (M, K)) in enumerate(shapes()):
         L = synth.layer(900 + i, M, K)
         xs = {B: synth.activations(950 + i * 10 + B, B, K) for B in batches}
         data.append((M, K, L, xs))
-    threads = host_threads()
-    bytes_per_rep = sum(fwd_bytes(M, K, B) for M, K, _, _ in data for B in batches)
+    step_bytes = sum(fwd_bytes(M, K, B) for M, K, _, _ in data for B in batches)
+    return batches, data, step_bytes
+
+
+def time_oracle(data, batches, threads, min_seconds, max_reps):
+    """Repetitions of the sample through the oracle's BitLinear: the literal
+    single-thread restatement (threads == 1) or its OpenMP form (row-parallel,
+    identical results). Returns (reps, seconds)."""
+    import oracle as orc
 
     def rep():
         for M, K, L, xs in data:
             for B in batches:
-                orc.bitlinear_omp(xs[B], L.packed, L.row_scales(), M, K, norm_w=L.gamma,
-                                  threads=threads)
+                if threads == 1:
+                    orc.bitlinear(xs[B], L.packed, L.row_scales(), M, K, norm_w=L.gamma)
+                else:
+                    orc.bitlinear_omp(xs[B], L.packed, L.row_scales(), M, K, norm_w=L.gamma,
+                                      threads=threads)
     rep()  # warm
     t0 = time.perf_counter()
     reps = 0
@@ -185,29 +215,37 @@ def cpu_sample(args, min_seconds=10.0, max_reps=50):
         reps += 1
         el = time.perf_counter() - t0
         if el >= min_seconds or reps >= max_reps:
-            break
+            return reps, el
+
+
+def cpu_sample(args, min_seconds=10.0, max_reps=50):
+    """Times the oracle on 1 layer x 5 shapes x every B: OpenMP over all host
+    threads (the reported value) and the literal single-thread build beside it."""
+    batches, data, bytes_per_rep = reference_sample(args)
+    threads = host_threads()
+    reps, el = time_oracle(data, batches, threads, min_seconds, max_reps)
+    reps1, el1 = time_oracle(data, batches, 1, min_seconds / 2, max_reps)
     return {"value": bytes_per_rep * reps / el / 1e9, "unit": "GB/s", "cores": threads,
             "kind": "port",
             "sample": f"1 layer x 5 shapes x B in {{{args.batches}}} ({reps} reps, "
-                      f"{el:.1f} s): the oracle's C restatement of the WGSL kernels"}
+                      f"{el:.1f} s): the oracle's C restatement of the WGSL kernels, OpenMP",
+            "single_thread": {"value": bytes_per_rep * reps1 / el1 / 1e9, "unit": "GB/s",
+                              "cores": 1, "kind": "port",
+                              "sample": f"same sample, literal single-thread build "
+                                        f"({reps1} reps, {el1:.1f} s)"}}
 
 
 def run_reference(args):
+    """The reference algorithm on the host cores: the oracle's C restatement of
+    the WGSL kernels (OpenMP over all host threads), one layer x 5 shapes x every
+    B per step. Nothing here imports the 0xbitnet_b200 package or maps libobn.so."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     import oracle as orc
-    import numpy as np
-    synth = importlib.import_module("0xbitnet_b200.synthetic")
-    batches = [int(b) for b in args.batches.split(",")]
-    data = []
-    for i, (name, (M, K)) in enumerate(shapes()):
-        L = synth.layer(900 + i, M, K)
-        xs = {B: synth.activations(950 + i * 10 + B, B, K) for B in batches}
-        data.append((M, K, L, xs))
+    batches, data, step_bytes = reference_sample(args)
     threads = host_threads()
-    step_bytes = sum(fwd_bytes(M, K, B) for M, K, _, _ in data for B in batches)
 
     def step():
         for M, K, L, xs in data:
@@ -221,6 +259,7 @@ def run_reference(args):
         step()
     el = time.perf_counter() - t0
     value = step_bytes * args.steps / el / 1e9
+    reps1, el1 = time_oracle(data, batches, 1, 5.0, 10)
     sample = (f"each step: 1 of the {args.layers} layers (5 shapes) x B in {{{args.batches}}}, "
               f"{step_bytes} algorithmic bytes; oracle C restatement, OpenMP")
     print(json.dumps({
@@ -230,7 +269,11 @@ def run_reference(args):
         "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded)",
         "config": config(args, world),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": sample,
+                         "single_thread": {"value": step_bytes * reps1 / el1 / 1e9,
+                                           "unit": "GB/s", "cores": 1, "kind": "port",
+                                           "sample": f"same step, literal single-thread build "
+                                                     f"({reps1} reps, {el1:.1f} s)"}},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)

@@ -146,7 +146,7 @@ OBN_API size_t obn_bitlinear_workspace_bytes(const obn_bitlinear* layer, int n);
  * or GEMM (n > 1) -> y[n, out_dim]. `workspace` (device, 256-byte aligned) must
  * hold obn_bitlinear_workspace_bytes(layer, n) bytes and must not be used by
  * other work in flight. The epilogue rounds like the reference: n == 1 gives
- * (f32(acc) * s_w) * s_x (ternary_gemv.wgsl:232), n > 1 gives
+ * (f32(acc) * s_w) * s_x (ternary_gemv.wgsl:95), n > 1 gives
  * f32(acc) * (s_w * s_x) (ternary_gemm.wgsl:132-133). */
 OBN_API int obn_bitlinear_forward(const obn_bitlinear* layer, const float* x, int n, float* y,
                           void* workspace, size_t workspace_bytes, void* stream);
@@ -167,10 +167,15 @@ OBN_API int obn_bitlinear_forward_residual(const obn_bitlinear* layer, const flo
  * obn_bitlinear_forward takes as `workspace` lives instead in one fixed device
  * array of 1 MiB + 32 KiB that every device loading the library holds until the
  * process exits; the call allocates nothing. Limits: n * in_dim <= 1048576 and
- * n <= 4096, otherwise OBN_ERR_UNSUPPORTED with a message naming the sizes.
+ * n <= 4096, and obn_bitlinear_workspace_bytes(layer, n) <= 1 MiB + 32 KiB (this
+ * only binds a gated layer on the dp4a GEMV path, 2-3 tokens, whose 4 * n *
+ * 2 * out_dim bytes of gate|up outputs also live there); otherwise
+ * OBN_ERR_UNSUPPORTED with a message naming the sizes.
  * The first call on a device looks the array's device address up (once per
  * device, with that device current); make that first call before any stream
- * capture. All calls on a device share the array and it keeps the previous
+ * capture. The address is kept for the life of the process, so a device reset
+ * (cudaDeviceReset) after that first call is not supported. All calls on a
+ * device share the array and it keeps the previous
  * call's contents (nothing in it needs to start at zero: every byte read is
  * first written by the same call); calls that overlap on the GPU race on it. */
 OBN_API int obn_bitlinear_forward_noalloc(const obn_bitlinear* layer, const float* x, int n,

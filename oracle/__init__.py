@@ -136,6 +136,19 @@ def ternary_acc(w_i2s: np.ndarray, q: np.ndarray, M: int, K: int) -> np.ndarray:
     return acc
 
 
+def ternary_acc_omp(w_i2s: np.ndarray, q: np.ndarray, M: int, K: int,
+                    threads: int = 0) -> np.ndarray:
+    """ternary_acc with rows split over OpenMP threads (identical results; for the
+    large test shapes)."""
+    w = np.ascontiguousarray(w_i2s, np.uint8)
+    q2 = np.ascontiguousarray(q, np.int8).reshape(-1, K)
+    N = q2.shape[0]
+    acc = np.empty((N, M), np.int32)
+    lib().orc_ternary_acc_omp(_p(w, _u8p), _p(q2, _i8p), M, N, K, _p(acc, _i32p),
+                              ctypes.c_int(threads))
+    return acc
+
+
 def ternary_gemv(w_i2s, q, s_w, s_x: float, M: int, K: int) -> np.ndarray:
     """ternary_gemv.wgsl:55-96."""
     w = np.ascontiguousarray(w_i2s, np.uint8)

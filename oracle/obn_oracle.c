@@ -174,7 +174,49 @@ void orc_ternary_acc(const uint8_t* w_i2s, const int8_t* q, int M, int N, int K,
       acc[(size_t)n * M + m] = row_dot(w_i2s + (size_t)m * rb, q + (size_t)n * K, K);
 }
 
-/* ternary_gemv.wgsl:230-233: sum * scales[row] * input_scale, left to right. */
+/* The same int32 accumulators, faster for large test shapes: each weight row is
+ * decoded once (the row_dot decode above: block = col/8, element base_gp + bi +
+ * 32 g of the block in bits 7-2g:6-2g of byte bi) and dotted with every token;
+ * rows are split over OpenMP threads. Integer sums do not depend on their order,
+ * so the result equals orc_ternary_acc exactly. */
+void orc_ternary_acc_omp(const uint8_t* w_i2s, const int8_t* q, int M, int N, int K,
+                         int32_t* acc, int threads) {
+#ifdef _OPENMP
+  int nt = threads > 0 ? threads : omp_get_max_threads();
+#else
+  int nt = 1; (void)threads;
+#endif
+  size_t rb = (size_t)K / 4;
+#pragma omp parallel num_threads(nt)
+  {
+    int8_t* w = (int8_t*)malloc((size_t)K);
+#pragma omp for schedule(static)
+    for (int m = 0; m < M; ++m) {
+      const uint8_t* wr = w_i2s + (size_t)m * rb;
+      for (int col = 0; col < K / 16; ++col) {
+        const uint8_t* p = wr + 4 * col;
+        int block = col / 8, base_gp = (col % 8) * 4;
+        for (int bi = 0; bi < 4; ++bi) {
+          uint32_t bv = p[bi];
+          int base = block * 128 + base_gp + bi;
+          w[base] = (int8_t)((int)((bv >> 6) & 3u) - 1);
+          w[base + 32] = (int8_t)((int)((bv >> 4) & 3u) - 1);
+          w[base + 64] = (int8_t)((int)((bv >> 2) & 3u) - 1);
+          w[base + 96] = (int8_t)((int)(bv & 3u) - 1);
+        }
+      }
+      for (int n = 0; n < N; ++n) {
+        const int8_t* qr = q + (size_t)n * K;
+        int32_t a = 0;
+        for (int k = 0; k < K; ++k) a += (int32_t)w[k] * (int32_t)qr[k];
+        acc[(size_t)n * M + m] = a;
+      }
+    }
+    free(w);
+  }
+}
+
+/* ternary_gemv.wgsl:93-95: sum * scales[row] * input_scale, left to right. */
 void orc_ternary_gemv(const uint8_t* w_i2s, const int8_t* q, const float* s_w,
                       float s_x, int M, int K, float* out) {
   size_t rb = (size_t)K / 4;
@@ -323,11 +365,13 @@ float orc_half_to_float(uint16_t h) {
  * pair, :51-57), then the halving tree (:63-68). embed [V, D] binary16. */
 void orc_lm_head_f16(const float* hidden, const uint16_t* embed, int N, int V, int D,
                      float* out) {
-  float part[ORC_LANES];
   const int dh_n = D / 2;
   for (int n = 0; n < N; ++n) {
     const float* h = hidden + (size_t)n * D;
+    /* logits are independent: split over threads, each with its own lanes */
+#pragma omp parallel for schedule(static)
     for (int v = 0; v < V; ++v) {
+      float part[ORC_LANES];
       const uint16_t* e = embed + (size_t)v * D;
       for (int tid = 0; tid < ORC_LANES; ++tid) {
         float acc = 0.0f;

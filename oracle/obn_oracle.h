@@ -69,6 +69,10 @@ void orc_quantize(const float* x, int N, int D, int8_t* q, float* scales);
  * t decoded from I2_S rows of K/4 bytes. */
 void orc_ternary_acc(const uint8_t* w_i2s, const int8_t* q, int M, int N, int K,
                      int32_t* acc);
+/* orc_ternary_acc with each row decoded once and rows split over OpenMP threads
+ * (threads <= 0: all); identical results. */
+void orc_ternary_acc_omp(const uint8_t* w_i2s, const int8_t* q, int M, int N, int K,
+                         int32_t* acc, int threads);
 
 /* ternary_gemv.wgsl: out[m] = (f32(acc[m]) * s_w[m]) * s_x.
  * acc is reduced per row exactly as the shader does (int, order-free). */

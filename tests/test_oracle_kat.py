@@ -134,7 +134,7 @@ def test_quantize_dequant_error():  # :68-83
 
 
 def test_quantize_rounds_ties_to_even():
-    # WGSL round() (quantize.wgsl:134) is ties-to-even. The TS helper's
+    # WGSL round() (quantize.wgsl:71) is ties-to-even. The TS helper's
     # Math.round (reference.ts:70) rounds ties up and would give -63 / 3 here;
     # the shader, which is what runs, is the contract.
     x = np.array([[127.0, -63.5, 2.5, 0.5, -0.5, 1.5]], np.float32)
@@ -477,3 +477,13 @@ def test_attention_uniform_scores_average_v():  # softmax.test.ts uniform
     V = np.arange(12, dtype=np.float32).reshape(4, 3)
     out = orc.attention(np.zeros((1, 3), np.float32), np.zeros((4, 3), np.float32), V, 1, 1, 3)
     np.testing.assert_allclose(out[0], V.mean(0), rtol=1e-6)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 128, 1), (100, 256, 7), (300, 640, 33), (17, 6912, 3)])
+def test_openmp_accumulators_equal_the_shader_restatement(M, K, N):
+    # orc_ternary_acc_omp (rows decoded once, OpenMP) is the checker of the large
+    # GPU parity shapes; it must equal the shader-order orc_ternary_acc exactly.
+    rng = np.random.default_rng(M * K + N)
+    w = rng.integers(0, 256, (M, K // 4), dtype=np.uint8)
+    q = rng.integers(-127, 128, (N, K), dtype=np.int8)
+    assert np.array_equal(orc.ternary_acc_omp(w, q, M, K), orc.ternary_acc(w, q, M, K))
