@@ -20,6 +20,8 @@
 
 namespace obn {
 
+int num_sms_cached();
+
 namespace {
 
 template <typename... KArgs, typename... Args>
@@ -447,61 +449,80 @@ __global__ __launch_bounds__(kGemvWarps * 32) void k_gemv(
 // ---------------------------------------------------------------------------
 // Single-token BitLinear in one kernel: RMSNorm + quantize + GEMV.
 //
-// One decode token leaves no work to share, so every CTA (two 16-row
-// subtiles, 256 threads) normalises and quantizes the token itself; that keeps
-// the whole BitLinear to one launch and one dependent round trip. Before the
-// PDL wait the CTA prefetches everything that does not depend on earlier
-// kernels: its packed weights (one bulk copy into shared memory), its row
-// scales and, in registers, the RMSNorm gamma of the columns each thread owns.
+// One decode token leaves no work to share, so every CTA normalises and
+// quantizes the token itself and the whole BitLinear is one launch and one
+// dependent round trip. The grid spreads the layer's 16-row subtiles evenly over
+// at most one CTA per SM (a CTA takes a contiguous run of up to NSUB subtiles,
+// one bulk copy in the T16 layout), so every SM streams weights. Before the PDL
+// wait a CTA fetches everything that does not depend on earlier kernels: its
+// packed weights (bulk copy into shared memory), its row scales and, in
+// registers, the RMSNorm gamma of the columns each thread owns. The grid keeps
+// shared memory near a third of an SM, so the next launches' CTAs become
+// resident, and start their own weight copies, while this one runs.
 //
-// After the wait the kernel is latency-bound (a chain of dependent steps that
-// is several times longer than streaming the CTA's weights), so the chain is
-// cut to four block barriers. Thread t owns columns t + 256j, the columns lane
-// t of rmsnorm.wgsl / quantize.wgsl owns, so its sum of squares is that lane's
-// partial (and its loads are coalesced). The partials meet in shared memory
-// once; then every warp finishes the shaders' halving tree by itself: lane l
-// folds strides 128, 64, 32 from eight partials in the tree's order, shuffles
-// do strides 16 .. 1, and every thread computes 1/rms, so no broadcast barrier
-// follows. The absmax takes a second barrier, the quantized row a third, the
-// row sums the last. In the dot product each warp covers both subtiles over
-// every eighth 128-column block, so one q vector read from shared memory feeds
-// two rows.
+// After the wait the kernel is a chain of dependent steps with three block
+// barriers:
+//   A  thread t loads the columns t + 256j (the lane mapping of rmsnorm.wgsl /
+//      quantize.wgsl), folds its sum of squares in the shader's order and
+//      publishes it; every warp then finishes the shader's halving tree itself
+//      (lane l folds strides 128, 64, 32 from eight partials, shuffles do 16..1)
+//      and derives 1/rms, so no broadcast barrier follows;
+//   B  each thread normalises its columns into shared memory and publishes its
+//      warp's max |value|; after the barrier every thread derives the scale;
+//   -  warp w then quantizes only the 128-column blocks b = w, w + 8, ... that
+//      its own dot product consumes (the normalised values of those columns are
+//      in shared memory since B), so the int8 row needs no block barrier, only
+//      a warp sync; the warp's code sum is kept for the epilogue;
+//   D  each warp's row partials (all of the CTA's subtiles over its blocks) meet
+//      in shared memory; one thread per row sums them, subtracts the code sum
+//      and applies ternary_gemv.wgsl:95's epilogue.
+// Integer sums are exact in any order; every float step rounds as the shaders.
 // ---------------------------------------------------------------------------
-constexpr int kN1Rows = 32;  // rows per CTA (two subtiles)
+constexpr int kN1MaxCtaSmem = 100 * 1024;  // two launches' CTAs resident per SM
 
+// Dynamic shared memory of k_bitlinear_n1 with room for `wslots` subtiles of
+// packed weights, then the normalised row (f32) and the quantized row (int8).
+inline size_t n1_smem_bytes(int K, int nsub) {
+  return static_cast<size_t>(nsub) * (K / kBlockK) * kSubtileBytes + 5 * static_cast<size_t>(K);
+}
 
-template <int EPT>
+template <int EPT, int NSUB>
 __global__ __launch_bounds__(256) void k_bitlinear_n1(
     const uint8_t* __restrict__ W, const float* __restrict__ s_w,
     const float* __restrict__ gamma, float eps, const float* __restrict__ x,
-    float* __restrict__ y, int M, int K, int accumulate, int act) {
+    float* __restrict__ y, int M, int K, int accumulate, int act, int wslots) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bar;
-  __shared__ float sh_ss[256];  // per thread: sum of squares of its columns
-  __shared__ float sh_max[8];  // per warp: max |normalised x|
-  __shared__ int red_q[8];     // per warp: sum of q
-  __shared__ int red[8][2][16];
+  __shared__ float sh_ss[256];          // per thread: sum of squares of its columns
+  __shared__ float sh_max[8];           // per warp: max |normalised x|
+  __shared__ int red_q[8];              // per warp: code sum of its blocks
+  __shared__ int red[8][NSUB][16];      // per warp: row partials
 
   const int KB = K / kBlockK;
-  const int S0 = blockIdx.x * 2;  // first subtile
-  const int nsub = min(2, (M + kSubRows - 1) / kSubRows - S0);
-  if (nsub <= 0) return;  // uniform per CTA; the launcher never makes such CTAs
+  const int S_total = (M + kSubRows - 1) / kSubRows;
+  const int s0 = static_cast<int>(static_cast<long long>(blockIdx.x) * S_total / gridDim.x);
+  const int s1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * S_total / gridDim.x);
+  const int ns = s1 - s0;  // 1 .. NSUB (the launcher sizes the grid)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  uint8_t* w_s = smem;                                                     // 2 * KB * 512
-  int8_t* q_s = reinterpret_cast<int8_t*>(smem + 2 * KB * kSubtileBytes);  // K bytes
+  const bool geom_ok = ns >= 1 && ns <= wslots && wslots <= NSUB;
+  if (tid == 0 && !geom_ok) record_error(DEVERR_BAD_LAUNCH);
+  if (!geom_ok) return;  // uniform per CTA
+  uint8_t* w_s = smem;                                                         // wslots * KB * 512
+  float* xn_s = reinterpret_cast<float*>(smem + wslots * KB * kSubtileBytes);  // K floats
+  uint8_t* q_s = reinterpret_cast<uint8_t*>(xn_s + K);                       // K bytes
 
   if (tid == 0) {
     mbar_init(&bar, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  if (tid == 0) {  // both subtiles are one contiguous run in the T16 layout
-    const uint32_t wbytes = static_cast<uint32_t>(nsub * KB) * kSubtileBytes;
+  if (tid == 0) {  // the CTA's subtiles are one contiguous run in the T16 layout
+    const uint32_t wbytes = static_cast<uint32_t>(ns * KB) * kSubtileBytes;
     mbar_arrive_expect_tx(&bar, wbytes);
-    bulk_g2s_hint(w_s, W + subtile_offset(S0, 0, KB), wbytes, &bar, policy_evict_first());
+    bulk_g2s_hint(w_s, W + subtile_offset(s0, 0, KB), wbytes, &bar, policy_evict_first());
   }
-  const int row = S0 * kSubRows + tid;
-  const bool row_thread = tid < kN1Rows && row < M;
+  const int row = s0 * kSubRows + tid;  // epilogue: thread t < 16 * ns owns row s0*16 + t
+  const bool row_thread = tid < ns * kSubRows && row < M;
   const float sw = row_thread ? s_w[row] : 0.0f;
   float gv[EPT];
 #pragma unroll
@@ -520,6 +541,7 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
   }
   const float y_old = (accumulate && row_thread) ? y[row] : 0.0f;  // x != y (host check)
 
+  // ---- A: sum of squares -> 1/rms
   float rms = 1.0f;
   if (gamma) {
     float part = 0.0f;
@@ -528,7 +550,6 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
       if (tid + 256 * j < K) part = __fadd_rn(part, __fmul_rn(xv[j], xv[j]));
     sh_ss[tid] = part;
     __syncthreads();
-    // lane l: strides 128, 64, 32 of the tree for shader lane l, then 16 .. 1
     const float* p = sh_ss + lane;
     const float b0 = __fadd_rn(__fadd_rn(p[0], p[128]), __fadd_rn(p[64], p[192]));
     const float b1 = __fadd_rn(__fadd_rn(p[32], p[160]), __fadd_rn(p[96], p[224]));
@@ -539,11 +560,16 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
     const float total = __shfl_sync(0xffffffffu, tsum, 0);
     rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(K)), eps)));
   }
+  // ---- B: normalised row into shared memory, max |value|
   float lmax = 0.0f;
 #pragma unroll
   for (int j = 0; j < EPT; ++j) {
-    if (gamma && tid + 256 * j < K) xv[j] = norm_mul(xv[j], rms, gv[j]);
-    lmax = fmaxf(lmax, fabsf(xv[j]));
+    const int col = tid + 256 * j;
+    if (col < K) {
+      const float v = gamma ? norm_mul(xv[j], rms, gv[j]) : xv[j];
+      xn_s[col] = v;
+      lmax = fmaxf(lmax, fabsf(v));
+    }
   }
 #pragma unroll
   for (int s = 16; s >= 1; s >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, s));
@@ -553,64 +579,68 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
 #pragma unroll
   for (int w = 1; w < 8; ++w) absmax = fmaxf(absmax, sh_max[w]);
   const float inv = absmax == 0.0f ? 0.0f : __fdiv_rn(127.0f, absmax);
+
+  // ---- the warp's own blocks: quantize (lane = 4 columns), warp sync
   int qpart = 0;
+  for (int b = warp; b < KB; b += 8) {
+    const float4 v = *reinterpret_cast<const float4*>(xn_s + b * kBlockK + 4 * lane);
+    *reinterpret_cast<uint32_t*>(q_s + b * kBlockK + 4 * lane) = quant4(v, inv, qpart);
+  }
+  __syncwarp();
+
+  // ---- dot: per block, the lane's 16-byte q chunks once, then every subtile
+  int a[NSUB][4];
 #pragma unroll
-  for (int j = 0; j < EPT; ++j) {
-    const int col = tid + 256 * j;
-    if (col < K) {
-      const int qi = min(127, max(-127, __float2int_rn(__fmul_rn(xv[j], inv))));
-      q_s[col] = static_cast<int8_t>(qi);
-      qpart += qi;
+  for (int s = 0; s < NSUB; ++s)
+#pragma unroll
+    for (int g = 0; g < 4; ++g) a[s][g] = 0;
+  const bool ok = mbar_wait(&bar, 0);  // the weights (normally landed long ago)
+  if (!ok) mbar_wait(&bar, 0);         // copies may still be in flight: once more, bounded
+  if (ok) {
+    const uint32_t wl = smem_u32(w_s) + lane * 16;
+    const uint32_t qb = smem_u32(q_s) + (lane >> 4) * 16;
+    for (int b = warp; b < KB; b += 8) {
+      uint4 xq[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) xq[g] = lds128(qb + b * kBlockK + 32 * g);
+#pragma unroll
+      for (int s = 0; s < NSUB; ++s) {
+        if (s < ns) {
+          const uint4 wv = lds128(wl + (s * KB + b) * kSubtileBytes);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const uint32_t mask = 0xC0C0C0C0u >> (2 * g);
+            a[s][g] = dp4a_us(wv.w & mask, xq[g].w, dp4a_us(wv.z & mask, xq[g].z,
+                      dp4a_us(wv.y & mask, xq[g].y, dp4a_us(wv.x & mask, xq[g].x, a[s][g]))));
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < NSUB; ++s) {
+    if (s < ns) {
+      int acc = (a[s][0] >> 6) + (a[s][1] >> 4) + (a[s][2] >> 2) + a[s][3];
+      acc += __shfl_xor_sync(0xffffffffu, acc, 16);  // the two halves of the row
+      if (lane < 16) red[warp][s][lane] = acc;
     }
   }
 #pragma unroll
   for (int s = 16; s >= 1; s >>= 1) qpart += __shfl_xor_sync(0xffffffffu, qpart, s);
   if (lane == 0) red_q[warp] = qpart;
-  const bool ok = mbar_wait(&bar, 0);  // the weights (normally landed long ago)
-  if (!ok) mbar_wait(&bar, 0);         // copies may still be in flight: once more, bounded
   __syncthreads();
 
-  // Subtile 1 of a one-subtile CTA reads allocated but unwritten shared memory;
-  // those rows are >= M and never stored.
-  int a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
-  if (ok) {
-    const uint32_t w0 = smem_u32(w_s) + lane * 16;
-    const uint32_t w1 = w0 + KB * kSubtileBytes;
-    const uint32_t qb = smem_u32(q_s) + (lane >> 4) * 16;
-#pragma unroll 2
-    for (int b = warp; b < KB; b += 8) {
-      const uint4 wa = lds128(w0 + b * kSubtileBytes);
-      const uint4 wb = lds128(w1 + b * kSubtileBytes);
-#pragma unroll
-      for (int g = 0; g < 4; ++g) {
-        const uint32_t mask = 0xC0C0C0C0u >> (2 * g);
-        const uint4 xa = lds128(qb + b * kBlockK + 32 * g);
-        a0[g] = dp4a_us(wa.w & mask, xa.w, dp4a_us(wa.z & mask, xa.z,
-                dp4a_us(wa.y & mask, xa.y, dp4a_us(wa.x & mask, xa.x, a0[g]))));
-        a1[g] = dp4a_us(wb.w & mask, xa.w, dp4a_us(wb.z & mask, xa.z,
-                dp4a_us(wb.y & mask, xa.y, dp4a_us(wb.x & mask, xa.x, a1[g]))));
-      }
-    }
-  }
-  int acc0 = (a0[0] >> 6) + (a0[1] >> 4) + (a0[2] >> 2) + a0[3];
-  int acc1 = (a1[0] >> 6) + (a1[1] >> 4) + (a1[2] >> 2) + a1[3];
-  acc0 += __shfl_xor_sync(0xffffffffu, acc0, 16);
-  acc1 += __shfl_xor_sync(0xffffffffu, acc1, 16);
-  if (lane < 16) {
-    red[warp][0][lane] = acc0;
-    red[warp][1][lane] = acc1;
-  }
-  __syncthreads();
-  if (warp == 0) {
+  // ---- D: one thread per row (rows of a gated pair are adjacent lanes)
+  if (tid < NSUB * kSubRows) {
     float val = 0.0f;
     if (row_thread && ok) {
       const int sb = tid >> 4, r = tid & 15;
-      int a = 0;
+      int acc = 0;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) a += red[w][sb][r] - red_q[w];
+      for (int w = 0; w < 8; ++w) acc += red[w][sb][r] - red_q[w];
       const float scale = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
       // ternary_gemv.wgsl:95 order: (f32(acc) * s_w) * s_x
-      val = __fmul_rn(__fmul_rn(static_cast<float>(a), sw), scale);
+      val = __fmul_rn(__fmul_rn(static_cast<float>(acc), sw), scale);
     }
     if (act < 0) {
       if (row_thread && ok) y[row] = accumulate ? __fadd_rn(y_old, val) : val;
@@ -661,18 +691,38 @@ cudaError_t gemv_nt(const WeightView& W, const int8_t* q, const float* s_x, cons
                     W.out_dim, K, n, order);
 }
 
+template <int EPT, int NSUB>
+cudaError_t bitlinear_n1_run(const WeightView& W, const float* gamma, float eps, const float* x,
+                             float* y, int accumulate, int act, int grid, int wslots,
+                             cudaStream_t s) {
+  const int K = W.in_dim;
+  const size_t smem = n1_smem_bytes(K, wslots);
+  auto kern = k_bitlinear_n1<EPT, NSUB>;
+  cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kern), smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(kern, dim3(grid), dim3(256), smem, s, W.w, W.s_w, gamma, eps, x, y,
+                    W.out_dim, K, accumulate, act, wslots);
+}
+
+// Grid of the single-token kernel: the layer's 16-row subtiles spread evenly over
+// one CTA per SM (more CTAs only when a CTA's share would not fit its shared
+// memory budget); subtiles per CTA <= 2 or <= 8 picks the kernel's register tile.
 template <int EPT>
 cudaError_t bitlinear_n1_ept(const WeightView& W, const float* gamma, float eps, const float* x,
                              float* y, int accumulate, int act, cudaStream_t s) {
   const int K = W.in_dim;
-  const size_t smem =
-      2 * static_cast<size_t>(K / kBlockK) * kSubtileBytes + static_cast<size_t>(K);
-  auto kern = k_bitlinear_n1<EPT>;
-  cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kern), smem);
-  if (e != cudaSuccess) return e;
-  dim3 grid((W.out_dim + kN1Rows - 1) / kN1Rows);
-  return launch_pdl(kern, grid, dim3(256), smem, s, W.w, W.s_w, gamma, eps, x, y, W.out_dim, K,
-                    accumulate, act);
+  const int KB = K / kBlockK;
+  const int S_total = (W.out_dim + kSubRows - 1) / kSubRows;
+  const long long budget = kN1MaxCtaSmem - 5LL * K;
+  int cap = budget > 0 ? static_cast<int>(budget / (static_cast<long long>(KB) * kSubtileBytes)) : 1;
+  cap = cap < 1 ? 1 : cap > 8 ? 8 : cap;
+  int grid = num_sms_cached();
+  if (grid > S_total) grid = S_total;
+  if ((S_total + grid - 1) / grid > cap) grid = (S_total + cap - 1) / cap;
+  const int per_cta = (S_total + grid - 1) / grid;  // the most subtiles any CTA takes
+  if (per_cta <= 2)
+    return bitlinear_n1_run<EPT, 2>(W, gamma, eps, x, y, accumulate, act, grid, per_cta, s);
+  return bitlinear_n1_run<EPT, 8>(W, gamma, eps, x, y, accumulate, act, grid, per_cta, s);
 }
 
 template <bool ACC>
