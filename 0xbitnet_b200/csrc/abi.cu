@@ -144,7 +144,23 @@ int check_layer(const obn_bitlinear* L) {
 bool gated_gemv_path(const obn_bitlinear* L, int n) {
   if (!L->gated) return false;
   if (n == 1 && L->in_dim <= obn::kGemvMaxK) return false;
-  return !obn::gemm_supported(view(L), n);
+  return !obn::mma_gemv_supported(view(L), n) && !obn::gemm_supported(view(L), n);
+}
+
+// The matmul after the quantize pass for n tokens: the warp-MMA decode kernel
+// (2..32 tokens), the tcgen05 GEMM, or the dp4a GEMV.
+cudaError_t run_matmul(const obn_bitlinear* L, const int8_t* q, const float* sc,
+                       const int32_t* qs, int n, float* y, int32_t* acc, int order,
+                       cudaStream_t s, bool* unsupported) {
+  *unsupported = false;
+  if (obn::mma_gemv_supported(view(L), n))
+    return obn::launch_mma_gemv(view(L), q, sc, qs, n, y, acc, order, s);
+  if (obn::gemm_supported(view(L), n))
+    return obn::launch_gemm(view(L), q, sc, qs, n, y, acc, order, s);
+  if (L->in_dim <= obn::kGemvMaxK && !(order & obn::kOutGated))
+    return obn::launch_gemv(view(L), q, sc, qs, n, y, acc, order, s);
+  *unsupported = true;
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -469,14 +485,10 @@ int obn_ternary_matmul(const obn_bitlinear* layer, const int8_t* q, const float*
   if (n <= 0) return fail(OBN_ERR_INVALID_ARGUMENT, "n must be positive (got %d)", n);
   if (!aligned(q, 16)) return fail(OBN_ERR_INVALID_ARGUMENT, "q must be 16-byte aligned");
   const int order = n == 1 ? obn::kOrderGemv : obn::kOrderGemm;
-  cudaError_t e;
-  if (obn::gemm_supported(view(layer), n))
-    e = obn::launch_gemm(view(layer), q, scales, qsum, n, y, nullptr, order,
-                         static_cast<cudaStream_t>(stream));
-  else if (layer->in_dim <= obn::kGemvMaxK)
-    e = obn::launch_gemv(view(layer), q, scales, qsum, n, y, nullptr, order,
-                         static_cast<cudaStream_t>(stream));
-  else
+  bool unsupported = false;
+  const cudaError_t e = run_matmul(layer, q, scales, qsum, n, y, nullptr, order,
+                                   static_cast<cudaStream_t>(stream), &unsupported);
+  if (unsupported)
     return fail(OBN_ERR_UNSUPPORTED, "in_dim %d exceeds the kernels' limit", layer->in_dim);
   if (e != cudaSuccess) return cuda_fail(e, "ternary matmul launch");
   return OBN_OK;
@@ -489,14 +501,10 @@ int obn_ternary_acc(const obn_bitlinear* layer, const int8_t* q, const int32_t* 
   if (!q || !qsum || !acc) return fail(OBN_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (n <= 0) return fail(OBN_ERR_INVALID_ARGUMENT, "n must be positive (got %d)", n);
   if (!aligned(q, 16)) return fail(OBN_ERR_INVALID_ARGUMENT, "q must be 16-byte aligned");
-  cudaError_t e;
-  if (obn::gemm_supported(view(layer), n))
-    e = obn::launch_gemm(view(layer), q, nullptr, qsum, n, nullptr, acc, obn::kOrderGemm,
-                         static_cast<cudaStream_t>(stream));
-  else if (layer->in_dim <= obn::kGemvMaxK)
-    e = obn::launch_gemv(view(layer), q, nullptr, qsum, n, nullptr, acc, obn::kOrderGemm,
-                         static_cast<cudaStream_t>(stream));
-  else
+  bool unsupported = false;
+  const cudaError_t e = run_matmul(layer, q, nullptr, qsum, n, nullptr, acc, obn::kOrderGemm,
+                                   static_cast<cudaStream_t>(stream), &unsupported);
+  if (unsupported)
     return fail(OBN_ERR_UNSUPPORTED, "in_dim %d exceeds the kernels' limit", layer->in_dim);
   if (e != cudaSuccess) return cuda_fail(e, "ternary acc launch");
   return OBN_OK;
@@ -586,18 +594,16 @@ int forward_impl(const obn_bitlinear* layer, const float* x, int n, float* y, vo
     if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");
     const int order =
         (n == 1 ? obn::kOrderGemv : obn::kOrderGemm) | accumulate;  // bitlinear.rs:90-94
-    if (obn::gemm_supported(view(layer), n) && layer->gated) {
-      // the GEMM epilogue forms act(gate) * up itself
-      e = obn::launch_gemm(view(layer), q, sc, qs, n, y, nullptr,
-                           order | obn::kOutGated | (layer->act ? obn::kOutSilu : 0), s);
+    bool unsupported = false;
+    if (layer->gated && !gated_gemv_path(layer, n)) {
+      // the warp-MMA and GEMM epilogues form act(gate) * up themselves
+      e = run_matmul(layer, q, sc, qs, n, y, nullptr,
+                     order | obn::kOutGated | (layer->act ? obn::kOutSilu : 0), s, &unsupported);
       if (e != cudaSuccess) return cuda_fail(e, "ternary matmul launch");
       return OBN_OK;
     }
-    if (obn::gemm_supported(view(layer), n))
-      e = obn::launch_gemm(view(layer), q, sc, qs, n, ym, nullptr, order, s);
-    else if (layer->in_dim <= obn::kGemvMaxK)
-      e = obn::launch_gemv(view(layer), q, sc, qs, n, ym, nullptr, order, s);
-    else
+    e = run_matmul(layer, q, sc, qs, n, ym, nullptr, order, s, &unsupported);
+    if (unsupported)
       return fail(OBN_ERR_UNSUPPORTED, "in_dim %d exceeds the kernels' limit", layer->in_dim);
     if (e != cudaSuccess) return cuda_fail(e, "ternary matmul launch");
   }

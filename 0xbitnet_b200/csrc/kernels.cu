@@ -653,6 +653,8 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
   }
 }
 
+}  // namespace
+
 // Raises a kernel's dynamic shared memory limit once per (kernel, device) to the
 // largest size requested so far.
 struct SmemCfg {
@@ -677,6 +679,8 @@ cudaError_t ensure_smem(const void* fn, size_t bytes) {
   if (e == cudaSuccess && used < 256) table[used++] = SmemCfg{fn, dev, bytes};
   return e;
 }
+
+namespace {
 
 template <int NT, bool ACC>
 cudaError_t gemv_nt(const WeightView& W, const int8_t* q, const float* s_x, const int32_t* qsum,
@@ -961,10 +965,11 @@ cudaError_t read_and_clear_dev_error_kernels(uint32_t* out) {
 }
 
 cudaError_t read_and_clear_dev_error(uint32_t* out) {
-  uint32_t a = 0, b = 0;
+  uint32_t a = 0, b = 0, c = 0;
   cudaError_t e = read_and_clear_dev_error_kernels(&a);
   if (e == cudaSuccess) e = read_and_clear_dev_error_gemm(&b);
-  *out = a ? a : b;
+  if (e == cudaSuccess) e = read_and_clear_dev_error_mma(&c);
+  *out = a ? a : b ? b : c;
   return e;
 }
 

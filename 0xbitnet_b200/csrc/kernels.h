@@ -72,9 +72,24 @@ cudaError_t launch_bitlinear_n1(const WeightView& W, const float* gamma, float e
 // Largest K the GEMV kernels accept.
 constexpr int kGemvMaxK = 16384;
 
+// Batched decode on the warp-level int8 MMA (gemv_mma.cu) for 2..kMmaMaxTokens
+// tokens: y (kOrderGemm rounding; kOutAccumulate / kOutGated / kOutSilu as for
+// the GEMM) or, when acc != nullptr, exact int32 sums.
+constexpr int kMmaMaxTokens = 16;
+bool mma_gemv_supported(const WeightView& W, int n);
+cudaError_t launch_mma_gemv(const WeightView& W, const int8_t* q, const float* s_x,
+                            const int32_t* qsum, int n, float* y, int32_t* acc, int order,
+                            cudaStream_t s);
+
+// SM count of the current device (cached per device).
+int num_sms_cached();
+// Raises a kernel's dynamic shared memory limit (once per kernel and device).
+cudaError_t ensure_smem(const void* fn, size_t bytes);
+
 // Device error words (one per translation unit): read and reset.
 cudaError_t read_and_clear_dev_error_kernels(uint32_t* out);
 cudaError_t read_and_clear_dev_error_gemm(uint32_t* out);
+cudaError_t read_and_clear_dev_error_mma(uint32_t* out);
 cudaError_t read_and_clear_dev_error(uint32_t* out);
 
 }  // namespace obn

@@ -167,10 +167,9 @@ OBN_API int obn_bitlinear_forward_residual(const obn_bitlinear* layer, const flo
  * obn_bitlinear_forward takes as `workspace` lives instead in one fixed device
  * array of 1 MiB + 32 KiB that every device loading the library holds until the
  * process exits; the call allocates nothing. Limits: n * in_dim <= 1048576 and
- * n <= 4096, and obn_bitlinear_workspace_bytes(layer, n) <= 1 MiB + 32 KiB (this
- * only binds a gated layer on the dp4a GEMV path, 2-3 tokens, whose 4 * n *
- * 2 * out_dim bytes of gate|up outputs also live there); otherwise
- * OBN_ERR_UNSUPPORTED with a message naming the sizes.
+ * n <= 4096 (and obn_bitlinear_workspace_bytes(layer, n) <= 1 MiB + 32 KiB, which
+ * those two imply for every layer whose matmul runs on the tensor cores or the
+ * warp MMA); otherwise OBN_ERR_UNSUPPORTED with a message naming the sizes.
  * The first call on a device looks the array's device address up (once per
  * device, with that device current); make that first call before any stream
  * capture. The address is kept for the life of the process, so a device reset

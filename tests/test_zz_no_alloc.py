@@ -5,13 +5,11 @@ obn_bitlinear_forward_noalloc serves callers that cannot allocate device memory
 latency-critical threads that must not call cudaMalloc/cudaFree): it takes no
 workspace and keeps its scratch in one fixed device array inside the library.
 This file checks, through the C ABI, that two calls in a row give outputs
-identical to obn_bitlinear_forward's on every path that uses the scratch: the
-dp4a GEMV (3 tokens), the split-K tensor-core GEMM (8 and 64 tokens), and a
-gated gate|up layer both on the GEMV path (3 tokens: the interleaved gate|up
-rows go through the scratch before act(gate) * up) and on the GEMM path (8
-tokens: the epilogue forms act(gate) * up). It also checks that sizes beyond the
-fixed array are refused with a clear error, through both of the entry point's
-size checks.
+identical to obn_bitlinear_forward's on every matmul that reads quantized
+activations from the scratch: the warp-MMA decode kernel (3 and 8 tokens), the
+split-K tensor-core GEMM (64 tokens), and a gated gate|up layer on the warp-MMA
+path (3 and 8 tokens: the epilogue forms act(gate) * up). It also checks that
+sizes beyond the fixed array are refused with a clear error.
 
 The file name sorts last so a run that stops at the first failure has already
 run every other test.
@@ -81,18 +79,4 @@ def test_noalloc_rejects_activations_beyond_its_scratch():
     L = synth().layer(5, 256, K)
     layer = obn().BitLinear.from_i2s(L.blob(), K, 256)
     _refused(torch, layer, (1 << 20) // K + 1)  # one token more than the array holds
-    layer.close()
-
-
-def test_noalloc_rejects_gated_rows_beyond_its_scratch():
-    # A gated layer on the GEMV path (3 tokens) keeps 3 x 2 x out_dim f32 gate|up
-    # values in the scratch: 46000 features need 1.1 MB, more than the array holds,
-    # although 3 x 128 activation bytes are far inside the first limit.
-    torch = need_cuda()
-    M, K, n = 46000, 128, 3
-    g = synth().layer(61, M, K)
-    u = synth().layer(62, M, K)
-    layer = obn().BitLinear.from_i2s_gated(g.blob(), u.blob(), K, M)
-    assert layer.workspace_bytes(n) > (1 << 20) + (32 << 10)
-    _refused(torch, layer, n)
     layer.close()
