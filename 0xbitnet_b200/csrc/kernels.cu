@@ -108,14 +108,25 @@ OBN_DEVINL int block_sum_int_256(int v, int* sh) {
 
 OBN_DEVINL float norm_mul(float x, float rms, float g) { return __fmul_rn(__fmul_rn(x, rms), g); }
 
+// quantize.wgsl:67-72 for four values: q = clamp(round(y * inv), -127, 127) with
+// WGSL round() = round half to even. For |v| < 2^22, v + 1.5 * 2^23 rounded to
+// nearest-even leaves round(v) in the low mantissa bits, so the low byte of the
+// sum's bit pattern is q as an int8 and (bits - 0x4B400000) is q as an int. The
+// clamp never binds: |y| <= absmax and inv = 127 / absmax rounded give
+// |y * inv| <= 127 * (1 + 2^-23), which rounds to at most 127. (Finite inputs;
+// the magic addition runs on the FMA pipe instead of the quarter-rate conversion
+// unit.)
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr uint32_t kRoundMagicBits = 0x4B400000u;
+OBN_DEVINL uint32_t round_bits(float v) { return __float_as_uint(__fadd_rn(v, kRoundMagic)); }
+
 OBN_DEVINL uint32_t quant4(float4 y, float inv, int& sum) {
-  int a = min(127, max(-127, __float2int_rn(__fmul_rn(y.x, inv))));
-  int b = min(127, max(-127, __float2int_rn(__fmul_rn(y.y, inv))));
-  int c = min(127, max(-127, __float2int_rn(__fmul_rn(y.z, inv))));
-  int d = min(127, max(-127, __float2int_rn(__fmul_rn(y.w, inv))));
-  sum += a + b + c + d;
-  return (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
-         ((static_cast<uint32_t>(c) & 0xffu) << 16) | ((static_cast<uint32_t>(d) & 0xffu) << 24);
+  const uint32_t a = round_bits(__fmul_rn(y.x, inv));
+  const uint32_t b = round_bits(__fmul_rn(y.y, inv));
+  const uint32_t c = round_bits(__fmul_rn(y.z, inv));
+  const uint32_t d = round_bits(__fmul_rn(y.w, inv));
+  sum += static_cast<int>(a + b + c + d - 4u * kRoundMagicBits);
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
 // ---------------------------------------------------------------------------
@@ -263,7 +274,7 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant_reg(const float* __restri
   for (int j = 0; j < EPT; ++j) {
     const int col = tid + 256 * j;
     if (col < d) {
-      const int qi = min(127, max(-127, __float2int_rn(__fmul_rn(xv[j], inv))));
+      const int qi = static_cast<int>(round_bits(__fmul_rn(xv[j], inv)) - kRoundMagicBits);
       qr[col] = static_cast<int8_t>(qi);
       lsum += qi;
     }
@@ -284,6 +295,168 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant_reg(const float* __restri
 #pragma unroll
   for (int j = 0; j < EPT; ++j) xv[j] = xn[j];
   }
+}
+
+// Fused RMSNorm + quantize for many tokens (prefill): 64 threads (two warps) per
+// token, four tokens per 256-thread CTA, persistent over tokens.
+//
+// Thread l of a token loads the float4 at columns 4l + 256m (m = 0, 1, ...), so
+// it owns the four shader lanes L = 4l + e of rmsnorm.wgsl / quantize.wgsl
+// (lane L covers columns L + 256j) with their columns in the shader's order:
+// each fold of squares is local and bit-identical. The halving tree
+// (rmsnorm.wgsl:50-55) then needs one exchange: after the token's threads
+// publish their four partials, each of the two warps folds stride 128 (thread l
+// + 32) from shared memory and strides 64 .. 4 with shuffles (lane + 16 .. + 1,
+// the same pairings), strides 2 and 1 inside the lane. Barriers are named
+// 64-thread barriers per token (publish partials, publish the warps' max
+// |value|, publish the warps' code sums); the quantized row is stored 4 bytes
+// per column quad. gamma sits in shared memory, loaded once per CTA before the
+// PDL wait.
+constexpr int kTokThreads = 64;
+constexpr int kTokPerCta = 4;
+constexpr int kQuantFewTokens = 256;  // up to here one CTA per token
+
+OBN_DEVINL void named_bar(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Named barrier that also ORs a predicate over its `count` threads.
+OBN_DEVINL bool named_bar_or(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, o;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.or.pred o, %2, %3, p;\n\tselp.u32 %0, 1, 0, o;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
+template <int EPT4, bool NORM>
+__global__ __launch_bounds__(256) void k_rmsnorm_quant_t64(const float* __restrict__ x,
+                                                           const float* __restrict__ w, float eps,
+                                                           int d, int n, int8_t* __restrict__ q,
+                                                           float* __restrict__ scales,
+                                                           int32_t* __restrict__ qsum) {
+  // dynamic: the row buffer of each token slot [kTokPerCta][d], then gamma [d] (NORM)
+  extern __shared__ __align__(16) float dyn[];
+  __shared__ __align__(16) float4 part_s[kTokPerCta][kTokThreads];
+  __shared__ float max_s[kTokPerCta][2];
+  __shared__ int sum_s[kTokPerCta][2];
+  __shared__ __align__(8) uint64_t row_bar[kTokPerCta];
+  const int tid = threadIdx.x, slot = tid >> 6, l = tid & 63, lane = tid & 31, half = l >> 5;
+  const int bar_id = 1 + slot;
+  float* row_s = dyn + static_cast<size_t>(slot) * d;
+  const float* g_s = dyn + static_cast<size_t>(kTokPerCta) * d;
+  if (NORM)
+    for (int i = 4 * tid; i < d; i += 4 * 256)
+      *reinterpret_cast<float4*>(dyn + static_cast<size_t>(kTokPerCta) * d + i) =
+          *reinterpret_cast<const float4*>(w + i);
+  if (tid < kTokPerCta) mbar_init(&row_bar[tid], 1);
+  fence_mbar_init();
+  __syncthreads();
+  pdl_launch_dependents();
+  pdl_wait();  // x may be the previous kernel's output
+  const size_t stride = static_cast<size_t>(gridDim.x) * kTokPerCta;
+  const uint32_t row_bytes = static_cast<uint32_t>(d) * 4;
+  size_t t = static_cast<size_t>(blockIdx.x) * kTokPerCta + slot;
+  // the slot's first row; every later row is requested once the current one is in registers
+  if (l == 0 && t < static_cast<size_t>(n)) {
+    mbar_arrive_expect_tx(&row_bar[slot], row_bytes);
+    bulk_g2s(row_s, x + t * d, row_bytes, &row_bar[slot]);
+  }
+  uint32_t phase = 0;
+  bool failed = false;  // a row copy that never landed (recorded): the slot stops
+  for (; t < static_cast<size_t>(n); t += stride, phase ^= 1u) {
+    const bool got = mbar_wait(&row_bar[slot], phase);
+    float4 xv[EPT4];
+#pragma unroll
+    for (int m = 0; m < EPT4; ++m) {
+      const int c = 4 * l + 256 * m;
+      xv[m] = c < d ? *reinterpret_cast<const float4*>(row_s + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const size_t tn = t + stride;
+    auto request_next = [&] {  // after a slot barrier: every thread has its columns
+      if (l == 0 && tn < static_cast<size_t>(n)) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&row_bar[slot], row_bytes);
+        bulk_g2s(row_s, x + tn * d, row_bytes, &row_bar[slot]);
+      }
+    };
+    float rms = 1.0f;
+    if (NORM) {
+      float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;  // shader lanes 4l .. 4l + 3
+#pragma unroll
+      for (int m = 0; m < EPT4; ++m) {
+        if (4 * l + 256 * m < d) {
+          p0 = __fadd_rn(p0, __fmul_rn(xv[m].x, xv[m].x));
+          p1 = __fadd_rn(p1, __fmul_rn(xv[m].y, xv[m].y));
+          p2 = __fadd_rn(p2, __fmul_rn(xv[m].z, xv[m].z));
+          p3 = __fadd_rn(p3, __fmul_rn(xv[m].w, xv[m].w));
+        }
+      }
+      part_s[slot][l] = make_float4(p0, p1, p2, p3);
+      failed = named_bar_or(bar_id, kTokThreads, !got);  // the slot agrees on a timeout
+      if (failed) break;
+      request_next();
+      const float4 a = part_s[slot][lane], b = part_s[slot][lane + 32];  // stride 128
+      float v0 = __fadd_rn(a.x, b.x), v1 = __fadd_rn(a.y, b.y);
+      float v2 = __fadd_rn(a.z, b.z), v3 = __fadd_rn(a.w, b.w);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {  // strides 64 .. 4
+        v0 = __fadd_rn(v0, __shfl_down_sync(0xffffffffu, v0, o));
+        v1 = __fadd_rn(v1, __shfl_down_sync(0xffffffffu, v1, o));
+        v2 = __fadd_rn(v2, __shfl_down_sync(0xffffffffu, v2, o));
+        v3 = __fadd_rn(v3, __shfl_down_sync(0xffffffffu, v3, o));
+      }
+      const float total =
+          __shfl_sync(0xffffffffu, __fadd_rn(__fadd_rn(v0, v2), __fadd_rn(v1, v3)), 0);
+      rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(d)), eps)));
+    }
+    float lmax = 0.0f;
+#pragma unroll
+    for (int m = 0; m < EPT4; ++m) {
+      const int c = 4 * l + 256 * m;
+      if (c < d) {
+        if (NORM) {
+          const float4 g = *reinterpret_cast<const float4*>(g_s + c);
+          xv[m] = make_float4(norm_mul(xv[m].x, rms, g.x), norm_mul(xv[m].y, rms, g.y),
+                              norm_mul(xv[m].z, rms, g.z), norm_mul(xv[m].w, rms, g.w));
+        }
+        lmax = fmaxf(lmax, fmaxf(fmaxf(fabsf(xv[m].x), fabsf(xv[m].y)),
+                                 fmaxf(fabsf(xv[m].z), fabsf(xv[m].w))));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    if (lane == 0) max_s[slot][half] = lmax;
+    if (NORM) {
+      named_bar(bar_id, kTokThreads);
+    } else {
+      failed = named_bar_or(bar_id, kTokThreads, !got);
+      if (failed) break;
+      request_next();
+    }
+    const float absmax = fmaxf(max_s[slot][0], max_s[slot][1]);
+    const float inv = absmax == 0.0f ? 0.0f : __fdiv_rn(127.0f, absmax);
+    int lsum = 0;
+    uint32_t* qr = reinterpret_cast<uint32_t*>(q + t * d);
+#pragma unroll
+    for (int m = 0; m < EPT4; ++m) {
+      const int c = 4 * l + 256 * m;
+      if (c < d) qr[c >> 2] = quant4(xv[m], inv, lsum);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (lane == 0) sum_s[slot][half] = lsum;
+    named_bar(bar_id, kTokThreads);
+    if (l == 0) {
+      scales[t] = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
+      if (qsum) qsum[t] = sum_s[slot][0] + sum_s[slot][1];
+    }
+  }
+  // a slot that stopped early may still have a row copy in flight: wait for it (bounded)
+  if (l == 0 && failed) mbar_wait(&row_bar[slot], phase);
 }
 
 // rmsnorm.wgsl alone.
@@ -796,17 +969,51 @@ cudaError_t rmsnorm_quant_ept(const float* x, const float* norm_w, float eps, in
   return launch_pdl(kern, dim3(grid), dim3(256), 0, s, x, norm_w, eps, d, n, q, scales, qsum);
 }
 
+template <int EPT4>
+cudaError_t rmsnorm_quant_t64(const float* x, const float* norm_w, float eps, int n, int d,
+                              int8_t* q, float* scales, int32_t* qsum, cudaStream_t s) {
+  auto kern = norm_w ? k_rmsnorm_quant_t64<EPT4, true> : k_rmsnorm_quant_t64<EPT4, false>;
+  const size_t smem = sizeof(float) * static_cast<size_t>(d) * (kTokPerCta + (norm_w ? 1 : 0));
+  cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kern), smem);
+  if (e != cudaSuccess) return e;
+  // four tokens per CTA up to the resident capacity, then persistent CTAs
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, smem);
+  if (e != cudaSuccess) return e;
+  const int cap = (per_sm > 0 ? per_sm : 1) * num_sms_cached();
+  const int want = (n + kTokPerCta - 1) / kTokPerCta;
+  return launch_pdl(kern, dim3(want < cap ? want : cap), dim3(256), smem, s, x, norm_w, eps, d, n,
+                    q, scales, qsum);
+}
+
 cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps, int n, int d,
                                  int8_t* q, float* scales, int32_t* qsum, cudaStream_t s) {
+  // Few tokens (decode): one 256-thread CTA per token keeps each token's chain short.
   const int ept = (d + 255) / 256;
-  if (ept <= 2) return rmsnorm_quant_ept<2>(x, norm_w, eps, n, d, q, scales, qsum, s);
-  if (ept <= 4) return rmsnorm_quant_ept<4>(x, norm_w, eps, n, d, q, scales, qsum, s);
-  if (ept <= 8) return rmsnorm_quant_ept<8>(x, norm_w, eps, n, d, q, scales, qsum, s);
-  if (ept <= 12) return rmsnorm_quant_ept<12>(x, norm_w, eps, n, d, q, scales, qsum, s);
-  if (ept <= 16) return rmsnorm_quant_ept<16>(x, norm_w, eps, n, d, q, scales, qsum, s);
-  if (ept <= 24) return rmsnorm_quant_ept<24>(x, norm_w, eps, n, d, q, scales, qsum, s);
-  if (ept <= 28) return rmsnorm_quant_ept<28>(x, norm_w, eps, n, d, q, scales, qsum, s);
-  if (ept <= 36) return rmsnorm_quant_ept<36>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (n <= kQuantFewTokens) {
+    if (ept <= 2) return rmsnorm_quant_ept<2>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    if (ept <= 4) return rmsnorm_quant_ept<4>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    if (ept <= 8) return rmsnorm_quant_ept<8>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    if (ept <= 12) return rmsnorm_quant_ept<12>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    if (ept <= 16) return rmsnorm_quant_ept<16>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    if (ept <= 24) return rmsnorm_quant_ept<24>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    if (ept <= 28) return rmsnorm_quant_ept<28>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    if (ept <= 36) return rmsnorm_quant_ept<36>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  }
+  // Many tokens (prefill): 64 threads per token, packed 4-byte stores.
+  const int ept4 = ept;  // float4 column quads per thread
+  if (ept4 <= 1) return rmsnorm_quant_t64<1>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept4 <= 2) return rmsnorm_quant_t64<2>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept4 <= 4) return rmsnorm_quant_t64<4>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept4 <= 6) return rmsnorm_quant_t64<6>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept4 <= 8) return rmsnorm_quant_t64<8>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept4 <= 10) return rmsnorm_quant_t64<10>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept4 <= 12) return rmsnorm_quant_t64<12>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept4 <= 16) return rmsnorm_quant_t64<16>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept4 <= 20) return rmsnorm_quant_t64<20>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept4 <= 24) return rmsnorm_quant_t64<24>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept4 <= 28) return rmsnorm_quant_t64<28>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  if (ept4 <= 36) return rmsnorm_quant_t64<36>(x, norm_w, eps, n, d, q, scales, qsum, s);
   // larger rows: the three-pass kernel re-reads x instead of holding it in registers
   if (norm_w)
     return launch_pdl(k_rmsnorm_quant<true>, dim3(n), dim3(256), 0, s, x, norm_w, eps, d, q,

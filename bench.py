@@ -63,7 +63,7 @@ def parse_args():
                    help="config-4 tensor-parallel prefill tokens when run on N > 1 GPUs (0 skips)")
     p.add_argument("--case", type=str, default=None,
                    help="SHAPE:B — run a few forwards of one 2B shape (or of 'all' five in "
-                        "turn; or 'lmhead' / 'attn' / 'gateup') at B tokens and exit (a "
+                        "turn; or 'lmhead' / 'attn' / 'gateup' / 'quant') at B tokens and exit (a "
                         "small, self-contained workload for ncu captures)")
     return p.parse_args()
 
@@ -1048,6 +1048,16 @@ def run_case(spec: str):
         torch.cuda.synchronize()
         obn.check_device_errors()
         print(f"case lmhead B={B}: ok")
+        return
+    if name == "quant":  # fused RMSNorm + int8 quantize alone, B tokens at K = 2560 and 6912
+        for K in (2560, 6912):
+            x = torch.randn(B, K, device="cuda")
+            gamma = torch.ones(K, device="cuda")
+            for _ in range(3):
+                obn.rmsnorm_quantize(x, gamma)
+        torch.cuda.synchronize()
+        obn.check_device_errors()
+        print(f"case quant B={B}: ok")
         return
     if name == "attn":  # decode attention, 5 KV heads, context 2048, B sequences, 3 steps
         att = importlib.import_module("0xbitnet_b200.attention")
