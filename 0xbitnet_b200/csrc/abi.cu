@@ -589,6 +589,11 @@ int forward_impl(const obn_bitlinear* layer, const float* x, int n, float* y, vo
                                  layer->gated ? layer->act : -1);
     if (e != cudaSuccess) return cuda_fail(e, "bitlinear (n=1) launch");
     return OBN_OK;
+  } else if (obn::bitlinear_mma_supported(view(layer), n)) {  // few tokens, many rows: one kernel
+    e = obn::launch_bitlinear_mma(view(layer), layer->norm, layer->eps, x, n, y, accumulate,
+                                  layer->gated ? layer->act : -1, s);
+    if (e != cudaSuccess) return cuda_fail(e, "bitlinear (fused few-token) launch");
+    return OBN_OK;
   } else {
     e = obn::launch_rmsnorm_quant(x, layer->norm, layer->eps, n, layer->in_dim, q, sc, qs, s);
     if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_quantize launch");

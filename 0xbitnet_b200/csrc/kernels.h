@@ -77,6 +77,17 @@ constexpr int kGemvMaxK = 16384;
 // the GEMM) or, when acc != nullptr, exact int32 sums.
 constexpr int kMmaMaxTokens = 16;
 bool mma_gemv_supported(const WeightView& W, int n);
+// The whole forward (RMSNorm when gamma != null, quantize, matmul) in one launch
+// on the warp MMA for 2..kFusedMaxTokens tokens, in_dim <= kFusedMaxK and at
+// least kFusedMinRows weight rows; y as launch_bitlinear_n1 writes it
+// (accumulate: y +=; act >= 0: gated rows).
+constexpr int kFusedMaxK = 3072;
+constexpr int kFusedMaxTokens = 8;
+constexpr int kFusedMinRows = 8192;
+bool bitlinear_mma_supported(const WeightView& W, int n);
+cudaError_t launch_bitlinear_mma(const WeightView& W, const float* gamma, float eps,
+                                 const float* x, int n, float* y, int accumulate, int act,
+                                 cudaStream_t s);
 cudaError_t launch_mma_gemv(const WeightView& W, const int8_t* q, const float* s_x,
                             const int32_t* qsum, int n, float* y, int32_t* acc, int order,
                             cudaStream_t s);
