@@ -42,6 +42,7 @@ SIGNATURES = {
     "obn_bitlinear_workspace_bytes": (_SZ, [_P, _I]),
     "obn_bitlinear_forward": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "obn_bitlinear_forward_noalloc": (_I, [_P, _P, _I, _P, _P]),
+    "obn_measure_mma_rate": (_I, [_I, _I, _I, ctypes.POINTER(ctypes.c_double)]),
     "obn_bitlinear_forward_residual": (_I, [_P, _P, _I, _P, _P, _SZ, _P]),
     "obn_bitlinear_forward_tp": (_I, [_P, _P, _I, _P, _P, _I, _I, _I, _P, _SZ, _P]),
     "obn_lm_head_f16": (_I, [_P, _I, _I, _P, _P, _F, _I, _P, _P]),

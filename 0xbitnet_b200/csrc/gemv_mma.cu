@@ -3,14 +3,14 @@
 // Out[t, m] = f32(sum_k w[m,k] q[t,k]) * (s_w[m] * s_x[t])   (ternary_gemm.wgsl:132-133)
 //
 // Why mma.sync here and tcgen05 for prefill: on B200 one tcgen05.mma kind::i8
-// (M = 128, K = 32) costs a flat ~168 cycles for every N from 8 to 256
-// (measured: 64-MMA bursts per SM, one commit), so at decode batch sizes the
-// tensor-core path pays the full N = 256 price for 8..64 token columns and is
-// bound by its MMA count (rows * K / 4096 per layer). The warp-level
-// m16n8k32 u8 x s8 MMA sustains ~2000 MACs per cycle per SM with N = 8, so an
-// 8-token group costs 1/8 of a 64-token tcgen05 tile per MAC. The persistent
-// tcgen05 GEMMs (gemm.cu) stay the path from 17 tokens up: there each CTA's
-// per-block activation loads from L2 leave the warp-MMA form latency-bound.
+// (M = 128, K = 32) costs a near-flat ~102-106 cycles for every N from 8 to 128
+// (143 at N = 256; obn_measure_mma_rate, 64-MMA bursts on every SM, one commit),
+// so at decode widths the tensor-core path pays for columns it does not use:
+// 310 MACs per cycle per SM at N = 8, 1280 at N = 32, 2560 at N = 64. The
+// warp-level m16n8k32 u8 x s8 MMA sustains ~1850 MACs per cycle per SM with
+// N = 8, so it wins up to ~32 tokens; the tcgen05 GEMMs (gemm.cu) serve 17
+// tokens and up, where this kernel's per-block activation loads from L2 also
+// leave it latency-bound.
 //
 // Work split: like the single-token kernel, the layer's 16-row subtiles are
 // spread evenly over at most one CTA per SM (a contiguous run, one bulk copy of

@@ -63,7 +63,7 @@ def parse_args():
                    help="config-4 tensor-parallel prefill tokens when run on N > 1 GPUs (0 skips)")
     p.add_argument("--case", type=str, default=None,
                    help="SHAPE:B — run a few forwards of one 2B shape (or of 'all' five in "
-                        "turn; or 'lmhead' / 'attn' / 'gateup' / 'quant') at B tokens and exit (a "
+                        "turn; or 'lmhead' / 'attn' / 'gateup' / 'quant' / 'mmarate') at B tokens and exit (a "
                         "small, self-contained workload for ncu captures)")
     return p.parse_args()
 
@@ -939,9 +939,9 @@ def run_ours(args):
             ms = k0.elapsed_time(k1) / reps
             nl = args.layers * len(shp)
             kb = args.layers * sum(gemv_kernel_bytes(M, K, B) for _, (M, K) in shp)
-            # Every BitNet-2B shape has < 74 row tiles, so from 4 tokens up the
-            # library takes the split-K cluster GEMM (launch list in profiles/).
-            name = ("k_gemv (dp4a, B=%d)" % B) if B < 4 else (
+            # 2..16 tokens: the warp-MMA decode kernel; from 17 tokens every
+            # BitNet-2B shape (< 74 row tiles) takes the split-K cluster GEMM.
+            name = ("k_mma_gemv (mma.sync m16n8k32 u8 x s8, B=%d)" % B) if B <= 16 else (
                 "k_gemm_sk (tcgen05 kind::i8, split-K over clusters, B=%d)" % B)
             kernels[B] = {"kernel": name, "bound": "hbm", "us": ms * 1e3 / nl, "bytes": kb / nl,
                           "step_share_ms": ms}
@@ -1048,6 +1048,22 @@ def run_case(spec: str):
         torch.cuda.synchronize()
         obn.check_device_errors()
         print(f"case lmhead B={B}: ok")
+        return
+    if name == "mmarate":  # MACs per cycle per SM of the integer MMA forms (B = MMAs per burst)
+        import ctypes
+        L = obn.lib()
+        out = {}
+        for form, label in ((0, "tcgen05 kind::i8 A=TMEM"), (1, "tcgen05 kind::i8 A=smem")):
+            for N in (8, 16, 32, 64, 128, 256):
+                r = ctypes.c_double()
+                obn._lib.check(L.obn_measure_mma_rate(form, N, B, ctypes.byref(r)))
+                out[f"{label} N={N}"] = r.value
+        for form, label in ((2, "mma.sync m16n8k32 u8.s8"), (3, "dp4a")):
+            r = ctypes.c_double()
+            obn._lib.check(L.obn_measure_mma_rate(form, 8, 4 * B, ctypes.byref(r)))
+            out[label] = r.value
+        print(json.dumps({"case": "mmarate", "ops_per_burst": B,
+                          "macs_per_cycle_per_sm": {k: round(v, 1) for k, v in out.items()}}))
         return
     if name == "quant":  # fused RMSNorm + int8 quantize alone, B tokens at K = 2560 and 6912
         for K in (2560, 6912):

@@ -329,6 +329,16 @@ OBN_API int obn_bitlinear_export_i2s(const obn_bitlinear* layer, uint8_t* dst_de
  * the current device. */
 OBN_API int obn_check_device_errors(void);
 
+/* ---- measurement --------------------------------------------------------------
+ * No counterpart in the reference. Multiply-accumulate rate of one integer MMA form,
+ * as MACs per cycle per SM (one CTA per SM, back-to-back operations, slowest SM):
+ * form 0 tcgen05.mma kind::i8 (M = 128, K = 32, A in tensor memory, N = n),
+ * form 1 the same with A in shared memory, form 2 mma.sync m16n8k32 u8 x s8,
+ * form 3 dp4a. `count` operations per issuing thread (1 .. 65536). The numbers
+ * decide which kernel serves which token count (a flat tcgen05 cost per MMA up to
+ * N = 256 favours the warp MMA at decode widths). Synchronises the device. */
+OBN_API int obn_measure_mma_rate(int form, int n, int count, double* macs_per_cycle_per_sm);
+
 #ifdef __cplusplus
 }
 #endif
