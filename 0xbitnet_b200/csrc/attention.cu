@@ -60,7 +60,8 @@ __global__ __launch_bounds__(256) void k_rope_kv_append(const float* __restrict_
                                                         float* __restrict__ q_out,
                                                         __half* __restrict__ k_cache,
                                                         __half* __restrict__ v_cache, int S_max) {
-  pdl_launch_dependents();
+  // No early launch of dependents: the cache rows written here are complete
+  // before any later kernel starts (the decode pass reads older rows early).
   pdl_wait();
   const size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= total) return;
@@ -116,6 +117,21 @@ OBN_DEVINL float warp_sum(float v) {
   return v;
 }
 
+// Where a kernel lets its dependents launch. Passes that append to the cache
+// (APPENDS) do it only after their own wait: a kernel that is still waiting then
+// proves every kernel before the latest appending pass complete, which is what
+// lets the clustered decode pass read older cache rows before its wait.
+template <bool APPENDS>
+OBN_DEVINL void pdl_order() {
+  if constexpr (APPENDS) {
+    pdl_wait();
+    pdl_launch_dependents();
+  } else {
+    pdl_launch_dependents();
+    pdl_wait();
+  }
+}
+
 // Partials layout (workspace): for row r, head h, split c:
 //   acc[((r * H + h) * nsplit + c) * D + dim], then m[...] and l[...] after all acc.
 // ROPE (decode, n = 1): q is the merged QKV row instead of rotated q; the CTA
@@ -136,8 +152,7 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split(
   float* sQ = reinterpret_cast<float*>(sV + kAttnChunk * D);          // [D][G]
   float* sP = sQ + G * D;                                             // [chunk keys][G]
   __shared__ float red[G][kAttnThreads / 32];
-  pdl_launch_dependents();
-  pdl_wait();
+  pdl_order<ROPE>();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int c = blockIdx.x, kvh = blockIdx.y;
   const size_t r = blockIdx.z;  // query row b * n + t
@@ -365,6 +380,120 @@ OBN_DEVINL void split_h2(float x0, float x1, uint32_t* hi, uint32_t* lo) {
 
 constexpr int kVStride = kAttnHeadDim + 8;  // halves per smem V row (ldmatrix.trans, no conflicts)
 
+// The tensor-core contractions of one chunk, shared by the split pass and the
+// clustered decode pass. On entry sK / sV hold the chunk's keys and values
+// (rows >= cnt zero) and sQ the group's rotated q [G][D] (f32, visible to the
+// CTA). SPLIT_WAIT: K and V are still two cp.async groups in flight, K first;
+// otherwise every copy has landed. On exit o holds this thread's P.V fragments
+// (dims 32 warp + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1) and red_m / red_l
+// every warp's max and sum per head.
+template <int G, bool SPLIT_WAIT>
+OBN_DEVINL void tc_chunk(const __half* sK, const __half* sV, const float* sQ, float* sP, int cnt,
+                         float scale, float (*red_m)[4], float (*red_l)[4], float (&o)[2][4]) {
+  constexpr int D = kAttnHeadDim;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int grp = lane >> 2, qd = lane & 3;
+  // B fragments of q (column = head grp, rows = dims), split hi / lo.
+  uint32_t qh[8][2], ql[8][2];
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    if (grp < G) {
+      const float* qc = sQ + grp * D + ks * 16 + 2 * qd;
+      split_h2(qc[0], qc[1], &qh[ks][0], &ql[ks][0]);
+      split_h2(qc[8], qc[9], &qh[ks][1], &ql[ks][1]);
+    } else {  // padding columns
+      qh[ks][0] = qh[ks][1] = ql[ks][0] = ql[ks][1] = 0u;
+    }
+  }
+  if constexpr (SPLIT_WAIT) cp_async_wait_group<1>();  // K landed
+  __syncthreads();
+  // Scores: warp w, keys 32w + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1.
+  float sc[2][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sc[mt][i] = 0.0f;
+    const int krow = 32 * warp + 16 * mt + (lane & 15);
+    const uint32_t abase = smem_u32(sK + krow * kKStride + ((lane >> 4) << 3));
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(abase + ks * 32, a);
+      mma_16816(sc[mt], a, qh[ks][0], qh[ks][1]);
+      mma_16816(sc[mt], a, ql[ks][0], ql[ks][1]);
+    }
+  }
+  // Scale, causal validity, per-head max over the chunk.
+  float mx[2] = {-FLT_MAX, -FLT_MAX};
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int key = 32 * warp + 16 * mt + grp + (i >= 2 ? 8 : 0);
+      sc[mt][i] = key < cnt ? __fmul_rn(sc[mt][i], scale) : -FLT_MAX;
+      mx[i & 1] = fmaxf(mx[i & 1], sc[mt][i]);
+    }
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int sft = 4; sft <= 16; sft <<= 1) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], sft));
+  if (grp == 0) {
+    red_m[2 * qd][warp] = mx[0];
+    red_m[2 * qd + 1][warp] = mx[1];
+  }
+  __syncthreads();
+  float mg[2], ls[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    mg[h] = fmaxf(fmaxf(red_m[2 * qd + h][0], red_m[2 * qd + h][1]),
+                  fmaxf(red_m[2 * qd + h][2], red_m[2 * qd + h][3]));
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int key = 32 * warp + 16 * mt + grp + (i >= 2 ? 8 : 0);
+      const int h = i & 1;
+      const float pv = key < cnt ? expf(sc[mt][i] - mg[h]) : 0.0f;
+      ls[h] += pv;
+      if (2 * qd + h < G) sP[key * G + 2 * qd + h] = pv;
+    }
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int sft = 4; sft <= 16; sft <<= 1) ls[h] += __shfl_xor_sync(0xffffffffu, ls[h], sft);
+  if (grp == 0) {
+    red_l[2 * qd][warp] = ls[0];
+    red_l[2 * qd + 1][warp] = ls[1];
+  }
+  if constexpr (SPLIT_WAIT) cp_async_wait_group<0>();  // V landed
+  __syncthreads();
+  // P.V: warp w, dims 32w + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1.
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[mt][i] = 0.0f;
+  // ldmatrix.trans row addresses: lanes 0-7 keys 0-7 / dims d0.., 8-15 keys 0-7 / dims
+  // d0 + 8.., 16-23 keys 8-15 / d0.., 24-31 keys 8-15 / d0 + 8..
+  const int vkey = (lane & 7) + ((lane >> 4) << 3);
+  const int vdim = ((lane >> 3) & 1) << 3;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    uint32_t ph0 = 0u, pl0 = 0u, ph1 = 0u, pl1 = 0u;
+    if (grp < G) {
+      const float* pc = sP + (ks * 16 + 2 * qd) * G + grp;
+      split_h2(pc[0], pc[G], &ph0, &pl0);          // keys 2qd, 2qd + 1
+      split_h2(pc[8 * G], pc[9 * G], &ph1, &pl1);  // keys 2qd + 8, 2qd + 9
+    }
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt) {
+      uint32_t a[4];
+      ldsm_x4_t(smem_u32(sV + (ks * 16 + vkey) * kVStride + 32 * warp + 16 * mt + vdim), a);
+      mma_16816(o[mt], a, ph0, ph1);
+      mma_16816(o[mt], a, pl0, pl1);
+    }
+  }
+}
+
 template <int G, bool ROPE = false>
 __global__ __launch_bounds__(kAttnThreads) void k_attn_split_tc(
     const float* __restrict__ q, const __half* __restrict__ k_cache,
@@ -380,8 +509,7 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split_tc(
   float* sQ = reinterpret_cast<float*>(sV + C * kVStride);      // [G][D] rotated q (f32)
   float* sP = sQ + G * D;                                       // [C][G] probabilities
   __shared__ float red_m[8][4], red_l[8][4];
-  pdl_launch_dependents();
-  pdl_wait();
+  pdl_order<ROPE>();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int grp = lane >> 2, qd = lane & 3;  // MMA fragment coordinates
   const int c = blockIdx.x, kvh = blockIdx.y;
@@ -468,106 +596,8 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split_tc(
       sQ[e] = q[(r * H + static_cast<size_t>(kvh) * G) * D + e];
   }
   __syncthreads();
-  // B fragments of q (column = head grp, rows = dims), split hi / lo.
-  uint32_t qh[8][2], ql[8][2];
-#pragma unroll
-  for (int ks = 0; ks < 8; ++ks) {
-    if (grp < G) {
-      const float* qc = sQ + grp * D + ks * 16 + 2 * qd;
-      split_h2(qc[0], qc[1], &qh[ks][0], &ql[ks][0]);
-      split_h2(qc[8], qc[9], &qh[ks][1], &ql[ks][1]);
-    } else {  // padding columns
-      qh[ks][0] = qh[ks][1] = ql[ks][0] = ql[ks][1] = 0u;
-    }
-  }
-  cp_async_wait_group<1>();  // K landed
-  __syncthreads();
-  // Scores: warp w, keys 32w + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1.
-  float sc[2][4];
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) sc[mt][i] = 0.0f;
-    const int krow = 32 * warp + 16 * mt + (lane & 15);
-    const uint32_t abase = smem_u32(sK + krow * kKStride + ((lane >> 4) << 3));
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      uint32_t a[4];
-      ldsm_x4(abase + ks * 32, a);
-      mma_16816(sc[mt], a, qh[ks][0], qh[ks][1]);
-      mma_16816(sc[mt], a, ql[ks][0], ql[ks][1]);
-    }
-  }
-  // Scale, causal validity, per-head max over the chunk.
-  float mx[2] = {-FLT_MAX, -FLT_MAX};
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int key = 32 * warp + 16 * mt + grp + (i >= 2 ? 8 : 0);
-      sc[mt][i] = key < cnt ? __fmul_rn(sc[mt][i], scale) : -FLT_MAX;
-      mx[i & 1] = fmaxf(mx[i & 1], sc[mt][i]);
-    }
-#pragma unroll
-  for (int h = 0; h < 2; ++h)
-#pragma unroll
-    for (int sft = 4; sft <= 16; sft <<= 1) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], sft));
-  if (grp == 0) {
-    red_m[2 * qd][warp] = mx[0];
-    red_m[2 * qd + 1][warp] = mx[1];
-  }
-  __syncthreads();
-  float mg[2], ls[2] = {0.0f, 0.0f};
-#pragma unroll
-  for (int h = 0; h < 2; ++h)
-    mg[h] = fmaxf(fmaxf(red_m[2 * qd + h][0], red_m[2 * qd + h][1]),
-                  fmaxf(red_m[2 * qd + h][2], red_m[2 * qd + h][3]));
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int key = 32 * warp + 16 * mt + grp + (i >= 2 ? 8 : 0);
-      const int h = i & 1;
-      const float pv = key < cnt ? expf(sc[mt][i] - mg[h]) : 0.0f;
-      ls[h] += pv;
-      if (2 * qd + h < G) sP[key * G + 2 * qd + h] = pv;
-    }
-#pragma unroll
-  for (int h = 0; h < 2; ++h)
-#pragma unroll
-    for (int sft = 4; sft <= 16; sft <<= 1) ls[h] += __shfl_xor_sync(0xffffffffu, ls[h], sft);
-  if (grp == 0) {
-    red_l[2 * qd][warp] = ls[0];
-    red_l[2 * qd + 1][warp] = ls[1];
-  }
-  cp_async_wait_group<0>();  // V landed
-  __syncthreads();
-  // P.V: warp w, dims 32w + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1.
   float o[2][4];
-#pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) o[mt][i] = 0.0f;
-  // ldmatrix.trans row addresses: lanes 0-7 keys 0-7 / dims d0.., 8-15 keys 0-7 / dims
-  // d0 + 8.., 16-23 keys 8-15 / d0.., 24-31 keys 8-15 / d0 + 8..
-  const int vkey = (lane & 7) + ((lane >> 4) << 3);
-  const int vdim = ((lane >> 3) & 1) << 3;
-#pragma unroll
-  for (int ks = 0; ks < 8; ++ks) {
-    uint32_t ph0 = 0u, pl0 = 0u, ph1 = 0u, pl1 = 0u;
-    if (grp < G) {
-      const float* pc = sP + (ks * 16 + 2 * qd) * G + grp;
-      split_h2(pc[0], pc[G], &ph0, &pl0);          // keys 2qd, 2qd + 1
-      split_h2(pc[8 * G], pc[9 * G], &ph1, &pl1);  // keys 2qd + 8, 2qd + 9
-    }
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-      uint32_t a[4];
-      ldsm_x4_t(smem_u32(sV + (ks * 16 + vkey) * kVStride + 32 * warp + 16 * mt + vdim), a);
-      mma_16816(o[mt], a, ph0, ph1);
-      mma_16816(o[mt], a, pl0, pl1);
-    }
-  }
+  tc_chunk<G, true>(sK, sV, sQ, sP, cnt, scale, red_m, red_l, o);
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -582,6 +612,214 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split_tc(
     part_l[pbase + static_cast<size_t>(tid) * nsplit] =
         (red_l[tid][0] + red_l[tid][1]) + (red_l[tid][2] + red_l[tid][3]);
   }
+}
+
+// ---- clustered decode pass ---------------------------------------------------
+// One decode token per sequence (n = 1) with RoPE, the cache append, the split
+// pass and the combine in ONE launch: a cluster of CS CTAs per (sequence, KV
+// head). CTA `rank` takes the chunks rank, rank + CS, ... (up to kClMaxSlots),
+// runs tc_chunk on each and keeps every chunk's partial (max, sum, unnormalised
+// P.V) in its own shared memory. After a cluster barrier each CTA gathers its
+// G * D / CS outputs' partials from all CTAs over distributed shared memory and
+// combines them with k_attn_combine's arithmetic in the same chunk order, so the
+// result equals the split + combine passes bit for bit.
+//
+// The chunk of the first slot is copied before griddepcontrol.wait, while the
+// QKV projection before this kernel still runs: its rows below pos - 1 were
+// appended by earlier steps. Appending passes (this one, the RoPE append, the
+// RoPE split) let their dependents launch only after their own wait or at their
+// end, so while this kernel waits every kernel before the latest appending pass
+// has completed; the one row that pass may still be writing is pos - 1 in a
+// decode sequence (or a row at or above pos when the caller went back), and row
+// pos - 1 is copied after the wait. The device position (*pos_dev) is written by
+// stream-ordered copies, never by a kernel of this library.
+constexpr int kClMaxSlots = 4;  // chunks per CTA
+constexpr int kClMaxChunks = 64;
+
+OBN_DEVINL uint32_t cl_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+OBN_DEVINL float cl_ld(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+OBN_DEVINL void cl_sync_publish() {  // this CTA's shared-memory writes -> the cluster
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+OBN_DEVINL void cl_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+OBN_DEVINL void cl_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+inline size_t cl_smem_bytes(int G, int slots) {
+  return static_cast<size_t>(kAttnChunk) * kKStride * 2 + static_cast<size_t>(kAttnChunk) * kVStride * 2 +
+         static_cast<size_t>(G) * kAttnHeadDim * 4 + static_cast<size_t>(kAttnChunk) * G * 4 +
+         static_cast<size_t>(slots) * G * (kAttnHeadDim + 2) * 4;
+}
+
+template <int G>
+__global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
+    const float* __restrict__ qkv, __half* __restrict__ k_cache, __half* __restrict__ v_cache,
+    int H, int Hkv, int S_max, int pos, const int* __restrict__ pos_dev, float scale, int nsplit,
+    int slots, float* __restrict__ out, float theta_base) {
+  constexpr int D = kAttnHeadDim;
+  constexpr int C = kAttnChunk;
+  static_assert(C == 128 && D == 128 && kAttnThreads == 128 && G <= 8, "tile shape");
+  extern __shared__ __align__(16) unsigned char smem[];
+  __half* sK = reinterpret_cast<__half*>(smem);             // [C][kKStride]
+  __half* sV = sK + C * kKStride;                           // [C][kVStride]
+  float* sQ = reinterpret_cast<float*>(sV + C * kVStride);  // [G][D] rotated q
+  float* sP = sQ + G * D;                                   // [C][G] probabilities
+  float* sAcc = sP + C * G;                                 // [slots][G][D] partial P.V
+  float* sM = sAcc + slots * G * D;                         // [slots][G] partial max
+  float* sL = sM + slots * G;                               // [slots][G] partial sum
+  __shared__ float red_m[8][4], red_l[8][4];
+  const int tid = threadIdx.x;
+  const int CS = static_cast<int>(gridDim.x);  // the cluster spans the grid's x
+  const int rank = static_cast<int>(blockIdx.x);
+  const int kvh = blockIdx.y;
+  const size_t b = blockIdx.z;
+  const int p_new = pos_dev ? *pos_dev : pos;
+  const int seq_len = min(p_new + 1, S_max);
+  const int nvalid = min(nsplit, (seq_len + C - 1) / C);  // chunks that hold keys
+  const int late = p_new - 1;  // first row copied after the wait
+
+  // Rows [0, cnt) of the chunk at s0 whose position is below `upto` (async
+  // copies), rows >= cnt zero, the new token's row left for the append.
+  auto copy_chunk = [&](int s0, int cnt, int from, int upto) {
+#pragma unroll 4
+    for (int e = tid; e < C * (D / 8); e += kAttnThreads) {
+      const int key = e / (D / 8), part = e % (D / 8);
+      __half* dk = sK + key * kKStride + part * 8;
+      __half* dv = sV + key * kVStride + part * 8;
+      const int p = s0 + key;
+      if (key >= cnt) {
+        if (from == 0) {
+          *reinterpret_cast<uint4*>(dk) = make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(dv) = make_uint4(0u, 0u, 0u, 0u);
+        }
+      } else if (p >= from && p < upto && p != p_new) {
+        const size_t g = ((b * S_max + p) * Hkv + kvh) * D + part * 8;
+        cp_async16(dk, k_cache + g);
+        cp_async16(dv, v_cache + g);
+      }
+    }
+    cp_async_commit();
+  };
+  // The new token's rotated key and value: into the caches and the chunk's tiles.
+  const float* qrow = qkv + b * static_cast<size_t>(H + 2 * Hkv) * D;
+  auto append_new = [&](int s0) {
+    if (p_new < 0 || p_new >= S_max || p_new < s0 || p_new >= s0 + C) return;
+    const int row = p_new - s0;
+    const size_t cache_off = ((b * S_max + p_new) * Hkv + kvh) * D;
+    if (tid < D / 2) {
+      const float* src = qrow + (static_cast<size_t>(H) + kvh) * D + 2 * tid;
+      float y0, y1;
+      rope_pair(src[0], src[1], tid, D, p_new, theta_base, &y0, &y1);
+      const __half2 h = __floats2half2_rn(y0, y1);
+      *reinterpret_cast<__half2*>(k_cache + cache_off + 2 * tid) = h;
+      *reinterpret_cast<__half2*>(sK + row * kKStride + 2 * tid) = h;
+    } else {
+      const int i = tid - D / 2;
+      const float* src = qrow + (static_cast<size_t>(H) + Hkv + kvh) * D + 2 * i;
+      const __half2 h = __floats2half2_rn(src[0], src[1]);
+      *reinterpret_cast<__half2*>(v_cache + cache_off + 2 * i) = h;
+      *reinterpret_cast<__half2*>(sV + row * kVStride + 2 * i) = h;
+    }
+  };
+  // This thread's partial of one chunk -> slot `slot` (after tc_chunk).
+  auto keep_partial = [&](int slot, const float (&o)[2][4]) {
+    const int lane = tid & 31, warp = tid >> 5, grp = lane >> 2, qd = lane & 3;
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int dim = 32 * warp + 16 * mt + grp + (i >= 2 ? 8 : 0);
+        const int h = 2 * qd + (i & 1);
+        if (h < G) sAcc[(slot * G + h) * D + dim] = o[mt][i];
+      }
+    if (tid < G) {
+      sM[slot * G + tid] =
+          fmaxf(fmaxf(red_m[tid][0], red_m[tid][1]), fmaxf(red_m[tid][2], red_m[tid][3]));
+      sL[slot * G + tid] = (red_l[tid][0] + red_l[tid][1]) + (red_l[tid][2] + red_l[tid][3]);
+    }
+  };
+
+  // ---- before the wait: the first slot's older rows
+  const int s00 = rank * C;
+  const int cnt0 = min(C, seq_len - s00);
+  if (rank < nvalid) copy_chunk(s00, cnt0, 0, late);
+  pdl_wait();
+  pdl_launch_dependents();
+
+  // ---- after the wait: q, the late rows, the new row, then every slot
+  for (int e = tid; e < G * (D / 2); e += kAttnThreads) {
+    const int g = e / (D / 2), i = e % (D / 2);
+    const float* src = qrow + (static_cast<size_t>(kvh) * G + g) * D + 2 * i;
+    float y0, y1;
+    rope_pair(src[0], src[1], i, D, p_new, theta_base, &y0, &y1);
+    sQ[g * D + 2 * i] = y0;
+    sQ[g * D + 2 * i + 1] = y1;
+  }
+  for (int slot = 0; slot < slots; ++slot) {
+    const int c = rank + slot * CS;
+    if (c >= nvalid) break;  // uniform per CTA
+    const int s0 = c * C;
+    const int cnt = min(C, seq_len - s0);
+    if (slot == 0) {
+      copy_chunk(s0, cnt, max(late, 0), 0x7fffffff);  // rows pos - 1 and up
+    } else {
+      __syncthreads();  // the previous slot is done with the tiles
+      copy_chunk(s0, cnt, 0, 0x7fffffff);
+    }
+    append_new(s0);
+    cp_async_wait_group<0>();
+    __syncthreads();
+    float o[2][4];
+    tc_chunk<G, false>(sK, sV, sQ, sP, cnt, scale, red_m, red_l, o);
+    keep_partial(slot, o);
+  }
+
+  // ---- combine over the cluster: this CTA's outputs [rank * per, rank * per + per)
+  cl_sync_publish();
+  const int per = G * D / CS;
+  float* gAcc = reinterpret_cast<float*>(sK);  // [nvalid][per], the tiles are free now
+  float* gM = reinterpret_cast<float*>(sV);    // [nvalid][G]
+  float* gL = gM + kClMaxChunks * G;
+  const uint32_t acc_base = smem_u32(sAcc) + static_cast<uint32_t>(rank * per) * 4u;
+  for (int e = tid; e < nvalid * per; e += kAttnThreads) {
+    const int c = e / per, j = e - c * per;
+    const uint32_t a = acc_base + static_cast<uint32_t>(((c / CS) * G * D + j) * 4);
+    gAcc[e] = cl_ld(cl_map(a, static_cast<uint32_t>(c % CS)));
+  }
+  for (int e = tid; e < nvalid * G; e += kAttnThreads) {
+    const int c = e / G, g = e - c * G;
+    const uint32_t off = static_cast<uint32_t>(((c / CS) * G + g) * 4);
+    gM[e] = cl_ld(cl_map(smem_u32(sM) + off, static_cast<uint32_t>(c % CS)));
+    gL[e] = cl_ld(cl_map(smem_u32(sL) + off, static_cast<uint32_t>(c % CS)));
+  }
+  __syncthreads();
+  cl_arrive_relaxed();  // done reading the other CTAs' shared memory
+  if (tid < per) {
+    const int oi = rank * per + tid;
+    const int g = oi / D, dim = oi - g * D;
+    float M = -FLT_MAX;
+    for (int c = 0; c < nvalid; ++c) M = fmaxf(M, gM[c * G + g]);
+    float L = 0.0f, o = 0.0f;
+    for (int c = 0; c < nvalid; ++c) {
+      const float l = gL[c * G + g];
+      if (l == 0.0f) continue;  // an empty chunk
+      const float w = expf(gM[c * G + g] - M);
+      L = fmaf(w, l, L);
+      o = fmaf(w, gAcc[c * per + tid], o);
+    }
+    out[((b * H) + static_cast<size_t>(kvh) * G + g) * D + dim] = o / L;
+  }
+  cl_wait();  // keep this CTA's partials alive until every CTA has read them
 }
 
 // One CTA per (query row, head): thread = dimension.
@@ -684,6 +922,75 @@ cudaError_t launch_pdl_attn(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaS
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
+// Cluster size of the clustered decode pass for group size G on the current
+// device: 16 when a 16-CTA cluster with the largest shared memory it uses can be
+// resident, else 8 when an 8-CTA one can, else 0 (the split + combine passes).
+// OBN_ATTN_CLUSTER=0 selects 0. Queried once per device.
+template <int G>
+int decode_cluster_size() {
+  static const bool enabled = [] {
+    const char* v = std::getenv("OBN_ATTN_CLUSTER");
+    return !(v && v[0] == '0');
+  }();
+  static int cache[64] = {};  // 0 not queried, -1 none, else the size
+  if (!enabled) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (cache[dev]) return cache[dev] > 0 ? cache[dev] : 0;
+  auto kern = k_attn_decode_cl<G>;
+  const size_t smem = cl_smem_bytes(G, kClMaxSlots);
+  int best = -1;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) == cudaSuccess &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+          cudaSuccess) {
+    for (int cs : {16, 8}) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(cs, 1, 1);
+      cfg.blockDim = dim3(kAttnThreads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = cs;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int count = 0;
+      if (cudaOccupancyMaxActiveClusters(&count, kern, &cfg) == cudaSuccess && count > 0) {
+        best = cs;
+        break;
+      }
+    }
+  }
+  cudaGetLastError();  // a refused query only selects the split + combine passes
+  cache[dev] = best;
+  return best > 0 ? best : 0;
+}
+
+template <int G>
+cudaError_t launch_decode_cl(const float* qkv, __half* k_cache, __half* v_cache, int B, int H,
+                             int Hkv, int S_max, int pos, const int* pos_dev, float scale,
+                             int nsplit, int CS, float* out, cudaStream_t s, float theta_base) {
+  const int slots = (nsplit + CS - 1) / CS;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CS, Hkv, B);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = cl_smem_bytes(G, slots);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = CS;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, k_attn_decode_cl<G>, qkv, k_cache, v_cache, H, Hkv, S_max, pos,
+                            pos_dev, scale, nsplit, slots, out, theta_base);
+}
+
 }  // namespace
 
 cudaError_t launch_rope_kv_append(const float* qkv, int B, int n, int H, int Hkv, int d, int pos,
@@ -716,6 +1023,24 @@ cudaError_t attention_impl(const float* q, const __half* k_cache, const __half* 
   float* pm = pa + rows * d;
   float* pl = pm + rows;
   const int G = H / Hkv;
+  if (rope) {  // one clustered launch when the chunks fit the cluster's slots
+#define OBN_CL(GG)                                                                              \
+  {                                                                                             \
+    const int cs = decode_cluster_size<GG>();                                                   \
+    if (cs > 0 && nsplit <= cs * kClMaxSlots)                                                   \
+      return launch_decode_cl<GG>(q, const_cast<__half*>(k_cache), const_cast<__half*>(v_cache), \
+                                  B, H, Hkv, S_max, seq_len - 1, pos_dev, scale, nsplit, cs, out, \
+                                  s, theta_base);                                               \
+  }
+    switch (G) {
+      case 1: OBN_CL(1) break;
+      case 2: OBN_CL(2) break;
+      case 4: OBN_CL(4) break;
+      case 8: OBN_CL(8) break;
+      default: return cudaErrorInvalidValue;
+    }
+#undef OBN_CL
+  }
   cudaError_t e;
 #define OBN_SPLIT(GG)                                                                           \
   (rope ? launch_split<GG, true>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev,  \

@@ -253,7 +253,10 @@ __global__ __launch_bounds__(kMmaWarps * 32) void k_mma_gemv(
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool geom_ok = ns >= 1 && ns <= wslots && wslots <= NSUB && n >= 1 && n <= NTOK;
   if (tid == 0 && !geom_ok) record_error(DEVERR_BAD_LAUNCH);
-  if (!geom_ok) return;  // uniform per CTA
+  if (!geom_ok) {  // uniform per CTA; still ordered after the preceding grid
+    pdl_wait();
+    return;
+  }
   uint8_t* w_s = smem;
   int32_t* red = reinterpret_cast<int32_t*>(smem + static_cast<size_t>(wslots) * KB * kSubtileBytes);
   const int m0 = s0 * kSubRows;
@@ -312,7 +315,10 @@ __global__ __launch_bounds__(kMmaWarps * 32) void k_bitlinear_mma(
   const bool geom_ok = ns >= 1 && ns <= wslots && wslots <= NSUB && n >= 1 && n <= NTOK &&
                        K <= EPT4 * 128;
   if (tid == 0 && !geom_ok) record_error(DEVERR_BAD_LAUNCH);
-  if (!geom_ok) return;  // uniform per CTA
+  if (!geom_ok) {  // uniform per CTA; still ordered after the preceding grid
+    pdl_wait();
+    return;
+  }
   const int ldq = K + 16;  // padded int8 rows
   uint8_t* w_s = smem;
   int32_t* red = reinterpret_cast<int32_t*>(smem + static_cast<size_t>(wslots) * KB * kSubtileBytes);

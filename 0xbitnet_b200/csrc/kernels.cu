@@ -679,7 +679,10 @@ __global__ __launch_bounds__(256) void k_bitlinear_n1(
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool geom_ok = ns >= 1 && ns <= wslots && wslots <= NSUB;
   if (tid == 0 && !geom_ok) record_error(DEVERR_BAD_LAUNCH);
-  if (!geom_ok) return;  // uniform per CTA
+  if (!geom_ok) {  // uniform per CTA; still ordered after the preceding grid
+    pdl_wait();
+    return;
+  }
   uint8_t* w_s = smem;                                                         // wslots * KB * 512
   float* xn_s = reinterpret_cast<float*>(smem + wslots * KB * kSubtileBytes);  // K floats
   uint8_t* q_s = reinterpret_cast<uint8_t*>(xn_s + K);                       // K bytes

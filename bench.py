@@ -1075,6 +1075,17 @@ def run_case(spec: str):
         obn.check_device_errors()
         print(f"case quant B={B}: ok")
         return
+    if name in ("attndec", "decoder"):  # the full-run blocks alone: B = layers / context
+        dev = torch.device("cuda", 0)
+        stream = torch.cuda.Stream(dev)
+        try:
+            peak = float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"])
+        except (OSError, ValueError, KeyError):
+            peak = 6650.0  # the pool's fallback copy bandwidth
+        res = (measure_attention(dev, stream, peak, B) if name == "attndec"
+               else measure_decoder(dev, stream, 1, 0, ctx=B))
+        print(json.dumps({name: res}), flush=True)
+        return
     if name == "attn":  # decode attention, 5 KV heads, context 2048, B sequences, 3 steps
         att = importlib.import_module("0xbitnet_b200.attention")
         cache = att.KVCache(B, 2048, 5, 128)

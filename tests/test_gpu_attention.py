@@ -96,7 +96,8 @@ def test_attention_decode_step_end_to_end():
 
 
 @pytest.mark.parametrize("B,H,Hkv,S_prev", [(1, 20, 5, 2047), (3, 20, 5, 127), (2, 16, 2, 128),
-                                             (1, 8, 8, 0), (2, 32, 4, 300)])
+                                             (1, 8, 8, 0), (2, 32, 4, 300), (1, 20, 5, 1),
+                                             (1, 20, 5, 4100), (1, 20, 5, 9000)])
 def test_fused_rope_attention_is_bit_identical(B, H, Hkv, S_prev):
     """obn_attention_decode_rope == obn_rope_kv_append + obn_attention_decode (n = 1):
     same output bits, same cache contents."""
@@ -116,4 +117,81 @@ def test_fused_rope_attention_is_bit_identical(B, H, Hkv, S_prev):
     got = att().attention_rope(qkv, c2, H, S_prev).cpu()
     torch.cuda.synchronize()
     assert torch.equal(got, want)
+    assert torch.equal(c1.k.cpu(), c2.k.cpu()) and torch.equal(c1.v.cpu(), c2.v.cpu())
+
+
+def _rope_at(qkv, cache, H, pos_dev, out, ws):
+    import ctypes
+    import torch
+    from importlib import import_module
+    L = import_module("0xbitnet_b200._lib")
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    L.check(L.lib().obn_attention_decode_rope_at(
+        p(qkv), p(cache.k), p(cache.v), cache.B, H, cache.Hkv, D, cache.S_max, p(pos_dev),
+        ctypes.c_float(500000.0), ctypes.c_float(float(np.float32(1.0) / np.sqrt(np.float32(D)))),
+        p(out), p(ws),
+        ctypes.c_size_t(ws.numel()), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+
+
+@pytest.mark.parametrize("B,H,Hkv,S_max,pos", [(1, 20, 5, 4096, 1000), (1, 20, 5, 4096, 2500),
+                                               (2, 32, 4, 2048, 2047), (1, 20, 5, 4096, 4096),
+                                               (1, 8, 8, 20000, 130)])
+def test_rope_attention_device_position(B, H, Hkv, S_max, pos):
+    """The _at form (position read on the device, chunks sized for S_max) equals
+    RoPE append + attention at the host position, bit for bit; a position at
+    S_max appends nothing and attends over the whole cache."""
+    torch = need_cuda()
+    rng = np.random.default_rng(S_max + pos)
+    k = torch.from_numpy(rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16))
+    v = torch.from_numpy(rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16))
+    qkv = torch.from_numpy(rng.standard_normal((B, (H + 2 * Hkv) * D)).astype(np.float32)).cuda()
+    c1, c2 = att().KVCache(B, S_max, Hkv, D), att().KVCache(B, S_max, Hkv, D)
+    for c in (c1, c2):
+        c.k.copy_(k)
+        c.v.copy_(v)
+    if pos < S_max:
+        q = att().rope_kv_append(qkv, c1, H, 1, 500000.0, pos=pos)
+        want = att().attention(q, c1, H, 1, pos + 1).cpu()
+    else:  # a full cache: q rotated at pos (scratch cache one row longer) over all S_max keys
+        scratch = att().KVCache(B, S_max + 1, Hkv, D)
+        q = att().rope_kv_append(qkv, scratch, H, 1, 500000.0, pos=pos)
+        want = att().attention(q, c1, H, 1, S_max).cpu()
+    from importlib import import_module
+    L = import_module("0xbitnet_b200._lib")
+    ws = torch.empty(int(L.lib().obn_attention_workspace_bytes(B, 1, H, D, S_max)),
+                     dtype=torch.uint8, device="cuda")
+    out = torch.empty((B, H * D), dtype=torch.float32, device="cuda")
+    pos_dev = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    _rope_at(qkv, c2, H, pos_dev, out, ws)
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), want)
+    assert torch.equal(c1.k.cpu(), c2.k.cpu()) and torch.equal(c1.v.cpu(), c2.v.cpu())
+
+
+def test_rope_attention_back_to_back_steps():
+    """Consecutive decode steps on one cache, enqueued with no host sync between
+    them (each reads the row the step before appended), equal the same steps run
+    one at a time through RoPE append + attention."""
+    torch = need_cuda()
+    B, H, Hkv, S_max, pos0, steps = 2, 20, 5, 2048, 1020, 12
+    rng = np.random.default_rng(77)
+    k = torch.from_numpy(rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16))
+    v = torch.from_numpy(rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16))
+    qkvs = [torch.from_numpy(rng.standard_normal((B, (H + 2 * Hkv) * D)).astype(np.float32)).cuda()
+            for _ in range(steps)]
+    c1, c2 = att().KVCache(B, S_max, Hkv, D), att().KVCache(B, S_max, Hkv, D)
+    for c in (c1, c2):
+        c.k.copy_(k)
+        c.v.copy_(v)
+    want = []
+    for i in range(steps):
+        q = att().rope_kv_append(qkvs[i], c1, H, 1, pos=pos0 + i)
+        want.append(att().attention(q, c1, H, 1, pos0 + i + 1).cpu())
+        torch.cuda.synchronize()
+    outs = [torch.empty((B, H * D), dtype=torch.float32, device="cuda") for _ in range(steps)]
+    for i in range(steps):
+        att().attention_rope(qkvs[i], c2, H, pos0 + i, out=outs[i])
+    torch.cuda.synchronize()
+    for i in range(steps):
+        assert torch.equal(outs[i].cpu(), want[i]), i
     assert torch.equal(c1.k.cpu(), c2.k.cpu()) and torch.equal(c1.v.cpu(), c2.v.cpu())
