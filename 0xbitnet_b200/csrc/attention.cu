@@ -43,14 +43,20 @@ constexpr int kKStride = kAttnHeadDim + 8;  // halves per smem K row: 16-byte ro
 // rope.wgsl:41-55 for the pair (x0, x1) = dims (2i, 2i + 1) of a head at
 // position p: theta = p * base^(-2i/d), then the rotation with products and
 // sums rounded as written.
-OBN_DEVINL void rope_pair(float x0, float x1, int i, int d, int p, float theta_base, float* y0,
-                          float* y1) {
+OBN_DEVINL void rope_angle(int i, int d, int p, float theta_base, float* c, float* sn) {
   const float freq_exp = __fdiv_rn(__fmul_rn(-2.0f, static_cast<float>(i)), static_cast<float>(d));
   const float theta = __fmul_rn(static_cast<float>(p), powf(theta_base, freq_exp));
-  float sn, c;
-  sincosf(theta, &sn, &c);
+  sincosf(theta, sn, c);
+}
+OBN_DEVINL void rope_rotate(float x0, float x1, float c, float sn, float* y0, float* y1) {
   *y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
   *y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+}
+OBN_DEVINL void rope_pair(float x0, float x1, int i, int d, int p, float theta_base, float* y0,
+                          float* y1) {
+  float c, sn;
+  rope_angle(i, d, p, theta_base, &c, &sn);
+  rope_rotate(x0, x1, c, sn, y0, y1);
 }
 
 __global__ __launch_bounds__(256) void k_rope_kv_append(const float* __restrict__ qkv, int n,
@@ -668,6 +674,7 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
     int slots, float* __restrict__ out, float theta_base) {
   constexpr int D = kAttnHeadDim;
   constexpr int C = kAttnChunk;
+  constexpr uint32_t kRowBytes = D * 2;
   static_assert(C == 128 && D == 128 && kAttnThreads == 128 && G <= 8, "tile shape");
   extern __shared__ __align__(16) unsigned char smem[];
   __half* sK = reinterpret_cast<__half*>(smem);             // [C][kKStride]
@@ -678,6 +685,8 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
   float* sM = sAcc + slots * G * D;                         // [slots][G] partial max
   float* sL = sM + slots * G;                               // [slots][G] partial sum
   __shared__ float red_m[8][4], red_l[8][4];
+  __shared__ float s_cos[D / 2], s_sin[D / 2];  // RoPE angle of dimension pair i at pos
+  __shared__ __align__(8) uint64_t bar[2];      // rows copied before / after the wait
   const int tid = threadIdx.x;
   const int CS = static_cast<int>(gridDim.x);  // the cluster spans the grid's x
   const int rank = static_cast<int>(blockIdx.x);
@@ -686,29 +695,38 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
   const int p_new = pos_dev ? *pos_dev : pos;
   const int seq_len = min(p_new + 1, S_max);
   const int nvalid = min(nsplit, (seq_len + C - 1) / C);  // chunks that hold keys
-  const int late = p_new - 1;  // first row copied after the wait
+  const int late = max(p_new - 1, 0);  // first row copied after the wait
+  if (tid == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_mbar_init();
+  }
+  if (tid < D / 2) rope_angle(tid, D, p_new, theta_base, &s_cos[tid], &s_sin[tid]);
+  __syncthreads();
 
-  // Rows [0, cnt) of the chunk at s0 whose position is below `upto` (async
-  // copies), rows >= cnt zero, the new token's row left for the append.
-  auto copy_chunk = [&](int s0, int cnt, int from, int upto) {
-#pragma unroll 4
-    for (int e = tid; e < C * (D / 8); e += kAttnThreads) {
-      const int key = e / (D / 8), part = e % (D / 8);
-      __half* dk = sK + key * kKStride + part * 8;
-      __half* dv = sV + key * kVStride + part * 8;
-      const int p = s0 + key;
-      if (key >= cnt) {
-        if (from == 0) {
-          *reinterpret_cast<uint4*>(dk) = make_uint4(0u, 0u, 0u, 0u);
-          *reinterpret_cast<uint4*>(dv) = make_uint4(0u, 0u, 0u, 0u);
-        }
-      } else if (p >= from && p < upto && p != p_new) {
-        const size_t g = ((b * S_max + p) * Hkv + kvh) * D + part * 8;
-        cp_async16(dk, k_cache + g);
-        cp_async16(dv, v_cache + g);
+  // Bulk copies (one 256-byte K row and one V row per thread) of the chunk at s0:
+  // its rows at positions [from, upto) below seq_len, except the new token's row,
+  // completing on `bar`. With zero_tail, rows past seq_len become zero.
+  auto copy_rows = [&](int s0, int from, int upto, uint64_t* bar_, bool zero_tail) {
+    const int a = max(s0, from), e = min(min(s0 + C, seq_len), upto);
+    int rows = max(e - a, 0);
+    if (p_new >= a && p_new < e) --rows;
+    if (tid == 0) mbar_arrive_expect_tx(bar_, static_cast<uint32_t>(rows) * 2u * kRowBytes);
+    const int p = s0 + tid;
+    if (p >= a && p < e && p != p_new) {
+      const size_t g = ((b * S_max + p) * Hkv + kvh) * D;
+      bulk_g2s(sK + tid * kKStride, k_cache + g, kRowBytes, bar_);
+      bulk_g2s(sV + tid * kVStride, v_cache + g, kRowBytes, bar_);
+    } else if (zero_tail && p >= seq_len) {
+#pragma unroll
+      for (int j = 0; j < D / 8; ++j) {
+        *reinterpret_cast<uint4*>(sK + tid * kKStride + 8 * j) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(sV + tid * kVStride + 8 * j) = make_uint4(0u, 0u, 0u, 0u);
       }
     }
-    cp_async_commit();
+  };
+  auto wait_rows = [&](uint64_t* bar_, uint32_t parity) {
+    if (!mbar_wait(bar_, parity)) mbar_wait(bar_, parity);  // bounded; the error is recorded
   };
   // The new token's rotated key and value: into the caches and the chunk's tiles.
   const float* qrow = qkv + b * static_cast<size_t>(H + 2 * Hkv) * D;
@@ -719,7 +737,7 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
     if (tid < D / 2) {
       const float* src = qrow + (static_cast<size_t>(H) + kvh) * D + 2 * tid;
       float y0, y1;
-      rope_pair(src[0], src[1], tid, D, p_new, theta_base, &y0, &y1);
+      rope_rotate(src[0], src[1], s_cos[tid], s_sin[tid], &y0, &y1);
       const __half2 h = __floats2half2_rn(y0, y1);
       *reinterpret_cast<__half2*>(k_cache + cache_off + 2 * tid) = h;
       *reinterpret_cast<__half2*>(sK + row * kKStride + 2 * tid) = h;
@@ -749,10 +767,8 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
     }
   };
 
-  // ---- before the wait: the first slot's older rows
-  const int s00 = rank * C;
-  const int cnt0 = min(C, seq_len - s00);
-  if (rank < nvalid) copy_chunk(s00, cnt0, 0, late);
+  // ---- before the wait: the first slot's rows below pos - 1
+  if (rank < nvalid) copy_rows(rank * C, 0, late, &bar[0], true);
   pdl_wait();
   pdl_launch_dependents();
 
@@ -761,7 +777,7 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
     const int g = e / (D / 2), i = e % (D / 2);
     const float* src = qrow + (static_cast<size_t>(kvh) * G + g) * D + 2 * i;
     float y0, y1;
-    rope_pair(src[0], src[1], i, D, p_new, theta_base, &y0, &y1);
+    rope_rotate(src[0], src[1], s_cos[i], s_sin[i], &y0, &y1);
     sQ[g * D + 2 * i] = y0;
     sQ[g * D + 2 * i + 1] = y1;
   }
@@ -770,14 +786,14 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
     if (c >= nvalid) break;  // uniform per CTA
     const int s0 = c * C;
     const int cnt = min(C, seq_len - s0);
-    if (slot == 0) {
-      copy_chunk(s0, cnt, max(late, 0), 0x7fffffff);  // rows pos - 1 and up
-    } else {
-      __syncthreads();  // the previous slot is done with the tiles
-      copy_chunk(s0, cnt, 0, 0x7fffffff);
+    if (slot > 0) {  // the previous slot is done with the tiles (generic writes included)
+      fence_proxy_async_smem();
+      __syncthreads();
     }
+    copy_rows(s0, slot == 0 ? late : 0, 0x7fffffff, &bar[1], slot > 0);
     append_new(s0);
-    cp_async_wait_group<0>();
+    if (slot == 0) wait_rows(&bar[0], 0);
+    wait_rows(&bar[1], static_cast<uint32_t>(slot & 1));
     __syncthreads();
     float o[2][4];
     tc_chunk<G, false>(sK, sV, sQ, sP, cnt, scale, red_m, red_l, o);
@@ -789,7 +805,10 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
   const int per = G * D / CS;
   float* gAcc = reinterpret_cast<float*>(sK);  // [nvalid][per], the tiles are free now
   float* gM = reinterpret_cast<float*>(sV);    // [nvalid][G]
-  float* gL = gM + kClMaxChunks * G;
+  float* gL = gM + kClMaxChunks * G;           // [nvalid][G]
+  float* gW = gL + kClMaxChunks * G;           // [nvalid][G] chunk weights
+  float* gMax = gW + kClMaxChunks * G;         // [G]
+  float* gSum = gMax + 8;                      // [G]
   const uint32_t acc_base = smem_u32(sAcc) + static_cast<uint32_t>(rank * per) * 4u;
   for (int e = tid; e < nvalid * per; e += kAttnThreads) {
     const int c = e / per, j = e - c * per;
@@ -804,20 +823,37 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
   }
   __syncthreads();
   cl_arrive_relaxed();  // done reading the other CTAs' shared memory
-  if (tid < per) {
-    const int oi = rank * per + tid;
-    const int g = oi / D, dim = oi - g * D;
+  // k_attn_combine's arithmetic, each step computed once: the global max per
+  // head, every chunk's weight, the normaliser per head (chunk order), then the
+  // outputs (chunk order).
+  if (tid < G) {
     float M = -FLT_MAX;
-    for (int c = 0; c < nvalid; ++c) M = fmaxf(M, gM[c * G + g]);
-    float L = 0.0f, o = 0.0f;
+    for (int c = 0; c < nvalid; ++c) M = fmaxf(M, gM[c * G + tid]);
+    gMax[tid] = M;
+  }
+  __syncthreads();
+  for (int e = tid; e < nvalid * G; e += kAttnThreads)
+    gW[e] = gL[e] == 0.0f ? 0.0f : expf(gM[e] - gMax[e % G]);
+  __syncthreads();
+  if (tid < G) {
+    float L = 0.0f;
     for (int c = 0; c < nvalid; ++c) {
-      const float l = gL[c * G + g];
+      const float l = gL[c * G + tid];
       if (l == 0.0f) continue;  // an empty chunk
-      const float w = expf(gM[c * G + g] - M);
-      L = fmaf(w, l, L);
-      o = fmaf(w, gAcc[c * per + tid], o);
+      L = fmaf(gW[c * G + tid], l, L);
     }
-    out[((b * H) + static_cast<size_t>(kvh) * G + g) * D + dim] = o / L;
+    gSum[tid] = L;
+  }
+  __syncthreads();
+  for (int j = tid; j < per; j += kAttnThreads) {
+    const int oi = rank * per + j;
+    const int g = oi / D, dim = oi - g * D;
+    float o = 0.0f;
+    for (int c = 0; c < nvalid; ++c) {
+      if (gL[c * G + g] == 0.0f) continue;
+      o = fmaf(gW[c * G + g], gAcc[c * per + j], o);
+    }
+    out[((b * H) + static_cast<size_t>(kvh) * G + g) * D + dim] = o / gSum[g];
   }
   cl_wait();  // keep this CTA's partials alive until every CTA has read them
 }
