@@ -640,31 +640,67 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split_tc(
 // pos - 1 is copied after the wait. The device position (*pos_dev) is written by
 // stream-ordered copies, never by a kernel of this library.
 constexpr int kClMaxSlots = 4;  // chunks per CTA
-constexpr int kClMaxChunks = 64;
 
 OBN_DEVINL uint32_t cl_map(uint32_t smem_addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
   return r;
 }
-OBN_DEVINL float cl_ld(uint32_t cluster_addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
-  return v;
+OBN_DEVINL void cl_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
-OBN_DEVINL void cl_sync_publish() {  // this CTA's shared-memory writes -> the cluster
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
-                   : "memory");
+OBN_DEVINL void cl_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-OBN_DEVINL void cl_arrive_relaxed() {
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+// Stores into another CTA's shared memory (cluster addresses) that complete
+// their bytes on that CTA's mbarrier.
+OBN_DEVINL void st_async_v4(uint32_t dst, float4 v, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, "
+      "[%5];" ::"r"(dst),
+      "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
+      : "memory");
 }
-OBN_DEVINL void cl_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+OBN_DEVINL void st_async_v2(uint32_t dst, float a, float b, uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+          dst),
+      "f"(a), "f"(b), "r"(remote_bar)
+      : "memory");
+}
+// Bounded wait on a barrier that other CTAs of the cluster complete.
+OBN_DEVINL bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  record_error(DEVERR_MBAR_TIMEOUT);
+  return false;
+}
+OBN_DEVINL void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
-inline size_t cl_smem_bytes(int G, int slots) {
-  return static_cast<size_t>(kAttnChunk) * kKStride * 2 + static_cast<size_t>(kAttnChunk) * kVStride * 2 +
-         static_cast<size_t>(G) * kAttnHeadDim * 4 + static_cast<size_t>(kAttnChunk) * G * 4 +
-         static_cast<size_t>(slots) * G * (kAttnHeadDim + 2) * 4;
+// Outputs of the group a CTA combines, and the stride of one chunk's record in
+// its receive buffer: `per` partial outputs, then the chunk's (max, sum) of the
+// head those outputs belong to, padded to 16 bytes.
+__host__ __device__ inline int cl_per(int G, int CS) { return G * kAttnHeadDim / CS; }
+__host__ __device__ inline int cl_rec(int G, int CS) { return cl_per(G, CS) + 4; }
+
+// Dynamic shared memory: K and V tiles, q, probabilities, one chunk's partial
+// [G][D] + (max, sum) per head, then the receive buffer [CS * slots][rec].
+inline size_t cl_smem_bytes(int G, int CS, int slots) {
+  return static_cast<size_t>(kAttnChunk) * kKStride * 2 +
+         static_cast<size_t>(kAttnChunk) * kVStride * 2 + static_cast<size_t>(G) * kAttnHeadDim * 4 +
+         static_cast<size_t>(kAttnChunk) * G * 4 + static_cast<size_t>(G) * kAttnHeadDim * 4 + 64 +
+         static_cast<size_t>(CS) * slots * cl_rec(G, CS) * 4;
 }
 
 template <int G>
@@ -677,18 +713,20 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
   constexpr uint32_t kRowBytes = D * 2;
   static_assert(C == 128 && D == 128 && kAttnThreads == 128 && G <= 8, "tile shape");
   extern __shared__ __align__(16) unsigned char smem[];
+  const int CS = static_cast<int>(gridDim.x);  // the cluster spans the grid's x
+  const int per = cl_per(G, CS), rec = cl_rec(G, CS);
   __half* sK = reinterpret_cast<__half*>(smem);             // [C][kKStride]
   __half* sV = sK + C * kKStride;                           // [C][kVStride]
   float* sQ = reinterpret_cast<float*>(sV + C * kVStride);  // [G][D] rotated q
   float* sP = sQ + G * D;                                   // [C][G] probabilities
-  float* sAcc = sP + C * G;                                 // [slots][G][D] partial P.V
-  float* sM = sAcc + slots * G * D;                         // [slots][G] partial max
-  float* sL = sM + slots * G;                               // [slots][G] partial sum
+  float* sAcc = sP + C * G;                                 // [G][D] a chunk's partial P.V
+  float* sM = sAcc + G * D;                                 // [8] its max per head
+  float* sL = sM + 8;                                       // [8] its sum per head
+  float* rbuf = sL + 8;                                     // [CS * slots][rec] received
   __shared__ float red_m[8][4], red_l[8][4];
   __shared__ float s_cos[D / 2], s_sin[D / 2];  // RoPE angle of dimension pair i at pos
-  __shared__ __align__(8) uint64_t bar[2];      // rows copied before / after the wait
+  __shared__ __align__(8) uint64_t bar[3];      // rows before / after the wait; partials in
   const int tid = threadIdx.x;
-  const int CS = static_cast<int>(gridDim.x);  // the cluster spans the grid's x
   const int rank = static_cast<int>(blockIdx.x);
   const int kvh = blockIdx.y;
   const size_t b = blockIdx.z;
@@ -699,14 +737,18 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
   if (tid == 0) {
     mbar_init(&bar[0], 1);
     mbar_init(&bar[1], 1);
+    mbar_init(&bar[2], 1);
     fence_mbar_init();
   }
   if (tid < D / 2) rope_angle(tid, D, p_new, theta_base, &s_cos[tid], &s_sin[tid]);
   __syncthreads();
+  cl_arrive_release();  // every CTA's barriers initialised before the first remote store
+  if (tid == 0)  // the partials of every chunk for this CTA's outputs
+    mbar_arrive_expect_tx(&bar[2], static_cast<uint32_t>(max(nvalid, 0) * (per + 2) * 4));
 
   // Bulk copies (one 256-byte K row and one V row per thread) of the chunk at s0:
   // its rows at positions [from, upto) below seq_len, except the new token's row,
-  // completing on `bar`. With zero_tail, rows past seq_len become zero.
+  // completing on `bar_`. With zero_tail, rows past seq_len become zero.
   auto copy_rows = [&](int s0, int from, int upto, uint64_t* bar_, bool zero_tail) {
     const int a = max(s0, from), e = min(min(s0 + C, seq_len), upto);
     int rows = max(e - a, 0);
@@ -749,8 +791,9 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
       *reinterpret_cast<__half2*>(sV + row * kVStride + 2 * i) = h;
     }
   };
-  // This thread's partial of one chunk -> slot `slot` (after tc_chunk).
-  auto keep_partial = [&](int slot, const float (&o)[2][4]) {
+  // One chunk's partial -> the CTAs that combine it: CTA j receives outputs
+  // [j * per, j * per + per) and the (max, sum) of their head, as record c.
+  auto push_partial = [&](int c, const float (&o)[2][4]) {
     const int lane = tid & 31, warp = tid >> 5, grp = lane >> 2, qd = lane & 3;
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
@@ -758,17 +801,38 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
       for (int i = 0; i < 4; ++i) {
         const int dim = 32 * warp + 16 * mt + grp + (i >= 2 ? 8 : 0);
         const int h = 2 * qd + (i & 1);
-        if (h < G) sAcc[(slot * G + h) * D + dim] = o[mt][i];
+        if (h < G) sAcc[h * D + dim] = o[mt][i];
       }
     if (tid < G) {
-      sM[slot * G + tid] =
-          fmaxf(fmaxf(red_m[tid][0], red_m[tid][1]), fmaxf(red_m[tid][2], red_m[tid][3]));
-      sL[slot * G + tid] = (red_l[tid][0] + red_l[tid][1]) + (red_l[tid][2] + red_l[tid][3]);
+      sM[tid] = fmaxf(fmaxf(red_m[tid][0], red_m[tid][1]), fmaxf(red_m[tid][2], red_m[tid][3]));
+      sL[tid] = (red_l[tid][0] + red_l[tid][1]) + (red_l[tid][2] + red_l[tid][3]);
+    }
+    __syncthreads();
+    const int pieces = per / 4 + 1;
+    for (int e = tid; e < CS * pieces; e += kAttnThreads) {
+      const int j = e / pieces, piece = e - j * pieces;
+      const uint32_t rbar = cl_map(smem_u32(&bar[2]), static_cast<uint32_t>(j));
+      const uint32_t dst = cl_map(smem_u32(rbuf + c * rec), static_cast<uint32_t>(j));
+      if (piece < per / 4) {
+        const float4 v = *reinterpret_cast<const float4*>(sAcc + j * per + 4 * piece);
+        st_async_v4(dst + 16u * piece, v, rbar);
+      } else {
+        const int g = (j * per) / D;
+        st_async_v2(dst + 4u * per, sM[g], sL[g], rbar);
+      }
     }
   };
 
-  // ---- before the wait: the first slot's rows below pos - 1
-  if (rank < nvalid) copy_rows(rank * C, 0, late, &bar[0], true);
+  // ---- before the wait: the first slot's rows below pos - 1, row pos - 1 into L2
+  if (rank < nvalid) {
+    copy_rows(rank * C, 0, late, &bar[0], true);
+    if (tid == 0 && p_new >= 1 && p_new - 1 < seq_len && (p_new - 1) / C == rank) {
+      const size_t g = ((b * S_max + (p_new - 1)) * Hkv + kvh) * D;
+      prefetch_l2(k_cache + g, kRowBytes);
+      prefetch_l2(v_cache + g, kRowBytes);
+    }
+  }
+  cl_wait_acquire();
   pdl_wait();
   pdl_launch_dependents();
 
@@ -797,65 +861,27 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
     __syncthreads();
     float o[2][4];
     tc_chunk<G, false>(sK, sV, sQ, sP, cnt, scale, red_m, red_l, o);
-    keep_partial(slot, o);
+    push_partial(c, o);
   }
 
-  // ---- combine over the cluster: this CTA's outputs [rank * per, rank * per + per)
-  cl_sync_publish();
-  const int per = G * D / CS;
-  float* gAcc = reinterpret_cast<float*>(sK);  // [nvalid][per], the tiles are free now
-  float* gM = reinterpret_cast<float*>(sV);    // [nvalid][G]
-  float* gL = gM + kClMaxChunks * G;           // [nvalid][G]
-  float* gW = gL + kClMaxChunks * G;           // [nvalid][G] chunk weights
-  float* gMax = gW + kClMaxChunks * G;         // [G]
-  float* gSum = gMax + 8;                      // [G]
-  const uint32_t acc_base = smem_u32(sAcc) + static_cast<uint32_t>(rank * per) * 4u;
-  for (int e = tid; e < nvalid * per; e += kAttnThreads) {
-    const int c = e / per, j = e - c * per;
-    const uint32_t a = acc_base + static_cast<uint32_t>(((c / CS) * G * D + j) * 4);
-    gAcc[e] = cl_ld(cl_map(a, static_cast<uint32_t>(c % CS)));
-  }
-  for (int e = tid; e < nvalid * G; e += kAttnThreads) {
-    const int c = e / G, g = e - c * G;
-    const uint32_t off = static_cast<uint32_t>(((c / CS) * G + g) * 4);
-    gM[e] = cl_ld(cl_map(smem_u32(sM) + off, static_cast<uint32_t>(c % CS)));
-    gL[e] = cl_ld(cl_map(smem_u32(sL) + off, static_cast<uint32_t>(c % CS)));
-  }
-  __syncthreads();
-  cl_arrive_relaxed();  // done reading the other CTAs' shared memory
-  // k_attn_combine's arithmetic, each step computed once: the global max per
-  // head, every chunk's weight, the normaliser per head (chunk order), then the
-  // outputs (chunk order).
-  if (tid < G) {
-    float M = -FLT_MAX;
-    for (int c = 0; c < nvalid; ++c) M = fmaxf(M, gM[c * G + tid]);
-    gMax[tid] = M;
-  }
-  __syncthreads();
-  for (int e = tid; e < nvalid * G; e += kAttnThreads)
-    gW[e] = gL[e] == 0.0f ? 0.0f : expf(gM[e] - gMax[e % G]);
-  __syncthreads();
-  if (tid < G) {
-    float L = 0.0f;
-    for (int c = 0; c < nvalid; ++c) {
-      const float l = gL[c * G + tid];
-      if (l == 0.0f) continue;  // an empty chunk
-      L = fmaf(gW[c * G + tid], l, L);
-    }
-    gSum[tid] = L;
-  }
-  __syncthreads();
-  for (int j = tid; j < per; j += kAttnThreads) {
+  // ---- combine: k_attn_combine's arithmetic over the records, in chunk order
+  const bool got = mbar_wait_cluster(&bar[2], 0);
+  for (int j = tid; j < per && got; j += kAttnThreads) {
     const int oi = rank * per + j;
     const int g = oi / D, dim = oi - g * D;
-    float o = 0.0f;
+    float M = -FLT_MAX;
+    for (int c = 0; c < nvalid; ++c) M = fmaxf(M, rbuf[c * rec + per]);
+    float L = 0.0f, o = 0.0f;
+#pragma unroll 4
     for (int c = 0; c < nvalid; ++c) {
-      if (gL[c * G + g] == 0.0f) continue;
-      o = fmaf(gW[c * G + g], gAcc[c * per + j], o);
+      const float l = rbuf[c * rec + per + 1];
+      if (l == 0.0f) continue;  // an empty chunk
+      const float w = expf(rbuf[c * rec + per] - M);
+      L = fmaf(w, l, L);
+      o = fmaf(w, rbuf[c * rec + j], o);
     }
-    out[((b * H) + static_cast<size_t>(kvh) * G + g) * D + dim] = o / gSum[g];
+    out[((b * H) + static_cast<size_t>(kvh) * G + g) * D + dim] = o / L;
   }
-  cl_wait();  // keep this CTA's partials alive until every CTA has read them
 }
 
 // One CTA per (query row, head): thread = dimension.
@@ -974,13 +1000,15 @@ int decode_cluster_size() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
   if (cache[dev]) return cache[dev] > 0 ? cache[dev] : 0;
   auto kern = k_attn_decode_cl<G>;
-  const size_t smem = cl_smem_bytes(G, kClMaxSlots);
   int best = -1;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem)) == cudaSuccess &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
-          cudaSuccess) {
+  // the attribute ends at the largest size any launch uses (16 first, then 8)
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+      cudaSuccess) {
     for (int cs : {16, 8}) {
+      const size_t smem = cl_smem_bytes(G, cs, kClMaxSlots);
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem)) != cudaSuccess)
+        continue;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(cs, 1, 1);
       cfg.blockDim = dim3(kAttnThreads);
@@ -1012,7 +1040,7 @@ cudaError_t launch_decode_cl(const float* qkv, __half* k_cache, __half* v_cache,
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CS, Hkv, B);
   cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = cl_smem_bytes(G, slots);
+  cfg.dynamicSmemBytes = cl_smem_bytes(G, CS, slots);
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
