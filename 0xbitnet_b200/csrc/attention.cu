@@ -864,23 +864,38 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
     push_partial(c, o);
   }
 
-  // ---- combine: k_attn_combine's arithmetic over the records, in chunk order
+  // ---- combine: k_attn_combine's arithmetic over the records, in chunk order.
+  // Every output of this CTA belongs to one head, so the chunk weights are
+  // shared: lane l of each warp holds chunks l and l + 32 (nvalid <= 64) and
+  // hands them out by shuffles; the max is exact in any order.
   const bool got = mbar_wait_cluster(&bar[2], 0);
-  for (int j = tid; j < per && got; j += kAttnThreads) {
-    const int oi = rank * per + j;
-    const int g = oi / D, dim = oi - g * D;
-    float M = -FLT_MAX;
-    for (int c = 0; c < nvalid; ++c) M = fmaxf(M, rbuf[c * rec + per]);
+  if (got && tid < ((per + 31) & ~31)) {  // whole warps
+    const int lane = tid & 31;
+    const bool h0 = lane < nvalid, h1 = lane + 32 < nvalid;
+    const float m0 = h0 ? rbuf[lane * rec + per] : -FLT_MAX;
+    const float m1 = h1 ? rbuf[(lane + 32) * rec + per] : -FLT_MAX;
+    const float l0 = h0 ? rbuf[lane * rec + per + 1] : 0.0f;
+    const float l1 = h1 ? rbuf[(lane + 32) * rec + per + 1] : 0.0f;
+    float M = fmaxf(m0, m1);
+#pragma unroll
+    for (int sft = 16; sft >= 1; sft >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sft));
+    const float w0 = l0 == 0.0f ? 0.0f : expf(m0 - M);
+    const float w1 = l1 == 0.0f ? 0.0f : expf(m1 - M);
+    const int j = tid;
     float L = 0.0f, o = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
     for (int c = 0; c < nvalid; ++c) {
-      const float l = rbuf[c * rec + per + 1];
-      if (l == 0.0f) continue;  // an empty chunk
-      const float w = expf(rbuf[c * rec + per] - M);
+      const float l = __shfl_sync(0xffffffffu, c < 32 ? l0 : l1, c & 31);
+      const float w = __shfl_sync(0xffffffffu, c < 32 ? w0 : w1, c & 31);
+      if (l == 0.0f) continue;  // an empty chunk (uniform over the warp)
       L = fmaf(w, l, L);
-      o = fmaf(w, rbuf[c * rec + j], o);
+      o = fmaf(w, j < per ? rbuf[c * rec + j] : 0.0f, o);
     }
-    out[((b * H) + static_cast<size_t>(kvh) * G + g) * D + dim] = o / L;
+    if (j < per) {
+      const int oi = rank * per + j;
+      const int g = oi / D, dim = oi - g * D;
+      out[((b * H) + static_cast<size_t>(kvh) * G + g) * D + dim] = o / L;
+    }
   }
 }
 
