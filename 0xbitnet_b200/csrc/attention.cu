@@ -883,13 +883,16 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
     const float w1 = l1 == 0.0f ? 0.0f : expf(m1 - M);
     const int j = tid;
     float L = 0.0f, o = 0.0f;
+    // an empty chunk (l == 0) leaves L and o as they are; selects, not branches,
+    // so the loads and shuffles of later chunks issue ahead of the chain
 #pragma unroll 8
     for (int c = 0; c < nvalid; ++c) {
       const float l = __shfl_sync(0xffffffffu, c < 32 ? l0 : l1, c & 31);
       const float w = __shfl_sync(0xffffffffu, c < 32 ? w0 : w1, c & 31);
-      if (l == 0.0f) continue;  // an empty chunk (uniform over the warp)
-      L = fmaf(w, l, L);
-      o = fmaf(w, j < per ? rbuf[c * rec + j] : 0.0f, o);
+      const float a = j < per ? rbuf[c * rec + j] : 0.0f;
+      const float Ln = fmaf(w, l, L), on = fmaf(w, a, o);
+      L = l == 0.0f ? L : Ln;
+      o = l == 0.0f ? o : on;
     }
     if (j < per) {
       const int oi = rank * per + j;
