@@ -34,6 +34,9 @@
 #include <cstdlib>
 
 namespace obn {
+
+int num_sms_cached();  // kernels.cu
+
 namespace {
 
 constexpr int kAttnThreads = 128;
@@ -1105,11 +1108,14 @@ cudaError_t attention_impl(const float* q, const __half* k_cache, const __half* 
   float* pm = pa + rows * d;
   float* pl = pm + rows;
   const int G = H / Hkv;
-  if (rope) {  // one clustered launch when the chunks fit the cluster's slots
+  // One clustered launch when the chunks fit the cluster's slots and the clusters
+  // fit about two CTAs per SM; more sequences run the split + combine passes,
+  // whose smaller CTAs fill the SMs beside the neighbouring matmuls better.
+  if (rope) {
 #define OBN_CL(GG)                                                                              \
   {                                                                                             \
     const int cs = decode_cluster_size<GG>();                                                   \
-    if (cs > 0 && nsplit <= cs * kClMaxSlots)                                                   \
+    if (cs > 0 && nsplit <= cs * kClMaxSlots && B * Hkv * cs <= 2 * num_sms_cached())           \
       return launch_decode_cl<GG>(q, const_cast<__half*>(k_cache), const_cast<__half*>(v_cache), \
                                   B, H, Hkv, S_max, seq_len - 1, pos_dev, scale, nsplit, cs, out, \
                                   s, theta_base);                                               \

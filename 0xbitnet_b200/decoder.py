@@ -194,8 +194,10 @@ class BitNetDecoder:
             L.o.forward_residual(self.attn, self.x, n=B)  # x += o_proj(attn)
             L.gate_up.forward(self.x, n=B, out=self.ffn_out)
             L.down.forward_residual(self.ffn_out, self.x, n=B)  # x += down(ffn)
-        if B <= 4:  # the shader's exact order (the reference's own case is one token)
+        if B == 1:  # the shader's exact order (the reference's own case is one token)
             return lm_head_f16(self.embed, self.x, self.final_norm, cfg.eps)
+        # two or more tokens: the tensor-core head reads the table once for all of
+        # them (the exact-order kernel is bound by its unfused f32 products there)
         return lm_head_f16_batched(self.embed, self.x, self.final_norm, cfg.eps,
                                    out=self.logits, workspace=self.lm_ws)
 

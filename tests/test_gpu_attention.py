@@ -97,7 +97,7 @@ def test_attention_decode_step_end_to_end():
 
 @pytest.mark.parametrize("B,H,Hkv,S_prev", [(1, 20, 5, 2047), (3, 20, 5, 127), (2, 16, 2, 128),
                                              (1, 8, 8, 0), (2, 32, 4, 300), (1, 20, 5, 1),
-                                             (1, 20, 5, 4100), (1, 20, 5, 9000)])
+                                             (1, 20, 5, 4100), (1, 20, 5, 9000), (8, 20, 5, 300)])
 def test_fused_rope_attention_is_bit_identical(B, H, Hkv, S_prev):
     """obn_attention_decode_rope == obn_rope_kv_append + obn_attention_decode (n = 1):
     same output bits, same cache contents."""

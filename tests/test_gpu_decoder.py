@@ -74,9 +74,9 @@ def host_caches(m, pos):
     return [(c.k[:, :pos + 1].cpu().numpy(), c.v[:, :pos + 1].cpu().numpy()) for c in m.caches]
 
 
-@pytest.mark.parametrize("B", [2, 6])
+@pytest.mark.parametrize("B", [1, 2, 6])
 def test_decoder_step_matches_oracle(B):
-    # B = 2: the shader-order LM head; B = 6: the tensor-core one
+    # B = 1: the shader-order LM head; B = 2, 6: the tensor-core one
     torch = need_cuda()
     D_ = dec()
     cfg = D_.DecoderConfig(layers=2, hidden=512, ffn=1024, heads=4, kv_heads=2, vocab=1000)
