@@ -274,7 +274,12 @@ OBN_API int obn_attention_decode_at(const float* q, const void* k_cache, const v
  * out [B, H * head_dim] is its attention over positions [0, pos]. Bit-identical to
  * obn_rope_kv_append followed by obn_attention_decode (n = 1) and one launch fewer.
  * Workspace: obn_attention_workspace_bytes(B, 1, H, head_dim, pos + 1), or with
- * S_max in place of pos + 1 for the _at form. */
+ * S_max in place of pos + 1 for the _at form (one and two sequences use none of it).
+ * The cache rows below pos - 1 are read while the kernel before this call may still
+ * run: the rows a decode sequence reads were appended by earlier calls (row pos - 1
+ * is read after that kernel ends). A caller that moves forward on one cache by more
+ * than one position must write the rows in between (obn_rope_kv_append or its own
+ * copy) before this call. */
 OBN_API int obn_attention_decode_rope(const float* qkv, void* k_cache, void* v_cache, int B, int H,
                                       int Hkv, int head_dim, int S_max, int pos, float theta_base,
                                       float scale, float* out, void* workspace,
