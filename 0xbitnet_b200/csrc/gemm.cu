@@ -33,6 +33,16 @@
 // Every mbarrier wait is bounded; on a timeout the CTA raises a shared abort
 // flag, every role leaves its loop, in-flight copies are waited for (bounded)
 // and TMEM is freed before exit.
+//
+// From 512 tokens the tiles are 256 weight rows x 256 tokens on a cluster of two
+// CTAs (PAIR, tcgen05 cta_group::2): each CTA copies and expands its own 128
+// rows and copies HALF of the token tile; the even CTA issues the 256-row MMAs,
+// which read the other CTA's token half through the pair, and each CTA's TMEM
+// gets its 128 accumulator rows. The single-CTA form re-reads every token tile
+// from L2 once per 128 rows, and at 8192 tokens that L2 -> SM stream
+// (~10 TB/s) is what held the MMA back. The odd CTA announces its codes and its
+// drained accumulators with relaxed remote arrivals; the even CTA's commits
+// reach both CTAs' barriers (multicast to the pair, no TMA multicast).
 #include <cuda.h>
 
 #include <cstdlib>
@@ -70,6 +80,110 @@ constexpr uint32_t idesc_i8() {
          (static_cast<uint32_t>(kBM >> 4) << 24);
 }
 
+// ---- pieces of the paired (cta_group::2) many-token GEMM ---------------------------
+// Two CTAs of a cluster share one MMA of 256 weight rows x BN tokens: each holds
+// its 128 rows of codes and half of the token tile (BN / 2 rows) in shared
+// memory, the even CTA issues the MMAs, and each CTA's TMEM receives its 128 rows
+// of the accumulator. Every token row then crosses L2 -> SM once per 256 weight
+// rows instead of once per 128.
+template <int BN>
+constexpr uint32_t idesc_i8_pair() {  // as idesc_i8, M = 256
+  return (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+         (static_cast<uint32_t>((2 * kBM) >> 4) << 24);
+}
+OBN_DEVINL uint32_t pair_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+OBN_DEVINL uint32_t pair_map(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+// Arrive on an mbarrier of another CTA of the cluster (cluster address), without
+// release semantics: callers order what the arrival announces themselves.
+OBN_DEVINL void arrive_cluster_relaxed(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+OBN_DEVINL void pair_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+OBN_DEVINL void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+OBN_DEVINL void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+OBN_DEVINL void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+OBN_DEVINL void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrives on `bar` (same offset) in both CTAs of the pair once every tcgen05
+// operation issued so far by this thread has completed.
+OBN_DEVINL void commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(static_cast<unsigned short>(3))
+      : "memory");
+}
+// wait_or_abort with cluster-scope acquire (arrivals from the other CTA).
+template <class Smem>
+OBN_DEVINL bool wait_or_abort_cl(Smem* sm, uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((i & 1023u) == 1023u && sm->abort_flag) return false;
+  }
+  record_error(DEVERR_MBAR_TIMEOUT);
+  sm->abort_flag = 1;
+  return false;
+}
+OBN_DEVINL bool mbar_wait_cl(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  record_error(DEVERR_MBAR_TIMEOUT);
+  return false;
+}
+template <bool PAIR, class Smem>
+OBN_DEVINL bool wait_x(Smem* sm, uint64_t* bar, uint32_t parity) {
+  if constexpr (PAIR)
+    return wait_or_abort_cl(sm, bar, parity);
+  else
+    return wait_or_abort(sm, bar, parity);
+}
+
 // Output modes of k_gemm: the plain [N][M] output, or a tensor-parallel gather
 // that writes this rank's columns of every rank's [N][ldy] output as it goes.
 enum : int { kOutLocal = 0, kOutMulticast = 1, kOutPeers = 2 };
@@ -89,7 +203,7 @@ OBN_DEVINL void multimem_st_v4(float* addr, float4 v) {
 // rows] f32 block, so each thread can store 4 consecutive rows of one token.
 constexpr int kGatherStageBytes = 4 * 16 * 32 * 4;
 
-template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal>
+template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal, bool PAIR = false>
 __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CUtensorMap tmap_q,
                                                       const __grid_constant__ CUtensorMap tmap_w,
                                                       const float* __restrict__ s_w,
@@ -99,12 +213,18 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                                                       int32_t* __restrict__ acc_out, int M, int N,
                                                       int K, int order, const GatherOut go) {
   constexpr int kAStage = KSTG * kBM * kBK;      // expanded A bytes per stage (smem variant)
-  constexpr int kBStage = KSTG * BN * kBK;       // activation bytes per stage
+  // PAIR: a cluster of 2 CTAs shares each 256-row x BN-token tile (cta_group::2);
+  // this CTA holds rows [128 rank, 128 rank + 128) and tokens [BN/2 rank, +BN/2).
+  static_assert(!PAIR || (OUT == kOutLocal && !A_TMEM && KSTG == 1),
+                "paired tiles: local output, codes in shared memory");
+  constexpr int kBRows = PAIR ? BN / 2 : BN;     // token rows of B in this CTA
+  constexpr int kBStage = KSTG * kBRows * kBK;   // activation bytes per stage
   constexpr int kPStage = KSTG * kPackedBlock;   // packed weight bytes per stage
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles.
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
+  static_assert(STAGES <= 8, "stage count");
   uint8_t* sA = base;                                  // STAGES x kAStage (A in shared memory)
   uint8_t* sB = sA + (A_TMEM ? 0 : STAGES * kAStage);  // STAGES x kBStage
   uint8_t* sP = sB + STAGES * kBStage;                 // STAGES x kPStage
@@ -115,9 +235,12 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int KB = K / kBK;
   const int n_stages = (KB + KSTG - 1) / KSTG;  // a missing last block is zero-filled by TMA
-  const int num_m = (M + kBM - 1) / kBM;
+  const int num_m = (M + (PAIR ? 2 : 1) * kBM - 1) / ((PAIR ? 2 : 1) * kBM);  // (paired) row tiles
   const int num_n = (N + BN - 1) / BN;
   const int tiles = num_m * num_n;
+  const uint32_t crank = PAIR ? pair_rank() : 0u;  // 0: issues the pair's MMAs
+  const int t0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int tstep = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   // TMEM columns: two BN-wide accumulators, then (A_TMEM) 32 columns per block per stage.
   constexpr uint32_t kTmemNeed = 2 * BN + (A_TMEM ? 32 * KSTG * STAGES : 0);
   constexpr uint32_t kTmemCols = kTmemNeed <= 32 ? 32 : kTmemNeed <= 64 ? 64 : kTmemNeed <= 128 ? 128
@@ -127,23 +250,29 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&sm->full_tma[s], 1);
-      mbar_init(&sm->full_a[s], 4);  // one arrival per expansion warp
+      mbar_init(&sm->full_a[s], PAIR ? 8 : 4);  // one arrival per expansion warp (both CTAs)
       mbar_init(&sm->empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&sm->accf[a], 1);
-      mbar_init(&sm->acce[a], 4);  // one arrival per epilogue warp
+      mbar_init(&sm->acce[a], PAIR ? 8 : 4);  // one arrival per epilogue warp (both CTAs)
     }
     mbar_init(&sm->drain, 1);
     sm->abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 2) {
-    tmem_alloc(&sm->tmem_base, kTmemCols);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(&sm->tmem_base, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&sm->tmem_base, kTmemCols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) pair_sync();  // both CTAs' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem = sm->tmem_base;
   pdl_launch_dependents();
@@ -157,19 +286,20 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
     }
     int it = 0;
     bool waited = false;
-    for (int t = blockIdx.x; t < tiles && !sm->abort_flag; t += gridDim.x) {
+    for (int t = t0; t < tiles && !sm->abort_flag; t += tstep) {
       const int mt = t % num_m, nt = t / num_m;
+      const int rowtile = PAIR ? 2 * mt + static_cast<int>(crank) : mt;
       bool ok = true;
       for (int st = 0; st < n_stages; ++st, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1u;
-        if (!wait_or_abort(sm, &sm->empty[s], ph ^ 1u)) {
+        if (!wait_x<PAIR>(sm, &sm->empty[s], ph ^ 1u)) {
           ok = false;
           break;
         }
         if (lane == 0) {
           mbar_arrive_expect_tx(&sm->full_tma[s], kBStage + kPStage);
-          tma_load_3d(sP + s * kPStage, &tmap_w, 0, st * KSTG, mt * (kBM / kSubRows),
+          tma_load_3d(sP + s * kPStage, &tmap_w, 0, st * KSTG, rowtile * (kBM / kSubRows),
                       &sm->full_tma[s]);
         }
         if (!waited) {  // q comes from the previous kernel; the weights do not
@@ -177,7 +307,8 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
           waited = true;
         }
         if (lane == 0)
-          tma_load_3d(sB + s * kBStage, &tmap_q, 0, nt * BN, st * KSTG, &sm->full_tma[s]);
+          tma_load_3d(sB + s * kBStage, &tmap_q, 0, nt * BN + static_cast<int>(crank) * kBRows,
+                      st * KSTG, &sm->full_tma[s]);
         __syncwarp();
       }
       if (!ok) break;
@@ -193,11 +324,12 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
     // Converged warp; one lane issues the MMAs and commits.
     pdl_wait();
     int it = 0, ti = 0;
-    constexpr uint32_t idesc = idesc_i8<BN>();
-    for (int t = blockIdx.x; t < tiles && !sm->abort_flag; t += gridDim.x, ++ti) {
+    constexpr uint32_t idesc = PAIR ? idesc_i8_pair<BN>() : idesc_i8<BN>();
+    // PAIR: the odd CTA's MMA warp issues nothing (its rows are in the even CTA's MMAs)
+    for (int t = t0; t < tiles && !sm->abort_flag && (!PAIR || crank == 0); t += tstep, ++ti) {
       const int a = ti & 1;
       const uint32_t aph = (ti >> 1) & 1u;
-      if (!wait_or_abort(sm, &sm->acce[a], aph ^ 1u)) break;
+      if (!wait_x<PAIR>(sm, &sm->acce[a], aph ^ 1u)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem + a * BN;
       bool ok = true;
@@ -206,7 +338,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
         const uint32_t ph = (it / STAGES) & 1u;
         // full_a implies full_tma: the expansion warps arrive only after waiting
         // for this stage's TMA bytes (weights and activations share the barrier).
-        if (!wait_or_abort(sm, &sm->full_a[s], ph)) {
+        if (!wait_x<PAIR>(sm, &sm->full_a[s], ph)) {
           ok = false;
           break;
         }
@@ -225,33 +357,51 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                           bdesc0 + static_cast<uint64_t>((bb * BN * kBK + kk * 32) >> 4), idesc,
                           (st > 0 || bb > 0 || kk > 0) ? 1u : 0u);
             } else {
-              const uint32_t b_addr = smem_u32(sB + s * kBStage + bb * BN * kBK);
+              const uint32_t b_addr = smem_u32(sB + s * kBStage + bb * kBRows * kBK);
               const uint32_t a_addr = smem_u32(sA + s * kAStage + bb * kBM * kBK);
 #pragma unroll
               for (int kk = 0; kk < kBK / 32; ++kk)
-                mma_i8(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
-                       (st > 0 || bb > 0 || kk > 0) ? 1u : 0u);
+                if constexpr (PAIR)
+                  mma_i8_pair(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32),
+                              idesc, (st > 0 || bb > 0 || kk > 0) ? 1u : 0u);
+                else
+                  mma_i8(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
+                         (st > 0 || bb > 0 || kk > 0) ? 1u : 0u);
             }
           }
-          mma_commit(&sm->empty[s]);
+          if constexpr (PAIR)
+            commit_pair(&sm->empty[s]);  // both CTAs' copy stages are free again
+          else
+            mma_commit(&sm->empty[s]);
         }
         __syncwarp();
       }
       if (!ok) break;
-      if (lane == 0) mma_commit(&sm->accf[a]);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          commit_pair(&sm->accf[a]);
+        else
+          mma_commit(&sm->accf[a]);
+      }
       __syncwarp();
     }
     // Every MMA issued by this warp must finish before TMEM is released.
-    if (lane == 0) mma_commit(&sm->drain);
-    __syncwarp();
-    mbar_wait(&sm->drain, 0);
+    if constexpr (PAIR) {
+      if (lane == 0 && crank == 0) commit_pair(&sm->drain);
+      __syncwarp();
+      mbar_wait_cl(&sm->drain, 0);
+    } else {
+      if (lane == 0) mma_commit(&sm->drain);
+      __syncwarp();
+      mbar_wait(&sm->drain, 0);
+    }
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ expansion
     pdl_wait();
     const int r = tid - 128;  // weight row within the tile = TMEM lane
     const int sub = r >> 4, rr = r & 15;
     int it = 0;
-    for (int t = blockIdx.x; t < tiles && !sm->abort_flag; t += gridDim.x) {
+    for (int t = t0; t < tiles && !sm->abort_flag; t += tstep) {
       bool ok = true;
       for (int st = 0; st < n_stages; ++st, ++it) {
         const int s = it % STAGES;
@@ -309,7 +459,18 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
           fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm->full_a[s]);
+        // PAIR: the even CTA's MMAs make each CTA's tensor core read its own
+        // codes, so the odd CTA only has to tell the even one that its codes are
+        // in place: a relaxed arrival, issued after this warp's writes were made
+        // visible to the async proxy by the (blocking) fence above. A release at
+        // cluster scope would order nothing more here and stalls the thread for
+        // ~1.5 k cycles while the SM's global stores drain.
+        if (lane == 0) {
+          if (PAIR && crank == 1)
+            arrive_cluster_relaxed(pair_map(smem_u32(&sm->full_a[s]), 0));
+          else
+            mbar_arrive(&sm->full_a[s]);
+        }
       }
       if (!ok) break;
     }
@@ -318,11 +479,12 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
     pdl_wait();
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     int ti = 0;
-    for (int t = blockIdx.x; t < tiles && !sm->abort_flag; t += gridDim.x, ++ti) {
+    for (int t = t0; t < tiles && !sm->abort_flag; t += tstep, ++ti) {
       const int mt = t % num_m, nt = t / num_m;
+      const int rowtile = PAIR ? 2 * mt + static_cast<int>(crank) : mt;
       const int a = ti & 1;
       const uint32_t aph = (ti >> 1) & 1u;
-      const int m = mt * kBM + quarter * 32 + lane;
+      const int m = rowtile * kBM + quarter * 32 + lane;
       if constexpr (OUT == kOutLocal) {
         // The tile's per-token code sums and scales are kernel inputs: load them
         // before waiting for the accumulator, lane l holding columns l, l + 32, ...
@@ -338,7 +500,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
           sxr[c] = (nl < N && !acc_out) ? s_x[nl] : 0.0f;
         }
         const float sw = (m < M && !acc_out) ? s_w[m] : 0.0f;
-        if (!wait_or_abort(sm, &sm->accf[a], aph)) break;
+        if (!wait_x<PAIR>(sm, &sm->accf[a], aph)) break;
         tc_fence_after();
         const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
         // Five store kinds, chosen once per tile so the plain store never carries
@@ -352,7 +514,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                                                     : 1;
         const bool gemv_order = (order & 1) == kOrderGemv;
         const size_t Mh = static_cast<size_t>(M) >> 1;
-        const bool full_tile = (nt + 1) * BN <= N && (mt + 1) * kBM <= M;
+        const bool full_tile = (nt + 1) * BN <= N && (rowtile + 1) * kBM <= M;
         auto chunk = [&](auto kind_c) {
           constexpr int K_ = decltype(kind_c)::value;
           if constexpr (K_ >= 3) {
@@ -530,7 +692,12 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
           chunk(std::integral_constant<int, 4>());
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sm->acce[a]);
+        if (lane == 0) {  // PAIR: the even CTA reuses the pair's accumulator
+          if (PAIR && crank == 1)  // the TMEM reads above completed (tcgen05.wait::ld)
+            arrive_cluster_relaxed(pair_map(smem_u32(&sm->acce[a]), 0));
+          else
+            mbar_arrive(&sm->acce[a]);
+        }
         continue;
       }
       if (!wait_or_abort(sm, &sm->accf[a], aph)) break;
@@ -622,8 +789,16 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
 
   tc_fence_before();
   __syncthreads();
+  // PAIR: no CTA leaves (or frees TMEM) while the other may still arrive on its
+  // barriers or its MMAs may still read this CTA's shared memory.
+  if constexpr (PAIR) pair_sync();
   tc_fence_after();
-  if (warp == 2) tmem_dealloc(tmem, kTmemCols);
+  if (warp == 2) {
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, kTmemCols);
+    else
+      tmem_dealloc(tmem, kTmemCols);
+  }
 }
 
 // ---- split-K over a thread-block cluster ---------------------------------------------
@@ -1098,11 +1273,11 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
 // ---- host side ------------------------------------------------------------------
 EncodeTiledFn encode_fn() { return tensor_map_encoder(); }
 
-template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal>
+template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal, bool PAIR = false>
 size_t gemm_smem_bytes() {
   return 1024 +
-         static_cast<size_t>(STAGES) *
-             ((A_TMEM ? 0 : KSTG * kBM * kBK) + KSTG * BN * kBK + KSTG * kPackedBlock) +
+         static_cast<size_t>(STAGES) * ((A_TMEM ? 0 : KSTG * kBM * kBK) +
+                                        KSTG * (PAIR ? BN / 2 : BN) * kBK + KSTG * kPackedBlock) +
          sizeof(GemmSmem) + (OUT == kOutLocal ? 0 : 16 + kGatherStageBytes);
 }
 
@@ -1149,16 +1324,16 @@ bool make_w_map(CUtensorMap* map, const WeightView& W, int KSTG) {
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal>
+template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal, bool PAIR = false>
 cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, const int32_t* qsum,
                     int n, float* y, int32_t* acc, int order, cudaStream_t s,
                     const GatherOut& go = GatherOut{}) {
   if (!encode_fn()) return cudaErrorNotSupported;
   CUtensorMap qmap, wmap;
-  if (!make_q_map(&qmap, q, n, W.in_dim, BN, KSTG) || !make_w_map(&wmap, W, KSTG))
+  if (!make_q_map(&qmap, q, n, W.in_dim, PAIR ? BN / 2 : BN, KSTG) || !make_w_map(&wmap, W, KSTG))
     return cudaErrorInvalidValue;
-  const size_t smem = gemm_smem_bytes<BN, STAGES, KSTG, A_TMEM, OUT>();
-  auto kern = k_gemm<BN, STAGES, KSTG, A_TMEM, OUT>;
+  const size_t smem = gemm_smem_bytes<BN, STAGES, KSTG, A_TMEM, OUT, PAIR>();
+  auto kern = k_gemm<BN, STAGES, KSTG, A_TMEM, OUT, PAIR>;
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1168,18 +1343,25 @@ cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, cons
     if (e != cudaSuccess) return e;
     configured[dev] = 1;
   }
-  const int tiles = ((W.out_dim + kBM - 1) / kBM) * ((n + BN - 1) / BN);
-  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const int rows = PAIR ? 2 * kBM : kBM;
+  const int tiles = ((W.out_dim + rows - 1) / rows) * ((n + BN - 1) / BN);
+  // PAIR: clusters of 2 CTAs, one pair per tile (an even grid)
+  const int cap = PAIR ? (num_sms() & ~1) : num_sms();
+  const int grid = (PAIR ? 2 * tiles : tiles) < cap ? (PAIR ? 2 * tiles : tiles) : cap;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = PAIR ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, qmap, wmap, W.s_w, s_x, qsum, y, acc, W.out_dim, n,
                             W.in_dim, order, go);
 }
@@ -1303,6 +1485,17 @@ bool gemm_supported(const WeightView& W, int n) {
   return split_k_factor<16>(W) > 1 || 2 * (W.m_pad / kBM) > num_sms();
 }
 
+// The paired (cta_group::2) tiles for many tokens; OBN_GEMM_PAIR=0 turns them
+// off (read once per process).
+constexpr int kPairMinTokens = 512;
+bool pair_tiles_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("OBN_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 cudaError_t launch_gemm(const WeightView& W, const int8_t* q, const float* s_x,
                         const int32_t* qsum, int n, float* y, int32_t* acc, int order,
                         cudaStream_t s) {
@@ -1321,6 +1514,10 @@ cudaError_t launch_gemm(const WeightView& W, const int8_t* q, const float* s_x,
   if (n <= 32) return gemm_bn<32, 3, 4, true>(W, q, s_x, qsum, n, y, acc, order, s);
   if (n <= 64) return gemm_bn<64, 3, 4, true>(W, q, s_x, qsum, n, y, acc, order, s);
   if (n <= 128) return gemm_bn<128, 4, 2, true>(W, q, s_x, qsum, n, y, acc, order, s);
+  // From 512 tokens: 256-row tiles on CTA pairs (cta_group::2), each CTA loading
+  // half of the token tile; below, the single-CTA 256-token tile.
+  if (n >= kPairMinTokens && pair_tiles_enabled())
+    return gemm_bn<256, 6, 1, false, kOutLocal, true>(W, q, s_x, qsum, n, y, acc, order, s);
   return gemm_bn<256, 4, 1, false>(W, q, s_x, qsum, n, y, acc, order, s);
 }
 

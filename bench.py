@@ -1075,6 +1075,13 @@ def run_case(spec: str):
         obn.check_device_errors()
         print(f"case quant B={B}: ok")
         return
+    if name == "prefill":  # the config-2 block alone at B tokens
+        import types
+        dev = torch.device("cuda", 0)
+        res = measure_prefill(types.SimpleNamespace(prefill=str(B)), obn, synth, dev,
+                              torch.cuda.Stream(dev))
+        print(json.dumps({"prefill": res}), flush=True)
+        return
     if name in ("attndec", "decoder"):  # the full-run blocks alone: B = layers / context
         dev = torch.device("cuda", 0)
         stream = torch.cuda.Stream(dev)

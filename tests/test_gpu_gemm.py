@@ -38,7 +38,8 @@ def test_gemm_small_exact(torch, M, K, n):
 
 @pytest.mark.parametrize("M,K,n", [(1, 128, 16), (100, 256, 17), (129, 128, 33), (300, 384, 100),
                                    (513, 640, 129), (1000, 256, 257), (2560, 2560, 64),
-                                   (6912, 2560, 32), (2560, 6912, 64), (3840, 2560, 300)])
+                                   (6912, 2560, 32), (2560, 6912, 64), (3840, 2560, 300),
+                                   (128, 256, 200), (129, 128, 300), (384, 640, 513)])
 def test_gemm_acc_bitexact(torch, M, K, n):
     got, want = run_acc(torch, M, K, n, M * 3 + K + n)
     assert np.array_equal(got, want)
