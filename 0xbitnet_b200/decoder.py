@@ -21,7 +21,7 @@ merged 3840-row BitLinear with a per-row scale table, gate and up are one
 interleaved gated layer, and the KV cache is fp16; small batches rotate q and
 append k/v inside the attention pass (one launch fewer). Every step is a fixed
 sequence of libobn launches on one stream, so it is captured as a CUDA graph.
-Batches above 4 tokens take the tensor-core LM head (f16 hi/lo split, f32
+Two or more sequences take the tensor-core LM head (f16 hi/lo split, f32
 accumulation) instead of the shader-order one. Weights are random (seeded)
 with the reference's distributions; no checkpoint is needed to measure speed.
 """
@@ -34,7 +34,8 @@ import torch
 
 from . import attention as att
 from ._lib import check, lib
-from .bitlinear import BitLinear, lm_head_f16, lm_head_f16_batched
+from .bitlinear import BitLinear, lm_head_f16, lm_head_f16_batched, rmsnorm
+from .diagnose import stage_stats
 
 
 # Batches up to this size take the fused RoPE + attention pass (one launch fewer);
@@ -175,31 +176,65 @@ class BitNetDecoder:
             c.v[:, :seq_len].normal_(generator=g)
             c.seq_len = seq_len
 
-    def step(self, pos: int) -> torch.Tensor:
-        """Enqueues one decode step for the tokens in self.ids at position `pos`
-        (every cache holds pos positions before it); returns logits [B, vocab]."""
-        cfg, B, dev = self.cfg, self.B, self.device
-        D, H = cfg.hidden, cfg.heads
-        s = _stream(dev)
-        check(lib().obn_embed_f16(_ptr(self.embed), cfg.vocab, D, _ptr(self.ids), B,
-                                  _ptr(self.x), s))
-        for L, c in zip(self.layers, self.caches):
-            L.qkv.forward(self.x, n=B, out=self.qkv_out)
-            if B <= FUSED_ROPE_MAX_BATCH:  # RoPE + KV append + attention in one pass
-                att.attention_rope(self.qkv_out, c, H, pos, cfg.rope_theta, out=self.attn,
-                                   workspace=self.attn_ws)
-            else:  # every split CTA would rotate its q heads again: rotate once first
-                att.rope_kv_append(self.qkv_out, c, H, 1, cfg.rope_theta, q_out=self.q, pos=pos)
-                att.attention(self.q, c, H, 1, pos + 1, out=self.attn, workspace=self.attn_ws)
-            L.o.forward_residual(self.attn, self.x, n=B)  # x += o_proj(attn)
-            L.gate_up.forward(self.x, n=B, out=self.ffn_out)
-            L.down.forward_residual(self.ffn_out, self.x, n=B)  # x += down(ffn)
-        if B == 1:  # the shader's exact order (the reference's own case is one token)
+    def _embed(self, s) -> None:
+        cfg = self.cfg
+        check(lib().obn_embed_f16(_ptr(self.embed), cfg.vocab, cfg.hidden, _ptr(self.ids),
+                                  self.B, _ptr(self.x), s))
+
+    def _layer(self, L, c, pos: int) -> None:
+        """One transformer block on self.x in place (transformer.rs:51-72)."""
+        cfg, B, H = self.cfg, self.B, self.cfg.heads
+        L.qkv.forward(self.x, n=B, out=self.qkv_out)
+        if B <= FUSED_ROPE_MAX_BATCH:  # RoPE + KV append + attention in one pass
+            att.attention_rope(self.qkv_out, c, H, pos, cfg.rope_theta, out=self.attn,
+                               workspace=self.attn_ws)
+        else:  # every split CTA would rotate its q heads again: rotate once first
+            att.rope_kv_append(self.qkv_out, c, H, 1, cfg.rope_theta, q_out=self.q, pos=pos)
+            att.attention(self.q, c, H, 1, pos + 1, out=self.attn, workspace=self.attn_ws)
+        L.o.forward_residual(self.attn, self.x, n=B)  # x += o_proj(attn)
+        L.gate_up.forward(self.x, n=B, out=self.ffn_out)
+        L.down.forward_residual(self.ffn_out, self.x, n=B)  # x += down(ffn)
+
+    def _lm_head(self) -> torch.Tensor:
+        cfg = self.cfg
+        if self.B == 1:  # the shader's exact order (the reference's own case is one token)
             return lm_head_f16(self.embed, self.x, self.final_norm, cfg.eps)
         # two or more tokens: the tensor-core head reads the table once for all of
         # them (the exact-order kernel is bound by its unfused f32 products there)
         return lm_head_f16_batched(self.embed, self.x, self.final_norm, cfg.eps,
                                    out=self.logits, workspace=self.lm_ws)
+
+    def step(self, pos: int) -> torch.Tensor:
+        """Enqueues one decode step for the tokens in self.ids at position `pos`
+        (every cache holds pos positions before it); returns logits [B, vocab]."""
+        self._embed(_stream(self.device))
+        for L, c in zip(self.layers, self.caches):
+            self._layer(L, c, pos)
+        return self._lm_head()
+
+    def diagnose(self, pos: int) -> list[dict]:
+        """The decode step of `step(pos)`, stage by stage, with the reference's
+        diagnostic statistics of each stage (model.ts:449-531): the embedding, the
+        hidden state after layers 0 and 1 and after the last layer, the final
+        RMSNorm, the LM-head input (every sequence's row: one token each) and the
+        first 100 logits of sequence 0. Synchronises after every stage; the caches
+        take the step's k / v as `step` would."""
+        cfg = self.cfg
+        host = lambda t: t.detach().float().cpu().numpy()
+        out = []
+        self._embed(_stream(self.device))
+        out.append(stage_stats("embedding", host(self.x)))
+        for i, (L, c) in enumerate(zip(self.layers, self.caches)):
+            self._layer(L, c, pos)
+            if i < 2:
+                out.append(stage_stats(f"layer_{i}", host(self.x)))
+        out.append(stage_stats("last_layer", host(self.x)))
+        normed = host(rmsnorm(self.x, self.final_norm, cfg.eps))
+        out.append(stage_stats("final_norm", normed))
+        out.append(stage_stats("lm_input", normed))
+        logits = self._lm_head()
+        out.append(stage_stats("logits_first100", host(logits[0, :100])))
+        return out
 
     def close(self) -> None:
         for L in self.layers:

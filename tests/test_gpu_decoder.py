@@ -29,13 +29,17 @@ def dec():
     return importlib.import_module("0xbitnet_b200.decoder")
 
 
-def oracle_logits(m, ids, caches, pos):
-    """The reference forward for one new token per sequence at position `pos`."""
+def oracle_logits(m, ids, caches, pos, stages=None):
+    """The reference forward for one new token per sequence at position `pos`.
+    `stages` (a dict), when given, receives the arrays of the reference's
+    diagnose() stages (model.ts:449-531)."""
     cfg, B = m.cfg, len(ids)
     H, Hkv, d, D, F = cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.hidden, cfg.ffn
     emb = m.embed.cpu().numpy()
     x = emb[ids].astype(np.float32)
-    for L, (kc, vc) in zip(m.layers, caches):
+    if stages is not None:
+        stages["embedding"] = x.copy()
+    for li, (L, (kc, vc)) in enumerate(zip(m.layers, caches)):
         src = L.source
         sw = np.concatenate([np.full(n_, s_, np.float32) for n_, s_ in
                              zip((H * d, Hkv * d, Hkv * d), L.qkv_scales)])
@@ -66,7 +70,14 @@ def oracle_logits(m, ids, caches, pos):
         dn = orc.bitlinear_omp(act, src["down"], np.full(D, L.down_scale, np.float32), D, F,
                                norm_w=L.ffn_sub_norm.cpu().numpy(), eps=cfg.eps)
         x = (x + dn).astype(np.float32)
-    return orc.lm_head_f16(x, emb, m.final_norm.cpu().numpy(), cfg.eps)
+        if stages is not None and li < 2:
+            stages[f"layer_{li}"] = x.copy()
+    logits = orc.lm_head_f16(x, emb, m.final_norm.cpu().numpy(), cfg.eps)
+    if stages is not None:
+        normed = orc.rmsnorm(x, m.final_norm.cpu().numpy(), cfg.eps)
+        stages.update(last_layer=x.copy(), final_norm=normed, lm_input=normed,
+                      logits_first100=logits[0, :100])
+    return logits
 
 
 def host_caches(m, pos):
@@ -122,4 +133,32 @@ def test_decoder_config3_dims_graph_matches_oracle(B):
     assert np.isfinite(logits).all()
     err = np.abs(logits - want).max()
     assert err <= 2e-2, err
+    m.close()
+
+
+def test_decoder_diagnose_stages_match_oracle():
+    """BitNetDecoder.diagnose (the reference's diagnose() stages and statistics)
+    against the same stages of the oracle composition; a fault planted in one
+    oracle stage's statistics is reported at that stage."""
+    import importlib
+    torch = need_cuda()
+    D_ = dec()
+    dg = importlib.import_module("0xbitnet_b200.diagnose")
+    cfg = D_.DecoderConfig(layers=3, hidden=512, ffn=1024, heads=4, kv_heads=2, vocab=1000)
+    ctx, pos, ids = 64, 10, [3, 777]
+    m = D_.BitNetDecoder(cfg, len(ids), ctx, seed=5, keep_source=True)
+    m.fill_caches(pos, seed=6)
+    m.ids.copy_(torch.tensor(ids, dtype=torch.int32))
+    caches = host_caches(m, pos)
+    got = m.diagnose(pos)
+    stages = {}
+    oracle_logits(m, ids, caches, pos, stages=stages)
+    want = [dg.stage_stats(n, stages[n]) for n in dg.STAGES]
+    assert [s["name"] for s in got] == list(dg.STAGES)
+    assert all(s["nan_count"] == 0 and s["inf_count"] == 0 for s in got)
+    msg = dg.format_stats(got) + "\n-- oracle --\n" + dg.format_stats(want)
+    assert dg.first_divergence(got, want, rtol=1e-2, atol=1e-3) is None, msg
+    bad = [dict(s) for s in want]
+    bad[2]["rms"] *= 1.1  # layer_1
+    assert dg.first_divergence(got, bad, rtol=1e-2, atol=1e-3) == "layer_1"
     m.close()
