@@ -15,7 +15,8 @@ value  = algorithmic bytes of the step / device time (GB/s, summed over ranks);
          bytes per forward = M*K/4 + B*K*4 + K*4 + B*M*4 + 4.
 e2e    = the same through host buffers: per step one H2D copy of all inputs
          from pinned memory and one D2H copy of all outputs, timed with the
-         graph replays.
+         graph replays (double-buffered on a copy stream, so a step's copies
+         overlap its neighbours' kernels).
 Multi-GPU (torchrun): independent decode sequences per GPU, full weight
 replicas, no collective on the data path (weak scaling); the max over ranks
 of the device time is reported.
@@ -814,21 +815,36 @@ def run_ours(args):
             xo += B * K
             yo += B * M
 
+    def views(xf, yf):
+        vx, vy = {}, {}
+        xo = yo = 0
+        for B in batches:
+            for i, (name, (M, K)) in enumerate(shp):
+                vx[B, i] = xf[xo:xo + B * K].view(B, K)
+                vy[B, i] = yf[yo:yo + B * M].view(B, M)
+                xo += B * K
+                yo += B * M
+        return vx, vy
+
+    def capture(vx, vy):
+        gs = {}
+        for B in batches:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for row in layers:
+                    for i, L in enumerate(row):
+                        L.forward(vx[B, i], out=vy[B, i])
+            gs[B] = g
+        return gs
+
     stream = torch.cuda.Stream(device=dev)
-    graphs = {}
     with torch.cuda.stream(stream):
         for B in batches:  # eager warm-up allocates every layer's workspace
             for row in layers:
                 for i, L in enumerate(row):
                     L.forward(xs[B, i], out=ys[B, i])
         stream.synchronize()
-        for B in batches:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                for row in layers:
-                    for i, L in enumerate(row):
-                        L.forward(xs[B, i], out=ys[B, i])
-            graphs[B] = g
+        graphs = capture(xs, ys)
     torch.cuda.synchronize()
     obn.check_device_errors()
 
@@ -836,11 +852,12 @@ def run_ours(args):
     # B = 1: one fused kernel per forward; B > 1: RMSNorm+quantize, then the matmul.
     launches_per_step = sum(1 if B == 1 else 2 for B in batches) * args.layers * len(shp)
 
-    def step(evs=None):
+    def step(evs=None, gs=None):
+        gs = graphs if gs is None else gs
         for j, B in enumerate(batches):
             if evs is not None:
                 evs[j][0].record(stream)
-            graphs[B].replay()
+            gs[B].replay()
             if evs is not None:
                 evs[j][1].record(stream)
 
@@ -874,27 +891,67 @@ def run_ours(args):
     bytes_all = world * args.steps * sum(step_bytes.values())
     value = bytes_all / (total_ms_max / 1e3) / 1e9
 
-    # e2e: pinned host inputs -> device, graphs, device -> pinned host outputs, every step.
+    # e2e: every step copies its inputs from pinned host memory to the device and
+    # its outputs back, as a serving loop would: two sets of device buffers (one
+    # graph set each) and a copy stream, so step k's H2D overlaps step k-1's
+    # kernels and its D2H overlaps step k+1's. The timed region runs from before
+    # the first H2D to after the last D2H.
     x_host = torch.empty(x_total, dtype=torch.float32, pin_memory=True)
     x_host.copy_(x_flat.cpu())
-    y_host = torch.empty(y_total, dtype=torch.float32, pin_memory=True)
+    y_host = [torch.empty(y_total, dtype=torch.float32, pin_memory=True) for _ in range(2)]
+    x_dev = [x_flat, torch.empty_like(x_flat)]
+    y_dev = [y_flat, torch.empty_like(y_flat)]
     with torch.cuda.stream(stream):
-        for _ in range(max(1, args.warmup)):
-            x_flat.copy_(x_host, non_blocking=True)
-            step()
-            y_host.copy_(y_flat, non_blocking=True)
+        graph_sets = [graphs, capture(*views(x_dev[1], y_dev[1]))]
+    torch.cuda.synchronize()
+    h2d = torch.cuda.Stream(device=dev)  # inputs in, one stream per direction so a
+    d2h = torch.cuda.Stream(device=dev)  # step's outputs never queue before the next inputs
+
+    def e2e_steps(count):
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_done = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
+        h2d.wait_stream(stream)
+        d2h.wait_stream(stream)
+
+        def load(k):
+            j = k & 1
+            with torch.cuda.stream(h2d):
+                if k >= 2:
+                    h2d.wait_event(ev_done[j])  # step k - 2 has read x_dev[j]
+                x_dev[j].copy_(x_host, non_blocking=True)
+                ev_in[j].record(h2d)
+
+        load(0)
+        for k in range(count):
+            j = k & 1
+            if k + 1 < count:
+                load(k + 1)  # overlaps step k's kernels
+            stream.wait_event(ev_in[j])
+            if k >= 2:
+                stream.wait_event(ev_out[j])  # step k - 2's outputs have left y_dev[j]
+            step(gs=graph_sets[j])
+            ev_done[j].record(stream)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(ev_done[j])
+                y_host[j].copy_(y_dev[j], non_blocking=True)  # overlaps step k + 1's kernels
+                ev_out[j].record(d2h)
+        for j in range(min(2, count)):
+            stream.wait_event(ev_out[j])
+
+    with torch.cuda.stream(stream):
+        e2e_steps(max(1, args.warmup))
         stream.synchronize()
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
-            x_flat.copy_(x_host, non_blocking=True)
-            step()
-            y_host.copy_(y_flat, non_blocking=True)
+        e2e_steps(args.steps)
         e1.record(stream)
         stream.synchronize()
         barrier()
+    if not torch.equal(y_host[(args.steps - 1) & 1], y_flat.cpu()):
+        raise RuntimeError("e2e outputs differ from the device-timed run's")
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     e2e_value = bytes_all / (e2e_ms / 1e3) / 1e9
 
@@ -1017,13 +1074,14 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "clocks": clock_info,
             "e2e": {"value": e2e_value, "unit": "GB/s",
-                    "h2d_bytes_per_step": x_total * 4, "d2h_bytes_per_step": y_total * 4},
+                    "h2d_bytes_per_step": x_total * 4, "d2h_bytes_per_step": y_total * 4,
+                    "copies": "double-buffered on H2D and D2H streams beside the kernels; "
+                              "outputs checked against the device-timed run"},
             "gpu_launches": launches_per_step * args.steps,
         }
         print(json.dumps(out), flush=True)
-    for g in graphs.values():
-        del g
-    graphs.clear()
+    for gs in graph_sets:
+        gs.clear()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
