@@ -392,13 +392,14 @@ constexpr int kVStride = kAttnHeadDim + 8;  // halves per smem V row (ldmatrix.t
 // The tensor-core contractions of one chunk, shared by the split pass and the
 // clustered decode pass. On entry sK / sV hold the chunk's keys and values
 // (rows >= cnt zero) and sQ the group's rotated q [G][D] (f32, visible to the
-// CTA). SPLIT_WAIT: K and V are still two cp.async groups in flight, K first;
-// otherwise every copy has landed. On exit o holds this thread's P.V fragments
+// CTA); wait_k() / wait_v() are called before the first read of K / V (the K and
+// V copies may still be in flight on entry). On exit o holds this thread's P.V fragments
 // (dims 32 warp + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1) and red_m / red_l
 // every warp's max and sum per head.
-template <int G, bool SPLIT_WAIT>
+template <int G, class WaitK, class WaitV>
 OBN_DEVINL void tc_chunk(const __half* sK, const __half* sV, const float* sQ, float* sP, int cnt,
-                         float scale, float (*red_m)[4], float (*red_l)[4], float (&o)[2][4]) {
+                         float scale, float (*red_m)[4], float (*red_l)[4], float (&o)[2][4],
+                         WaitK wait_k, WaitV wait_v) {
   constexpr int D = kAttnHeadDim;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int grp = lane >> 2, qd = lane & 3;
@@ -414,7 +415,7 @@ OBN_DEVINL void tc_chunk(const __half* sK, const __half* sV, const float* sQ, fl
       qh[ks][0] = qh[ks][1] = ql[ks][0] = ql[ks][1] = 0u;
     }
   }
-  if constexpr (SPLIT_WAIT) cp_async_wait_group<1>();  // K landed
+  wait_k();
   __syncthreads();
   // Scores: warp w, keys 32w + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1.
   float sc[2][4];
@@ -474,7 +475,7 @@ OBN_DEVINL void tc_chunk(const __half* sK, const __half* sV, const float* sQ, fl
     red_l[2 * qd][warp] = ls[0];
     red_l[2 * qd + 1][warp] = ls[1];
   }
-  if constexpr (SPLIT_WAIT) cp_async_wait_group<0>();  // V landed
+  wait_v();
   __syncthreads();
   // P.V: warp w, dims 32w + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1.
 #pragma unroll
@@ -518,6 +519,13 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split_tc(
   float* sQ = reinterpret_cast<float*>(sV + C * kVStride);      // [G][D] rotated q (f32)
   float* sP = sQ + G * D;                                       // [C][G] probabilities
   __shared__ float red_m[8][4], red_l[8][4];
+  __shared__ __align__(8) uint64_t bar_kv[2];  // K rows, V rows
+  if (threadIdx.x == 0) {
+    mbar_init(&bar_kv[0], 1);
+    mbar_init(&bar_kv[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
   pdl_order<ROPE>();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int grp = lane >> 2, qd = lane & 3;  // MMA fragment coordinates
@@ -546,29 +554,26 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split_tc(
   }
   const int p_new = ROPE ? (pos_dev ? *pos_dev : seq_len - 1) : 0;
   const int new_row = (ROPE && p_new < S_max && p_new >= s0 && p_new < s0 + C) ? p_new - s0 : -1;
-  // K in one copy group, V in a second one that lands while the scores run.
-#pragma unroll 4
-  for (int e = tid; e < C * (D / 8); e += kAttnThreads) {
-    const int key = e / (D / 8), part = e % (D / 8);
-    __half* dk = sK + key * kKStride + part * 8;
-    if (key == new_row) continue;
-    if (key < cnt)
-      cp_async16(dk, k_cache + ((b * S_max + s0 + key) * Hkv + kvh) * D + part * 8);
-    else
-      *reinterpret_cast<uint4*>(dk) = make_uint4(0u, 0u, 0u, 0u);
+  // One 256-byte bulk copy per K row and per V row (thread = key), K and V on
+  // their own barriers so V lands while the scores run; rows past cnt zero.
+  {
+    int rows = cnt - (new_row >= 0 && new_row < cnt ? 1 : 0);
+    if (tid == 0) {
+      mbar_arrive_expect_tx(&bar_kv[0], static_cast<uint32_t>(rows) * (D * 2));
+      mbar_arrive_expect_tx(&bar_kv[1], static_cast<uint32_t>(rows) * (D * 2));
+    }
+    if (tid < cnt && tid != new_row) {
+      const size_t g = ((b * S_max + s0 + tid) * Hkv + kvh) * D;
+      bulk_g2s(sK + tid * kKStride, k_cache + g, D * 2, &bar_kv[0]);
+      bulk_g2s(sV + tid * kVStride, v_cache + g, D * 2, &bar_kv[1]);
+    } else if (tid >= cnt) {
+#pragma unroll
+      for (int j = 0; j < D / 8; ++j) {
+        *reinterpret_cast<uint4*>(sK + tid * kKStride + 8 * j) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(sV + tid * kVStride + 8 * j) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
   }
-  cp_async_commit();
-#pragma unroll 4
-  for (int e = tid; e < C * (D / 8); e += kAttnThreads) {
-    const int key = e / (D / 8), part = e % (D / 8);
-    __half* dv = sV + key * kVStride + part * 8;
-    if (key == new_row) continue;
-    if (key < cnt)
-      cp_async16(dv, v_cache + ((b * S_max + s0 + key) * Hkv + kvh) * D + part * 8);
-    else
-      *reinterpret_cast<uint4*>(dv) = make_uint4(0u, 0u, 0u, 0u);
-  }
-  cp_async_commit();
   // q of the group's heads (rotated here for ROPE), f32, heads above G zero.
   if constexpr (ROPE) {
     const int slots = H + 2 * Hkv;
@@ -606,7 +611,14 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split_tc(
   }
   __syncthreads();
   float o[2][4];
-  tc_chunk<G, true>(sK, sV, sQ, sP, cnt, scale, red_m, red_l, o);
+  tc_chunk<G>(
+      sK, sV, sQ, sP, cnt, scale, red_m, red_l, o,
+      [&] {
+        if (!mbar_wait(&bar_kv[0], 0)) mbar_wait(&bar_kv[0], 0);  // bounded; error recorded
+      },
+      [&] {
+        if (!mbar_wait(&bar_kv[1], 0)) mbar_wait(&bar_kv[1], 0);
+      });
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
@@ -863,7 +875,7 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_decode_cl(
     wait_rows(&bar[1], static_cast<uint32_t>(slot & 1));
     __syncthreads();
     float o[2][4];
-    tc_chunk<G, false>(sK, sV, sQ, sP, cnt, scale, red_m, red_l, o);
+    tc_chunk<G>(sK, sV, sQ, sP, cnt, scale, red_m, red_l, o, [] {}, [] {});
     push_partial(c, o);
   }
 
