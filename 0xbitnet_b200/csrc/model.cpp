@@ -162,6 +162,7 @@ Model::~Model() {
   if (decode_exec_) cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(decode_exec_));
   cudaFree(recent_d_);
   cudaFree(sel_d_);
+  cudaFree(sel_scratch_d_);
   cudaFree(step_d_);
   cudaFreeHost(step_h_);
   cudaFreeHost(logits_h_);
@@ -415,6 +416,7 @@ std::string Model::build(const gguf::File& f, const uint8_t* data, size_t size,
     return cuda_fail(ce, "pinned host buffers");
   if ((ce = cudaMalloc(&recent_d_, sizeof(uint32_t) * kMaxSeq)) != cudaSuccess ||
       (ce = cudaMalloc(&sel_d_, sel_bytes)) != cudaSuccess ||
+      (ce = cudaMalloc(&sel_scratch_d_, select_topk_scratch_bytes(c.vocab))) != cudaSuccess ||
       (ce = cudaMalloc(&step_d_, 2 * sizeof(int32_t))) != cudaSuccess ||
       (ce = cudaMallocHost(&step_h_, 2 * sizeof(int32_t))) != cudaSuccess)
     return cuda_fail(ce, "sampling buffers");
@@ -615,7 +617,7 @@ std::string Model::sample(float temperature, size_t top_k, float repeat_penalty,
   uint2* pairs_d = reinterpret_cast<uint2*>(static_cast<uint8_t*>(sel_d_) + 16);
   ce = launch_select_topk(logits_d_, cfg_.vocab, recent_d_, penalise ? static_cast<int>(n_recent) : 0,
                           penalise ? repeat_penalty : 1.0f, temperature, static_cast<int>(k),
-                          pairs_d, kSelCap, count_d, s);
+                          pairs_d, kSelCap, count_d, sel_scratch_d_, s);
   if (ce != cudaSuccess) return cuda_fail(ce, "top-k launch");
   // The count and the first 4k + 256 pairs (ties past that need a second copy).
   const size_t first = std::min<size_t>(kSelCap, 4 * k + 256);

@@ -132,6 +132,7 @@ class Model {
   uint32_t* recent_h_ = nullptr;        // pinned [kMaxSeq]
   void* sel_d_ = nullptr;               // count, then kSelCap ids, then kSelCap values
   void* sel_h_ = nullptr;               // pinned copy of sel_d_
+  void* sel_scratch_d_ = nullptr;       // candidates of the two-stage top-k selection
   int32_t* step_d_ = nullptr;           // decode step input: token id, position
   int32_t* step_h_ = nullptr;           // pinned
   void* decode_exec_ = nullptr;         // cudaGraphExec_t of one decode step
