@@ -159,7 +159,8 @@ Model::~Model() {
                   static_cast<void*>(ffn_), static_cast<void*>(lm_in_),
                   static_cast<void*>(logits_d_), static_cast<void*>(ids_d_), ws_, attn_ws_})
     cudaFree(p);
-  if (decode_exec_) cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(decode_exec_));
+  for (void* ge : decode_exec_)
+    if (ge) cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(ge));
   cudaFree(recent_d_);
   cudaFree(sel_d_);
   cudaFree(sel_scratch_d_);
@@ -451,13 +452,22 @@ std::string Model::forward(const uint32_t* ids, int n, bool copy_logits) {
 // kernels, for the captured decode step). With want_logits the last token's
 // logits land in logits_d_.
 std::string Model::enqueue(int n, const int32_t* ids_dev, const int* pos_dev, bool want_logits) {
+  return enqueue_part(n, ids_dev, pos_dev, want_logits, 0, static_cast<int>(layers_.size()));
+}
+
+// The forward's launches for layers [first, last): the embedding when first is 0,
+// the final norm and the LM head (want_logits) when last is the layer count.
+std::string Model::enqueue_part(int n, const int32_t* ids_dev, const int* pos_dev,
+                                bool want_logits, int first, int last) {
   const ModelConfig& c = cfg_;
   cudaStream_t s = static_cast<cudaStream_t>(stream_);
   const int D = c.hidden, H = c.heads, Hkv = c.kv_heads, d = c.head_dim;
   const float scale = 1.0f / std::sqrt(static_cast<float>(d));  // attention.rs:206
   const int seq = pos_ + n;
-  if (obn_embed_f16(embed_, c.vocab, D, ids_dev, n, x_, s) != OBN_OK) return obn_fail("embedding");
-  for (size_t i = 0; i < layers_.size(); ++i) {
+  if (first == 0 &&
+      obn_embed_f16(embed_, c.vocab, D, ids_dev, n, x_, s) != OBN_OK)
+    return obn_fail("embedding");
+  for (size_t i = static_cast<size_t>(first); i < static_cast<size_t>(last); ++i) {
     const Layer& L = layers_[i];
     if (obn_bitlinear_forward(L.qkv, x_, n, qkv_, ws_, ws_bytes_, s) != OBN_OK)
       return obn_fail("q|k|v projection");
@@ -496,17 +506,17 @@ std::string Model::enqueue(int n, const int32_t* ids_dev, const int* pos_dev, bo
     if (obn_bitlinear_forward_residual(L.down, ffn_, n, x_, ws_, ws_bytes_, s) != OBN_OK)
       return obn_fail("down_proj + residual");
   }
-  if (!want_logits) return std::string();
+  if (!want_logits || last < static_cast<int>(layers_.size())) return std::string();
   // model.rs:235-262: final RMSNorm and the LM head on the last position only.
-  const float* last = x_ + static_cast<size_t>(n - 1) * D;
+  const float* x_last = x_ + static_cast<size_t>(n - 1) * D;
   if (lm_ternary_) {
-    if (obn_rmsnorm(last, final_norm_, c.eps, 1, D, lm_in_, s) != OBN_OK)
+    if (obn_rmsnorm(x_last, final_norm_, c.eps, 1, D, lm_in_, s) != OBN_OK)
       return obn_fail("final norm");
     if (obn_bitlinear_forward(lm_ternary_, lm_in_, 1, logits_d_, ws_, ws_bytes_, s) != OBN_OK)
       return obn_fail("LM head");
   } else {
     const void* table = lm_f16_ ? lm_f16_ : embed_;
-    if (obn_lm_head_f16(table, c.vocab, D, last, final_norm_, c.eps, 1, logits_d_, s) != OBN_OK)
+    if (obn_lm_head_f16(table, c.vocab, D, x_last, final_norm_, c.eps, 1, logits_d_, s) != OBN_OK)
       return obn_fail("LM head");
   }
   return std::string();
@@ -535,28 +545,41 @@ std::string Model::run_chunk(const uint32_t* ids, int n, bool want_logits, bool 
     step_h_[1] = pos_;
     ce = cudaMemcpyAsync(step_d_, step_h_, 2 * sizeof(int32_t), cudaMemcpyHostToDevice, s);
     if (ce != cudaSuccess) return cuda_fail(ce, "step upload");
-    if (!decode_exec_ && decode_steps_ >= 1) {
-      // A capture that fails (nothing was enqueued: the stream was capturing)
+    if (!decode_exec_[0] && decode_steps_ >= 1) {
+      // Three graphs of growing size: launching a graph costs the host ~0.9 us
+      // per kernel, so the next piece is launched while the previous one runs
+      // and only the small first piece's launch is exposed after sampling. A
+      // capture that fails (nothing was enqueued: the stream was capturing)
       // leaves the model on eager steps.
-      cudaGraph_t g = nullptr;
-      cudaGraphExec_t ge = nullptr;
-      bool ok = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
-      if (ok) {
-        ok = enqueue(1, step_d_, step_d_ + 1, true).empty();
-        ok = cudaStreamEndCapture(s, &g) == cudaSuccess && ok;
-        ok = ok && cudaGraphInstantiate(&ge, g, 0) == cudaSuccess;
-        if (g) cudaGraphDestroy(g);
+      const int L = static_cast<int>(layers_.size());
+      const int cut[4] = {0, std::min(1, L), std::min(6, L), L};
+      bool ok = true;
+      for (int g = 0; g < 3 && ok; ++g) {
+        cudaGraph_t gr = nullptr;
+        cudaGraphExec_t ge = nullptr;
+        ok = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+        if (ok) {
+          ok = enqueue_part(1, step_d_, step_d_ + 1, true, cut[g], cut[g + 1]).empty();
+          ok = cudaStreamEndCapture(s, &gr) == cudaSuccess && ok;
+          ok = ok && cudaGraphInstantiate(&ge, gr, 0) == cudaSuccess;
+          if (gr) cudaGraphDestroy(gr);
+        }
+        decode_exec_[g] = ok ? ge : nullptr;
       }
-      if (ok) {
-        decode_exec_ = ge;
-      } else {
+      if (!ok) {
+        for (int g = 0; g < 3; ++g) {
+          if (decode_exec_[g]) cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(decode_exec_[g]));
+          decode_exec_[g] = nullptr;
+        }
         use_graph_ = false;
         cudaGetLastError();
       }
     }
-    if (decode_exec_) {
-      ce = cudaGraphLaunch(static_cast<cudaGraphExec_t>(decode_exec_), s);
-      if (ce != cudaSuccess) return cuda_fail(ce, "graph launch");
+    if (decode_exec_[0]) {
+      for (int g = 0; g < 3; ++g) {
+        ce = cudaGraphLaunch(static_cast<cudaGraphExec_t>(decode_exec_[g]), s);
+        if (ce != cudaSuccess) return cuda_fail(ce, "graph launch");
+      }
     } else {
       e = enqueue(1, step_d_, step_d_ + 1, true);
       if (!e.empty()) return e;

@@ -96,6 +96,8 @@ class Model {
                     const ProgressFn& progress, const LogFn& log);
   std::string run_chunk(const uint32_t* ids, int n, bool want_logits, bool copy_logits);
   std::string enqueue(int n, const int32_t* ids_dev, const int* pos_dev, bool want_logits);
+  std::string enqueue_part(int n, const int32_t* ids_dev, const int* pos_dev, bool want_logits,
+                           int first, int last);
   std::string logits_to_host();
 
   struct Layer {
@@ -135,7 +137,7 @@ class Model {
   void* sel_scratch_d_ = nullptr;       // candidates of the two-stage top-k selection
   int32_t* step_d_ = nullptr;           // decode step input: token id, position
   int32_t* step_h_ = nullptr;           // pinned
-  void* decode_exec_ = nullptr;         // cudaGraphExec_t of one decode step
+  void* decode_exec_[3] = {};           // cudaGraphExec_t of one decode step, in three pieces
   bool use_graph_ = true;
   long long decode_steps_ = 0;
 };
