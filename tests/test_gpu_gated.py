@@ -26,7 +26,9 @@ def layers(M, K, seed):
                                    (6912, 2560, 64), (1000, 384, 3), (300, 256, 40),
                                    (6912, 2560, 300), (513, 640, 17),
                                    # split-K over 3 and 7 CTAs (owner row blocks 44, 20)
-                                   (2560, 2560, 4), (1280, 2560, 9), (1280, 2560, 40)])
+                                   (2560, 2560, 4), (1280, 2560, 9), (1280, 2560, 40),
+                                   # CTA-pair tiles (from 512 tokens), full and partial
+                                   (6912, 2560, 512), (513, 640, 600)])
 def test_gated_forward_matches_two_bitlinears(M, K, n):
     torch = need_cuda()
     gate, up = layers(M, K, 100 + n)
@@ -42,7 +44,7 @@ def test_gated_forward_matches_two_bitlinears(M, K, n):
 
 @pytest.mark.parametrize("M,K,n", [(6912, 2560, 1), (6912, 2560, 2), (6912, 2560, 64),
                                    (300, 256, 3), (6912, 2560, 300), (513, 640, 17),
-                                   (1280, 2560, 9)])
+                                   (1280, 2560, 9), (513, 640, 600)])
 def test_gated_silu_forward(M, K, n):
     """SiLU gate (x / (1 + exp(-x)), activation.wgsl): every matmul path within the
     error of the device's expf (a few ulp) of silu(gate) * up."""

@@ -338,7 +338,9 @@ def test_no_device_wait_gave_up(torch):
 
 
 @pytest.mark.parametrize("M,K,n", [(2560, 2560, 1), (2560, 6912, 3), (2560, 2560, 8),
-                                   (2560, 6912, 64), (3000, 512, 300)])
+                                   (2560, 6912, 64), (3000, 512, 300),
+                                   # CTA-pair tiles (from 512 tokens), full and partial
+                                   (2560, 2560, 512), (3000, 512, 777)])
 def test_forward_residual_is_forward_plus_add(M, K, n):
     # y += forward(x) in the epilogue equals forward(x) then the f32 add, bit for bit
     torch = need_cuda()
