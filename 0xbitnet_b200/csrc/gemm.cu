@@ -91,6 +91,21 @@ constexpr uint32_t idesc_i8_pair() {  // as idesc_i8, M = 256
   return (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
          (static_cast<uint32_t>((2 * kBM) >> 4) << 24);
 }
+// Work units of the persistent tile loop. Tiles [0, split_from) run whole (BN
+// tokens); each tile from split_from on runs as two BN / 2-token halves, one unit
+// each (paired kernel only). The host splits the last partial wave of tiles, or
+// every tile when all the halves fit on the GPU at once, so that the pairs' work
+// evens out instead of a few pairs running one more whole tile at the end.
+struct TileUnit {
+  int mt;    // (paired) row tile
+  int tok0;  // first token
+  int half;  // 1: BN / 2 tokens, else BN
+};
+OBN_DEVINL TileUnit tile_unit(int u, int num_m, int split_from, int bn) {
+  if (u < split_from) return {u % num_m, (u / num_m) * bn, 0};
+  const int h = u - split_from, t = split_from + (h >> 1);
+  return {t % num_m, (t / num_m) * bn + (h & 1) * (bn / 2), 1};
+}
 OBN_DEVINL uint32_t pair_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -205,13 +220,15 @@ constexpr int kGatherStageBytes = 4 * 16 * 32 * 4;
 
 template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal, bool PAIR = false>
 __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CUtensorMap tmap_q,
+                                                      const __grid_constant__ CUtensorMap tmap_qh,
                                                       const __grid_constant__ CUtensorMap tmap_w,
                                                       const float* __restrict__ s_w,
                                                       const float* __restrict__ s_x,
                                                       const int32_t* __restrict__ qsum,
                                                       float* __restrict__ y,
                                                       int32_t* __restrict__ acc_out, int M, int N,
-                                                      int K, int order, const GatherOut go) {
+                                                      int K, int order, int split_arg,
+                                                      const GatherOut go) {
   constexpr int kAStage = KSTG * kBM * kBK;      // expanded A bytes per stage (smem variant)
   // PAIR: a cluster of 2 CTAs shares each 256-row x BN-token tile (cta_group::2);
   // this CTA holds rows [128 rank, 128 rank + 128) and tokens [BN/2 rank, +BN/2).
@@ -238,6 +255,9 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
   const int num_m = (M + (PAIR ? 2 : 1) * kBM - 1) / ((PAIR ? 2 : 1) * kBM);  // (paired) row tiles
   const int num_n = (N + BN - 1) / BN;
   const int tiles = num_m * num_n;
+  // half tiles (tmap_qh: BN / 4 token rows per CTA) only on pairs
+  const int split_from = PAIR ? (split_arg < 0 ? 0 : split_arg < tiles ? split_arg : tiles) : tiles;
+  const int units = 2 * tiles - split_from;
   const uint32_t crank = PAIR ? pair_rank() : 0u;  // 0: issues the pair's MMAs
   const int t0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int tstep = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
@@ -282,13 +302,16 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
     // The whole warp runs the loop (converged); one lane issues the copies.
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_q) : "memory");
+      if (PAIR && split_from < tiles)
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_qh) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_w) : "memory");
     }
     int it = 0;
     bool waited = false;
-    for (int t = t0; t < tiles && !sm->abort_flag; t += tstep) {
-      const int mt = t % num_m, nt = t / num_m;
-      const int rowtile = PAIR ? 2 * mt + static_cast<int>(crank) : mt;
+    for (int u = t0; u < units && !sm->abort_flag; u += tstep) {
+      const TileUnit tu = tile_unit(u, num_m, split_from, BN);
+      const int rowtile = PAIR ? 2 * tu.mt + static_cast<int>(crank) : tu.mt;
+      const bool half = PAIR && tu.half;
       bool ok = true;
       for (int st = 0; st < n_stages; ++st, ++it) {
         const int s = it % STAGES;
@@ -298,7 +321,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
           break;
         }
         if (lane == 0) {
-          mbar_arrive_expect_tx(&sm->full_tma[s], kBStage + kPStage);
+          mbar_arrive_expect_tx(&sm->full_tma[s], (half ? kBStage / 2 : kBStage) + kPStage);
           tma_load_3d(sP + s * kPStage, &tmap_w, 0, st * KSTG, rowtile * (kBM / kSubRows),
                       &sm->full_tma[s]);
         }
@@ -306,9 +329,17 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
           pdl_wait();
           waited = true;
         }
-        if (lane == 0)
-          tma_load_3d(sB + s * kBStage, &tmap_q, 0, nt * BN + static_cast<int>(crank) * kBRows,
-                      st * KSTG, &sm->full_tma[s]);
+        if (lane == 0) {
+          // a half unit: this CTA's BN / 4 token rows land in the first half of
+          // the stage (KSTG == 1 on pairs), where the N = BN / 2 MMA reads them
+          if (half)
+            tma_load_3d(sB + s * kBStage, &tmap_qh, 0,
+                        tu.tok0 + static_cast<int>(crank) * (kBRows / 2), st * KSTG,
+                        &sm->full_tma[s]);
+          else
+            tma_load_3d(sB + s * kBStage, &tmap_q, 0, tu.tok0 + static_cast<int>(crank) * kBRows,
+                        st * KSTG, &sm->full_tma[s]);
+        }
         __syncwarp();
       }
       if (!ok) break;
@@ -324,9 +355,11 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
     // Converged warp; one lane issues the MMAs and commits.
     pdl_wait();
     int it = 0, ti = 0;
-    constexpr uint32_t idesc = PAIR ? idesc_i8_pair<BN>() : idesc_i8<BN>();
+    constexpr uint32_t kIdesc = PAIR ? idesc_i8_pair<BN>() : idesc_i8<BN>();
+    constexpr uint32_t kIdescHalf = PAIR ? idesc_i8_pair<BN / 2>() : idesc_i8<BN>();
     // PAIR: the odd CTA's MMA warp issues nothing (its rows are in the even CTA's MMAs)
-    for (int t = t0; t < tiles && !sm->abort_flag && (!PAIR || crank == 0); t += tstep, ++ti) {
+    for (int u = t0; u < units && !sm->abort_flag && (!PAIR || crank == 0); u += tstep, ++ti) {
+      const uint32_t idesc = u >= split_from ? kIdescHalf : kIdesc;
       const int a = ti & 1;
       const uint32_t aph = (ti >> 1) & 1u;
       if (!wait_x<PAIR>(sm, &sm->acce[a], aph ^ 1u)) break;
@@ -401,7 +434,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
     const int r = tid - 128;  // weight row within the tile = TMEM lane
     const int sub = r >> 4, rr = r & 15;
     int it = 0;
-    for (int t = t0; t < tiles && !sm->abort_flag; t += tstep) {
+    for (int u = t0; u < units && !sm->abort_flag; u += tstep) {
       bool ok = true;
       for (int st = 0; st < n_stages; ++st, ++it) {
         const int s = it % STAGES;
@@ -479,8 +512,9 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
     pdl_wait();
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     int ti = 0;
-    for (int t = t0; t < tiles && !sm->abort_flag; t += tstep, ++ti) {
-      const int mt = t % num_m, nt = t / num_m;
+    for (int u = t0; u < units && !sm->abort_flag; u += tstep, ++ti) {
+      const TileUnit tu = tile_unit(u, num_m, split_from, BN);
+      const int mt = tu.mt, tok0 = tu.tok0;
       const int rowtile = PAIR ? 2 * mt + static_cast<int>(crank) : mt;
       const int a = ti & 1;
       const uint32_t aph = (ti >> 1) & 1u;
@@ -495,7 +529,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
         float sxr[kChunks];
 #pragma unroll
         for (int c = 0; c < kChunks; ++c) {
-          const int nl = nt * BN + c * kCols + (lane % kCols);
+          const int nl = tok0 + c * kCols + (lane % kCols);
           qsr[c] = nl < N ? qsum[nl] : 0;
           sxr[c] = (nl < N && !acc_out) ? s_x[nl] : 0.0f;
         }
@@ -514,7 +548,10 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                                                     : 1;
         const bool gemv_order = (order & 1) == kOrderGemv;
         const size_t Mh = static_cast<size_t>(M) >> 1;
-        const bool full_tile = (nt + 1) * BN <= N && (rowtile + 1) * kBM <= M;
+        // a half unit's accumulator holds BN / 2 columns
+        const int width = tu.half ? BN / 2 : BN;
+        const int nchunks = width / kCols;
+        const bool full_tile = tok0 + width <= N && (rowtile + 1) * kBM <= M;
         auto chunk = [&](auto kind_c) {
           constexpr int K_ = decltype(kind_c)::value;
           if constexpr (K_ >= 3) {
@@ -532,9 +569,9 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                 xr[c] = sxr[c];
               }
               const bool odd = (m & 1) != 0;
-              float* yb = y + static_cast<size_t>(nt * BN + (odd ? 1 : 0)) * Mh + (m >> 1);
+              float* yb = y + static_cast<size_t>(tok0 + (odd ? 1 : 0)) * Mh + (m >> 1);
 #pragma unroll 1
-              for (int c = 0; c < kChunks; ++c) {
+              for (int c = 0; c < nchunks; ++c) {
                 uint32_t v[kCols];
                 if constexpr (kCols == 32)
                   tmem_ld32(taddr + c * 32, v);
@@ -588,7 +625,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
               xr[c] = sxr[c];
             }
 #pragma unroll 1
-            for (int c = 0; c < kChunks; ++c) {
+            for (int c = 0; c < nchunks; ++c) {
               uint32_t v[kCols];
               if constexpr (kCols == 32)
                 tmem_ld32(taddr + c * 32, v);
@@ -607,7 +644,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                 xr[k] = xr[k + 1];
               }
               tmem_ld_wait();
-              const size_t o0 = static_cast<size_t>(nt * BN + c * kCols) * M + m;
+              const size_t o0 = static_cast<size_t>(tok0 + c * kCols) * M + m;
 #pragma unroll
               for (int j = 0; j < kCols; ++j) {
                 const int d = static_cast<int>(v[j]) - qs_v[j];
@@ -636,7 +673,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
             xr[c] = sxr[c];
           }
 #pragma unroll 1
-          for (int c = 0; c < kChunks; ++c) {
+          for (int c = 0; c < nchunks; ++c) {
             uint32_t v[kCols];
             if constexpr (kCols == 32)
               tmem_ld32(taddr + c * 32, v);
@@ -652,7 +689,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
             tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < kCols; ++j) {
-              const int n = nt * BN + c * kCols + j;
+              const int n = tok0 + c * kCols + j;
               const int qs_j = __shfl_sync(0xffffffffu, qs_c, j);
               const float sx_j = __shfl_sync(0xffffffffu, sx_c, j);
               if constexpr (K_ >= 3) {  // the pair's shuffle runs in every lane
@@ -709,7 +746,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
         uint32_t v[16];
         tmem_ld16(taddr + j0, v);
         tmem_ld_wait();
-        const int n0 = nt * BN + j0;
+        const int n0 = tok0 + j0;
         // Column j's code sum and scale, fetched once per warp and broadcast.
         const int nl = n0 + (lane & 15);
         const int qs_l = nl < N ? qsum[nl] : 0;
@@ -1324,14 +1361,34 @@ bool make_w_map(CUtensorMap* map, const WeightView& W, int KSTG) {
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// First tile of the paired GEMM that runs as two half-width units (tiles when
+// none does), for `pairs` co-resident pairs: every tile when all the halves fit
+// in one wave, else the last partial wave when its halves fit in one; not when
+// the last token tile's second half would be empty. OBN_GEMM_HALVES=0 disables.
+int pair_split_from(int tiles, int pairs, int n, int bn) {
+  static const bool on = [] {
+    const char* e = std::getenv("OBN_GEMM_HALVES");
+    return !(e && e[0] == '0');
+  }();
+  if (!on || pairs <= 0) return tiles;
+  const int tail = n % bn;
+  if (tail != 0 && tail <= bn / 2) return tiles;
+  if (2 * tiles <= pairs) return 0;
+  if (tiles <= pairs) return tiles;
+  const int rem = tiles % pairs;
+  return rem > 0 && 2 * rem <= pairs ? tiles - rem : tiles;
+}
+
 template <int BN, int STAGES, int KSTG, bool A_TMEM, int OUT = kOutLocal, bool PAIR = false>
 cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, const int32_t* qsum,
                     int n, float* y, int32_t* acc, int order, cudaStream_t s,
                     const GatherOut& go = GatherOut{}) {
   if (!encode_fn()) return cudaErrorNotSupported;
-  CUtensorMap qmap, wmap;
+  CUtensorMap qmap, qhmap, wmap;
   if (!make_q_map(&qmap, q, n, W.in_dim, PAIR ? BN / 2 : BN, KSTG) || !make_w_map(&wmap, W, KSTG))
     return cudaErrorInvalidValue;
+  if (PAIR && !make_q_map(&qhmap, q, n, W.in_dim, BN / 4, KSTG)) return cudaErrorInvalidValue;
+  if (!PAIR) qhmap = qmap;
   const size_t smem = gemm_smem_bytes<BN, STAGES, KSTG, A_TMEM, OUT, PAIR>();
   auto kern = k_gemm<BN, STAGES, KSTG, A_TMEM, OUT, PAIR>;
   static int configured[64] = {0};
@@ -1345,9 +1402,11 @@ cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, cons
   }
   const int rows = PAIR ? 2 * kBM : kBM;
   const int tiles = ((W.out_dim + rows - 1) / rows) * ((n + BN - 1) / BN);
-  // PAIR: clusters of 2 CTAs, one pair per tile (an even grid)
+  // PAIR: clusters of 2 CTAs, one pair per unit (an even grid)
   const int cap = PAIR ? (num_sms() & ~1) : num_sms();
-  const int grid = (PAIR ? 2 * tiles : tiles) < cap ? (PAIR ? 2 * tiles : tiles) : cap;
+  const int split_from = PAIR ? pair_split_from(tiles, cap / 2, n, BN) : tiles;
+  const int units = 2 * tiles - split_from;
+  const int grid = (PAIR ? 2 * units : units) < cap ? (PAIR ? 2 * units : units) : cap;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
@@ -1362,8 +1421,8 @@ cudaError_t gemm_bn(const WeightView& W, const int8_t* q, const float* s_x, cons
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = PAIR ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, kern, qmap, wmap, W.s_w, s_x, qsum, y, acc, W.out_dim, n,
-                            W.in_dim, order, go);
+  return cudaLaunchKernelEx(&cfg, kern, qmap, qhmap, wmap, W.s_w, s_x, qsum, y, acc, W.out_dim,
+                            n, W.in_dim, order, split_from, go);
 }
 
 template <int BN>

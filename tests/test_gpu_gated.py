@@ -27,8 +27,10 @@ def layers(M, K, seed):
                                    (6912, 2560, 300), (513, 640, 17),
                                    # split-K over 3 and 7 CTAs (owner row blocks 44, 20)
                                    (2560, 2560, 4), (1280, 2560, 9), (1280, 2560, 40),
-                                   # CTA-pair tiles (from 512 tokens), full and partial
-                                   (6912, 2560, 512), (513, 640, 600)])
+                                   # CTA-pair tiles (from 512 tokens), full and partial;
+                                   # the last wave split into half tiles (6912 x 512),
+                                   # every tile split, the last half partial (640 x 700)
+                                   (6912, 2560, 512), (513, 640, 600), (640, 640, 700)])
 def test_gated_forward_matches_two_bitlinears(M, K, n):
     torch = need_cuda()
     gate, up = layers(M, K, 100 + n)
@@ -44,7 +46,7 @@ def test_gated_forward_matches_two_bitlinears(M, K, n):
 
 @pytest.mark.parametrize("M,K,n", [(6912, 2560, 1), (6912, 2560, 2), (6912, 2560, 64),
                                    (300, 256, 3), (6912, 2560, 300), (513, 640, 17),
-                                   (1280, 2560, 9), (513, 640, 600)])
+                                   (1280, 2560, 9), (513, 640, 600), (640, 640, 700)])
 def test_gated_silu_forward(M, K, n):
     """SiLU gate (x / (1 + exp(-x)), activation.wgsl): every matmul path within the
     error of the device's expf (a few ulp) of silu(gate) * up."""

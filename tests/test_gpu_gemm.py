@@ -4,7 +4,8 @@ Token counts >= 16 run on the tensor cores, and so do 4-15 tokens when the
 layer has few enough 128-row tiles for the split-K (cluster) form. Shapes cover
 partial tiles in both the weight-row (128) and token (16/32/64/128/256)
 dimensions, single and many K blocks, one and several tiles per persistent CTA,
-and cluster sizes 2 through 8.
+cluster sizes 2 through 8, and the CTA-pair kernel's half-width (128-token)
+units, with the last half ragged.
 """
 import numpy as np
 import pytest
@@ -39,13 +40,17 @@ def test_gemm_small_exact(torch, M, K, n):
 @pytest.mark.parametrize("M,K,n", [(1, 128, 16), (100, 256, 17), (129, 128, 33), (300, 384, 100),
                                    (513, 640, 129), (1000, 256, 257), (2560, 2560, 64),
                                    (6912, 2560, 32), (2560, 6912, 64), (3840, 2560, 300),
-                                   (128, 256, 200), (129, 128, 300), (384, 640, 513)])
+                                   (128, 256, 200), (129, 128, 300), (384, 640, 513),
+                                   # CTA pairs with half-width units: every tile split,
+                                   # the last half partial (1280 x 900); the last partial
+                                   # wave split (2560 x 2048: 80 tiles on 74 pairs)
+                                   (1280, 640, 900), (2560, 384, 2048), (2560, 256, 8092)])
 def test_gemm_acc_bitexact(torch, M, K, n):
     got, want = run_acc(torch, M, K, n, M * 3 + K + n)
     assert np.array_equal(got, want)
 
 
-@pytest.mark.parametrize("n", [4, 8, 16, 32, 64, 512])
+@pytest.mark.parametrize("n", [4, 8, 16, 32, 64, 512, 2048])
 def test_gemm_forward_matches_oracle(torch, n):
     M, K = 2560, 2560
     L = synth().layer(700 + n, M, K)
