@@ -15,6 +15,8 @@
 #include "kernels.h"
 
 #include <cuda_fp16.h>
+
+#include <cstdlib>
 #include "layout.cuh"
 #include "obn_common.cuh"
 
@@ -457,6 +459,164 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant_t64(const float* __restri
   }
   // a slot that stopped early may still have a row copy in flight: wait for it (bounded)
   if (l == 0 && failed) mbar_wait(&row_bar[slot], phase);
+}
+
+// Fused RMSNorm + quantize for many tokens of wide rows (prefill, d > 4096):
+// 128 threads per token group, three groups per CTA, each group double-buffering
+// its rows in shared memory, so a row is in flight while the previous one is
+// processed and a row of 6912 floats costs 54 registers per thread instead of 108.
+//
+// Thread l of a group owns shader lanes 2l, 2l + 1 (float2 at columns 2l + 256m),
+// each lane folding its columns in the shader's order. The halving tree
+// (rmsnorm.wgsl:50-55): strides 128 and 64 from the group's published partials
+// (every warp folds the same way, so each gets the total without another
+// barrier), strides 32 .. 2 with shuffles (lane + 16 .. + 1), stride 1 inside the
+// thread. Named 128-thread barriers per group: partials, the warps' max |value|,
+// the warps' code sums. q is stored two bytes per column pair.
+constexpr int kWideThreads = 128;
+constexpr int kWideGroups = 3;
+constexpr int kWideMinCols = 4097;  // narrower rows keep the 64-thread form
+
+template <int EPT2, bool NORM>
+__global__ __launch_bounds__(kWideThreads* kWideGroups, 1) void k_rmsnorm_quant_w128(
+    const float* __restrict__ x, const float* __restrict__ w, float eps, int d, int n,
+    int8_t* __restrict__ q, float* __restrict__ scales, int32_t* __restrict__ qsum) {
+  // dynamic: two row buffers per group [kWideGroups][2][d], then gamma [d] (NORM)
+  extern __shared__ __align__(16) float dyn[];
+  __shared__ __align__(16) float2 part_s[kWideGroups][kWideThreads];
+  __shared__ float max_s[kWideGroups][4];
+  __shared__ int sum_s[kWideGroups][4];
+  __shared__ __align__(8) uint64_t row_bar[kWideGroups][2];
+  const int tid = threadIdx.x, grp = tid / kWideThreads, l = tid % kWideThreads;
+  const int lane = tid & 31, wq = l >> 5;
+  const int bar_id = 1 + grp;
+  float* rows = dyn + static_cast<size_t>(2 * grp) * d;
+  const float* g_s = dyn + static_cast<size_t>(2 * kWideGroups) * d;
+  if (NORM)
+    for (int i = 4 * tid; i < d; i += 4 * kWideThreads * kWideGroups)
+      *reinterpret_cast<float4*>(dyn + static_cast<size_t>(2 * kWideGroups) * d + i) =
+          *reinterpret_cast<const float4*>(w + i);
+  if (tid < 2 * kWideGroups) mbar_init(&row_bar[tid >> 1][tid & 1], 1);
+  fence_mbar_init();
+  __syncthreads();
+  pdl_launch_dependents();
+  pdl_wait();  // x may be the previous kernel's output
+  const size_t stride = static_cast<size_t>(gridDim.x) * kWideGroups;
+  const uint32_t row_bytes = static_cast<uint32_t>(d) * 4;
+  size_t t = static_cast<size_t>(blockIdx.x) * kWideGroups + grp;
+  // the group's first two rows; each later row is requested into the buffer the
+  // row two steps earlier has left (once every thread holds that row's columns)
+  if (l == 0)
+    for (int b = 0; b < 2; ++b) {
+      const size_t tb = t + b * stride;
+      if (tb < static_cast<size_t>(n)) {
+        mbar_arrive_expect_tx(&row_bar[grp][b], row_bytes);
+        bulk_g2s(rows + static_cast<size_t>(b) * d, x + tb * d, row_bytes, &row_bar[grp][b]);
+      }
+    }
+  int i = 0;
+  bool failed = false;  // a row copy that never landed (recorded): the group stops
+  for (; t < static_cast<size_t>(n); t += stride, ++i) {
+    const int b = i & 1;
+    const uint32_t ph = static_cast<uint32_t>(i >> 1) & 1u;
+    const bool got = mbar_wait(&row_bar[grp][b], ph);
+    const float* row = rows + static_cast<size_t>(b) * d;
+    float2 xv[EPT2];
+#pragma unroll
+    for (int m = 0; m < EPT2; ++m) {
+      const int c = 2 * l + 256 * m;
+      xv[m] = c < d ? *reinterpret_cast<const float2*>(row + c) : make_float2(0.f, 0.f);
+    }
+    const size_t tn = t + 2 * stride;
+    auto request_next = [&] {  // after a group barrier: every thread has its columns
+      if (l == 0 && tn < static_cast<size_t>(n)) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&row_bar[grp][b], row_bytes);
+        bulk_g2s(rows + static_cast<size_t>(b) * d, x + tn * d, row_bytes, &row_bar[grp][b]);
+      }
+    };
+    float rms = 1.0f;
+    if (NORM) {
+      float p0 = 0.f, p1 = 0.f;  // shader lanes 2l, 2l + 1
+#pragma unroll
+      for (int m = 0; m < EPT2; ++m) {
+        if (2 * l + 256 * m < d) {
+          p0 = __fadd_rn(p0, __fmul_rn(xv[m].x, xv[m].x));
+          p1 = __fadd_rn(p1, __fmul_rn(xv[m].y, xv[m].y));
+        }
+      }
+      part_s[grp][l] = make_float2(p0, p1);
+      failed = named_bar_or(bar_id, kWideThreads, !got);  // the group agrees on a timeout
+      if (failed) break;
+      request_next();
+      // stride 128: lanes 2j + e += lanes 2j + e + 128 (thread j + 64), for the
+      // lanes of threads lane and lane + 32; stride 64 then folds the second pair
+      const float2 a = part_s[grp][lane], a2 = part_s[grp][lane + 64];
+      const float2 c = part_s[grp][lane + 32], c2 = part_s[grp][lane + 96];
+      float v0 = __fadd_rn(a.x, a2.x), v1 = __fadd_rn(a.y, a2.y);
+      const float w0 = __fadd_rn(c.x, c2.x), w1 = __fadd_rn(c.y, c2.y);
+      v0 = __fadd_rn(v0, w0);
+      v1 = __fadd_rn(v1, w1);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {  // strides 32 .. 2
+        v0 = __fadd_rn(v0, __shfl_down_sync(0xffffffffu, v0, o));
+        v1 = __fadd_rn(v1, __shfl_down_sync(0xffffffffu, v1, o));
+      }
+      const float total = __shfl_sync(0xffffffffu, __fadd_rn(v0, v1), 0);  // stride 1
+      rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(total, static_cast<float>(d)), eps)));
+    }
+    float lmax = 0.0f;
+#pragma unroll
+    for (int m = 0; m < EPT2; ++m) {
+      const int c = 2 * l + 256 * m;
+      if (c < d) {
+        if (NORM) {
+          const float2 g = *reinterpret_cast<const float2*>(g_s + c);
+          xv[m] = make_float2(norm_mul(xv[m].x, rms, g.x), norm_mul(xv[m].y, rms, g.y));
+        }
+        lmax = fmaxf(lmax, fmaxf(fabsf(xv[m].x), fabsf(xv[m].y)));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+    if (lane == 0) max_s[grp][wq] = lmax;
+    if (NORM) {
+      named_bar(bar_id, kWideThreads);
+    } else {
+      failed = named_bar_or(bar_id, kWideThreads, !got);
+      if (failed) break;
+      request_next();
+    }
+    const float absmax =
+        fmaxf(fmaxf(max_s[grp][0], max_s[grp][1]), fmaxf(max_s[grp][2], max_s[grp][3]));
+    const float inv = absmax == 0.0f ? 0.0f : __fdiv_rn(127.0f, absmax);
+    int lsum = 0;
+    uint16_t* qr = reinterpret_cast<uint16_t*>(q + t * d);
+#pragma unroll
+    for (int m = 0; m < EPT2; ++m) {
+      const int c = 2 * l + 256 * m;
+      if (c < d) {
+        const uint32_t qa = round_bits(__fmul_rn(xv[m].x, inv));
+        const uint32_t qb = round_bits(__fmul_rn(xv[m].y, inv));
+        lsum += static_cast<int>(qa + qb - 2u * kRoundMagicBits);
+        qr[c >> 1] = static_cast<uint16_t>(__byte_perm(qa, qb, 0x0040));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    if (lane == 0) sum_s[grp][wq] = lsum;
+    named_bar(bar_id, kWideThreads);
+    if (l == 0) {
+      scales[t] = absmax == 0.0f ? 1.0f : __fdiv_rn(absmax, 127.0f);
+      if (qsum) qsum[t] = (sum_s[grp][0] + sum_s[grp][1]) + (sum_s[grp][2] + sum_s[grp][3]);
+    }
+  }
+  // a group that stopped early may still have row copies in flight: wait for them (bounded)
+  if (l == 0 && failed) {
+    mbar_wait(&row_bar[grp][i & 1], static_cast<uint32_t>(i >> 1) & 1u);
+    if (t + stride < static_cast<size_t>(n))
+      mbar_wait(&row_bar[grp][(i + 1) & 1], static_cast<uint32_t>((i + 1) >> 1) & 1u);
+  }
 }
 
 // rmsnorm.wgsl alone.
@@ -989,6 +1149,38 @@ cudaError_t rmsnorm_quant_t64(const float* x, const float* norm_w, float eps, in
                     q, scales, qsum);
 }
 
+template <int EPT2>
+cudaError_t rmsnorm_quant_w128(const float* x, const float* norm_w, float eps, int n, int d,
+                               int8_t* q, float* scales, int32_t* qsum, cudaStream_t s) {
+  auto kern = norm_w ? k_rmsnorm_quant_w128<EPT2, true> : k_rmsnorm_quant_w128<EPT2, false>;
+  const size_t smem = sizeof(float) * static_cast<size_t>(d) * (2 * kWideGroups + (norm_w ? 1 : 0));
+  cudaError_t e = ensure_smem(reinterpret_cast<const void*>(kern), smem);
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWideThreads * kWideGroups, smem);
+  if (e != cudaSuccess) return e;
+  const int cap = (per_sm > 0 ? per_sm : 1) * num_sms_cached();
+  const int want = (n + kWideGroups - 1) / kWideGroups;
+  return launch_pdl(kern, dim3(want < cap ? want : cap), dim3(kWideThreads * kWideGroups), smem, s,
+                    x, norm_w, eps, d, n, q, scales, qsum);
+}
+
+// Rows from this many columns (and whose double-buffered groups fit in shared
+// memory) take the 128-thread form for many tokens: kWideMinCols, or
+// OBN_QUANT_WIDE_MIN=<columns>; OBN_QUANT_WIDE=0 keeps every row on the 64-thread
+// form. Read once per process.
+int quant_wide_min_cols() {
+  static const int v = [] {
+    const char* e = std::getenv("OBN_QUANT_WIDE");
+    if (e && e[0] == '0') return 1 << 30;
+    const char* m = std::getenv("OBN_QUANT_WIDE_MIN");
+    const int c = m ? std::atoi(m) : 0;
+    return c > 0 ? c : kWideMinCols;
+  }();
+  return v;
+}
+constexpr int kWideMaxCols = 7936;  // (2 * 3 + 1) rows of floats within 227 KB
+
 cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps, int n, int d,
                                  int8_t* q, float* scales, int32_t* qsum, cudaStream_t s) {
   // Few tokens (decode): one 256-thread CTA per token keeps each token's chain short.
@@ -1002,6 +1194,14 @@ cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps,
     if (ept <= 24) return rmsnorm_quant_ept<24>(x, norm_w, eps, n, d, q, scales, qsum, s);
     if (ept <= 28) return rmsnorm_quant_ept<28>(x, norm_w, eps, n, d, q, scales, qsum, s);
     if (ept <= 36) return rmsnorm_quant_ept<36>(x, norm_w, eps, n, d, q, scales, qsum, s);
+  }
+  if (d >= quant_wide_min_cols() && d <= kWideMaxCols) {
+    if (ept <= 8) return rmsnorm_quant_w128<8>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    if (ept <= 12) return rmsnorm_quant_w128<12>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    if (ept <= 16) return rmsnorm_quant_w128<16>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    if (ept <= 24) return rmsnorm_quant_w128<24>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    if (ept <= 28) return rmsnorm_quant_w128<28>(x, norm_w, eps, n, d, q, scales, qsum, s);
+    return rmsnorm_quant_w128<32>(x, norm_w, eps, n, d, q, scales, qsum, s);
   }
   // Many tokens (prefill): 64 threads per token, packed 4-byte stores.
   const int ept4 = ept;  // float4 column quads per thread

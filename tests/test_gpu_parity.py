@@ -78,17 +78,20 @@ def test_rmsnorm_quantize_bitexact(torch, K, n, norm):
     assert np.array_equal(qs.cpu().numpy(), q_ref.astype(np.int64).sum(1))
 
 
-@pytest.mark.parametrize("K", [128, 640, 2560, 6912, 9216])
+@pytest.mark.parametrize("K", [128, 640, 2560, 4100, 6912, 7936, 9216])
 @pytest.mark.parametrize("n", [257, 1000, 3001])
 @pytest.mark.parametrize("norm", [True, False])
 def test_rmsnorm_quantize_many_tokens_bitexact(torch, K, n, norm):
     # above 256 tokens the quantize pass runs 64 threads per token, four tokens per
     # CTA, each slot's next row staged by a bulk copy: ragged token counts leave
     # slots of the last CTAs idle, and K = 640 leaves the last column quad to the
-    # first half of the slot's threads
+    # first half of the slot's threads. Rows of 4097 .. 7936 columns take the
+    # 128-thread form (three double-buffered groups per CTA): K = 4100 ends on a
+    # partial column pair sweep, 7936 fills its shared memory; K = 9216 is past it
     x = synth().activations(3 * K + n, n, K)
     x[n // 2] = 0.0                                       # an all-zero row: scale 1, q 0
-    gamma = synth().layer(K + 1, 1, K).gamma
+    gamma = (synth().layer(K + 1, 1, K).gamma if K % 128 == 0 else
+             (1 + 0.1 * np.random.default_rng(K).standard_normal(K)).astype(np.float32))
     q, s, qs = obn().rmsnorm_quantize(to_dev(torch, x), to_dev(torch, gamma) if norm else None)
     src = orc.rmsnorm(x, gamma, 1e-5) if norm else x
     q_ref, s_ref = orc.quantize(src)
