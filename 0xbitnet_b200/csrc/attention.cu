@@ -110,6 +110,18 @@ OBN_DEVINL void cp_async16(void* smem_dst, const void* gmem_src) {
                : "memory");
 }
 OBN_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// The same with a source size: bytes past src_bytes (all 16 when 0) are zero-filled.
+OBN_DEVINL void cp_async16_zfill(void* smem_dst, const void* gmem_src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src), "r"(src_bytes)
+               : "memory");
+}
+// Arrives on `bar` (without raising its pending count) once every cp.async this
+// thread issued so far has completed.
+OBN_DEVINL void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
 template <int N>
 OBN_DEVINL void cp_async_wait_group() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
@@ -395,11 +407,12 @@ constexpr int kVStride = kAttnHeadDim + 8;  // halves per smem V row (ldmatrix.t
 // CTA); wait_k() / wait_v() are called before the first read of K / V (the K and
 // V copies may still be in flight on entry). On exit o holds this thread's P.V fragments
 // (dims 32 warp + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1) and red_m / red_l
-// every warp's max and sum per head.
-template <int G, class WaitK, class WaitV>
+// every warp's max and sum per head. k_free() runs (in every thread) once no
+// thread reads sK any more, before the P.V contraction.
+template <int G, class WaitK, class WaitV, class KFree>
 OBN_DEVINL void tc_chunk(const __half* sK, const __half* sV, const float* sQ, float* sP, int cnt,
                          float scale, float (*red_m)[4], float (*red_l)[4], float (&o)[2][4],
-                         WaitK wait_k, WaitV wait_v) {
+                         WaitK wait_k, WaitV wait_v, KFree k_free) {
   constexpr int D = kAttnHeadDim;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int grp = lane >> 2, qd = lane & 3;
@@ -477,6 +490,7 @@ OBN_DEVINL void tc_chunk(const __half* sK, const __half* sV, const float* sQ, fl
   }
   wait_v();
   __syncthreads();
+  k_free();
   // P.V: warp w, dims 32w + 16 mt + {grp, grp + 8}, heads 2 qd, 2 qd + 1.
 #pragma unroll
   for (int mt = 0; mt < 2; ++mt)
@@ -502,6 +516,13 @@ OBN_DEVINL void tc_chunk(const __half* sK, const __half* sV, const float* sQ, fl
       mma_16816(o[mt], a, pl0, pl1);
     }
   }
+}
+
+template <int G, class WaitK, class WaitV>
+OBN_DEVINL void tc_chunk(const __half* sK, const __half* sV, const float* sQ, float* sP, int cnt,
+                         float scale, float (*red_m)[4], float (*red_l)[4], float (&o)[2][4],
+                         WaitK wait_k, WaitV wait_v) {
+  tc_chunk<G>(sK, sV, sQ, sP, cnt, scale, red_m, red_l, o, wait_k, wait_v, [] {});
 }
 
 template <int G, bool ROPE = false>
@@ -632,6 +653,156 @@ __global__ __launch_bounds__(kAttnThreads) void k_attn_split_tc(
         fmaxf(fmaxf(red_m[tid][0], red_m[tid][1]), fmaxf(red_m[tid][2], red_m[tid][3]));
     part_l[pbase + static_cast<size_t>(tid) * nsplit] =
         (red_l[tid][0] + red_l[tid][1]) + (red_l[tid][2] + red_l[tid][3]);
+  }
+}
+
+// ---- persistent split pass (many sequences) -----------------------------------
+// k_attn_split_tc's work items (128-key chunk, KV head, query row) on persistent
+// CTAs, three per SM, each cycling through its items (blockIdx.x, + gridDim.x,
+// ...) with one K and one V buffer that it refills as soon as they are free:
+// the next item's K rows are requested once the scores are done (tc_chunk's
+// k_free hook) and its V rows once P.V is, so every CTA keeps a load in flight
+// while it computes instead of loading only between its start and its compute.
+// The next item's q is fetched with its K rows (tc_chunk reads q first). Copies are 16-byte cp.async pieces
+// (a warp moves two 256-byte cache rows per instruction) completing on the
+// buffer's barrier through cp.async.mbarrier.arrive. The per-item arithmetic
+// and the partials are k_attn_split_tc's (same tc_chunk, same layout), so
+// k_attn_combine's result is the same bit for bit.
+constexpr int kPipeCtasPerSm = 3;
+
+template <int G>
+__global__ __launch_bounds__(kAttnThreads, kPipeCtasPerSm) void k_attn_split_pipe(
+    const float* __restrict__ q, const __half* __restrict__ k_cache,
+    const __half* __restrict__ v_cache, int n, int H, int Hkv, int S_max, int seq_len,
+    const int* __restrict__ pos_dev, float scale, int nsplit, int rows_total,
+    float* __restrict__ part_acc, float* __restrict__ part_m, float* __restrict__ part_l) {
+  constexpr int D = kAttnHeadDim;
+  constexpr int C = kAttnChunk;
+  static_assert(C == 128 && D == 128 && kAttnThreads == 128 && G <= 8, "tile shape");
+  extern __shared__ __align__(16) unsigned char smem[];
+  __half* sK = reinterpret_cast<__half*>(smem);             // [C][kKStride]
+  __half* sV = sK + C * kKStride;                           // [C][kVStride]
+  float* sQ = reinterpret_cast<float*>(sV + C * kVStride);  // [G][D]
+  float* sP = sQ + G * D;                                   // [C][G]
+  __shared__ float red_m[8][4], red_l[8][4];
+  __shared__ __align__(8) uint64_t bar_k, bar_v, bar_q;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = lane >> 2, qd = lane & 3;  // MMA fragment coordinates
+  if (tid == 0) {  // K / V: every thread arrives once per item; q: one bulk copy
+    mbar_init(&bar_k, kAttnThreads);
+    mbar_init(&bar_v, kAttnThreads);
+    mbar_init(&bar_q, 1);
+  }
+  fence_mbar_init();
+  __syncthreads();
+  pdl_order<false>();
+  if (pos_dev) seq_len = min(*pos_dev + n, S_max);
+  const int nvalid = min(nsplit, (seq_len + C - 1) / C);  // chunks that hold keys
+  const int items = rows_total * Hkv * nvalid;
+  const int first = static_cast<int>(blockIdx.x), step = static_cast<int>(gridDim.x);
+  const int count = first < items ? (items - first + step - 1) / step : 0;
+  struct Item {
+    size_t r;
+    int kvh, c, cnt;
+  };
+  auto item_at = [&](int k) {
+    const int it = first + k * step;
+    Item x;
+    x.c = it % nvalid;
+    const int rest = it / nvalid;
+    x.kvh = rest % Hkv;
+    x.r = static_cast<size_t>(rest / Hkv);
+    const int t = static_cast<int>(x.r % n);
+    x.cnt = min(C, seq_len - n + t + 1 - x.c * C);  // keys of the chunk up to the causal limit
+    return x;
+  };
+  // Item k's K (or V) rows into dst, rows past cnt zero-filled, then this
+  // thread's arrival on bar once its pieces landed (a plain arrival for an empty
+  // item), so the barrier's phase k & 1 completes with the copies. 16-byte piece
+  // i = tid + 128 j of the chunk is row i / 16, piece i % 16.
+  auto issue = [&](int k, const __half* cache, __half* dst, int stride, uint64_t* bar) {
+    const Item x = item_at(k);
+    const int rows = max(0, x.cnt);
+    if (rows == 0) {
+      mbar_arrive(bar);
+      return;
+    }
+    const size_t g0 = ((x.r / n * S_max + static_cast<size_t>(x.c) * C) * Hkv + x.kvh) * D;
+#pragma unroll 4
+    for (int j = 0; j < C * D / 8 / kAttnThreads; ++j) {
+      const int i = tid + kAttnThreads * j, row = i >> 4, pc = i & 15;
+      const size_t go = row < rows ? g0 + static_cast<size_t>(row) * Hkv * D + pc * 8 : g0;
+      cp_async16_zfill(dst + row * stride + pc * 8, cache + go, row < rows ? 16u : 0u);
+    }
+    cp_async_arrive(bar);
+  };
+  // q of item k's group (f32 [G][D]): one bulk copy (a cp.async arrival would
+  // also wait for the K / V pieces issued before it), phase k & 1 of bar_q.
+  auto fetch_q = [&](int k) {
+    if (tid != 0) return;
+    const Item x = item_at(k);
+    fence_proxy_async_smem();  // the previous item's generic reads of sQ come first
+    mbar_arrive_expect_tx(&bar_q, static_cast<uint32_t>(G * D * 4));
+    bulk_g2s(sQ, q + (x.r * H + static_cast<size_t>(x.kvh) * G) * D, G * D * 4, &bar_q);
+  };
+  auto wait2 = [](uint64_t* bar, uint32_t ph) {  // bounded; the error is recorded
+    if (!mbar_wait(bar, ph)) mbar_wait(bar, ph);
+  };
+  if (count > 0) {
+    issue(0, k_cache, sK, kKStride, &bar_k);
+    issue(0, v_cache, sV, kVStride, &bar_v);
+    fetch_q(0);
+  }
+  for (int k = 0; k < count; ++k) {
+    const Item x = item_at(k);
+    const uint32_t ph = static_cast<uint32_t>(k) & 1u;
+    wait2(&bar_q, ph);  // this item's q
+    const size_t pbase = (x.r * H + static_cast<size_t>(x.kvh) * G) * nsplit + x.c;
+    if (x.cnt <= 0) {  // no key of the chunk is visible to this query row
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        part_acc[(pbase + static_cast<size_t>(g) * nsplit) * D + tid] = 0.0f;
+        if (tid == 0) {
+          part_m[pbase + static_cast<size_t>(g) * nsplit] = -FLT_MAX;
+          part_l[pbase + static_cast<size_t>(g) * nsplit] = 0.0f;
+        }
+      }
+      wait2(&bar_k, ph);  // the empty item's plain arrivals
+      wait2(&bar_v, ph);
+      __syncthreads();  // every thread is past this item's phases
+      if (k + 1 < count) {
+        issue(k + 1, k_cache, sK, kKStride, &bar_k);
+        issue(k + 1, v_cache, sV, kVStride, &bar_v);
+        fetch_q(k + 1);
+      }
+      continue;
+    }
+    float o[2][4];
+    tc_chunk<G>(
+        sK, sV, sQ, sP, x.cnt, scale, red_m, red_l, o, [&] { wait2(&bar_k, ph); },
+        [&] { wait2(&bar_v, ph); },
+        [&] {  // the scores are done (and q is in registers): the next item's K rows and q
+          if (k + 1 < count) {
+            issue(k + 1, k_cache, sK, kKStride, &bar_k);
+            fetch_q(k + 1);
+          }
+        });
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int dim = 32 * warp + 16 * mt + grp + (i >= 2 ? 8 : 0);
+        const int h = 2 * qd + (i & 1);
+        if (h < G) part_acc[(pbase + static_cast<size_t>(h) * nsplit) * D + dim] = o[mt][i];
+      }
+    if (tid < G) {
+      part_m[pbase + static_cast<size_t>(tid) * nsplit] =
+          fmaxf(fmaxf(red_m[tid][0], red_m[tid][1]), fmaxf(red_m[tid][2], red_m[tid][3]));
+      part_l[pbase + static_cast<size_t>(tid) * nsplit] =
+          (red_l[tid][0] + red_l[tid][1]) + (red_l[tid][2] + red_l[tid][3]);
+    }
+    __syncthreads();  // sV, sP and red_* are free again
+    if (k + 1 < count) issue(k + 1, v_cache, sV, kVStride, &bar_v);
   }
 }
 
@@ -1002,6 +1173,50 @@ cudaError_t launch_split(const float* q, const __half* k_cache, const __half* v_
                             scale, nsplit, pa, pm, pl, theta_base);
 }
 
+// The persistent split pass when there are at least kPipeMinItemsPerSm items per
+// SM (and q is 16-byte aligned for its bulk copy); OBN_ATTN_PIPE=0 keeps the
+// one-item CTAs. Read once per process.
+constexpr int kPipeMinItemsPerSm = 4;
+bool attn_pipe_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("OBN_ATTN_PIPE");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+template <int G>
+cudaError_t launch_split_pipe(const float* q, const __half* k_cache, const __half* v_cache, int B,
+                              int n, int H, int Hkv, int S_max, int seq_len, const int* pos_dev,
+                              float scale, int nsplit, float* pa, float* pm, float* pl,
+                              cudaStream_t s) {
+  constexpr int D = kAttnHeadDim;
+  const size_t smem = static_cast<size_t>(kAttnChunk) * (kKStride + kVStride) * 2 +
+                      (static_cast<size_t>(G) * D + static_cast<size_t>(kAttnChunk) * G) * 4;
+  auto kern = k_attn_split_pipe<G>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kAttnThreads, smem);
+  if (e != cudaSuccess) return e;
+  const int rows_total = B * n;
+  const long long items = static_cast<long long>(rows_total) * Hkv * nsplit;
+  const long long cap = static_cast<long long>(per_sm > 0 ? per_sm : 1) * num_sms_cached();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(items < cap ? items : cap));
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, q, k_cache, v_cache, n, H, Hkv, S_max, seq_len, pos_dev,
+                            scale, nsplit, rows_total, pa, pm, pl);
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl_attn(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s,
                             Args... args) {
@@ -1142,8 +1357,14 @@ cudaError_t attention_impl(const float* q, const __half* k_cache, const __half* 
 #undef OBN_CL
   }
   cudaError_t e;
+  const bool pipe = !rope && attn_pipe_enabled() &&
+                    reinterpret_cast<uintptr_t>(q) % 16 == 0 &&
+                    static_cast<long long>(B) * n * Hkv * nsplit >=
+                        static_cast<long long>(kPipeMinItemsPerSm) * num_sms_cached();
 #define OBN_SPLIT(GG)                                                                           \
-  (rope ? launch_split<GG, true>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev,  \
+  (pipe   ? launch_split_pipe<GG>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev,  \
+                                  scale, nsplit, pa, pm, pl, s)                                 \
+   : rope ? launch_split<GG, true>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev,  \
                                  scale, nsplit, pa, pm, pl, s, theta_base)                     \
         : launch_split<GG, false>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, \
                                   scale, nsplit, pa, pm, pl, s, theta_base))

@@ -52,7 +52,13 @@ def test_rope_kv_append(B, n, H, Hkv, pos):
 @pytest.mark.parametrize("B,n,H,Hkv,S", [(1, 1, 20, 5, 1), (1, 1, 20, 5, 2048), (3, 1, 20, 5, 700),
                                          (2, 5, 20, 5, 300), (1, 7, 8, 8, 7), (2, 1, 16, 2, 129),
                                          (1, 130, 4, 1, 260), (1, 1, 20, 5, 5000),
-                                         (1, 1, 16, 8, 4096), (2, 1, 4, 4, 33)])
+                                         (1, 1, 16, 8, 4096), (2, 1, 4, 4, 33),
+                                         # >= 4 work items per SM: the pipelined split pass
+                                         # (decode at the bench's batch, a ragged last chunk,
+                                         # causal prefill with empty items, G = 8 and G = 1)
+                                         (64, 1, 20, 5, 2048), (8, 1, 20, 5, 1900),
+                                         (1, 300, 20, 5, 600), (20, 1, 32, 4, 1100),
+                                         (3, 40, 8, 8, 2000)])
 def test_attention_matches_oracle(B, n, H, Hkv, S):
     torch = need_cuda()
     S_max = S + 3
@@ -97,7 +103,9 @@ def test_attention_decode_step_end_to_end():
 
 @pytest.mark.parametrize("B,H,Hkv,S_prev", [(1, 20, 5, 2047), (3, 20, 5, 127), (2, 16, 2, 128),
                                              (1, 8, 8, 0), (2, 32, 4, 300), (1, 20, 5, 1),
-                                             (1, 20, 5, 4100), (1, 20, 5, 9000), (8, 20, 5, 300)])
+                                             (1, 20, 5, 4100), (1, 20, 5, 9000), (8, 20, 5, 300),
+                                             # RoPE split pass against the pipelined one
+                                             (64, 20, 5, 2047), (8, 20, 5, 1900)])
 def test_fused_rope_attention_is_bit_identical(B, H, Hkv, S_prev):
     """obn_attention_decode_rope == obn_rope_kv_append + obn_attention_decode (n = 1):
     same output bits, same cache contents."""
