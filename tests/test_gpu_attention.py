@@ -143,7 +143,10 @@ def _rope_at(qkv, cache, H, pos_dev, out, ws):
 
 @pytest.mark.parametrize("B,H,Hkv,S_max,pos", [(1, 20, 5, 4096, 1000), (1, 20, 5, 4096, 2500),
                                                (2, 32, 4, 2048, 2047), (1, 20, 5, 4096, 4096),
-                                               (1, 8, 8, 20000, 130)])
+                                               (1, 8, 8, 20000, 130),
+                                               # many sequences: the RoPE split pass against
+                                               # RoPE append + the persistent pass (and a full cache)
+                                               (64, 20, 5, 2048, 1500), (32, 20, 5, 2048, 2048)])
 def test_rope_attention_device_position(B, H, Hkv, S_max, pos):
     """The _at form (position read on the device, chunks sized for S_max) equals
     RoPE append + attention at the host position, bit for bit; a position at
@@ -176,12 +179,14 @@ def test_rope_attention_device_position(B, H, Hkv, S_max, pos):
     assert torch.equal(c1.k.cpu(), c2.k.cpu()) and torch.equal(c1.v.cpu(), c2.v.cpu())
 
 
-def test_rope_attention_back_to_back_steps():
+@pytest.mark.parametrize("B", [2, 64])
+def test_rope_attention_back_to_back_steps(B):
     """Consecutive decode steps on one cache, enqueued with no host sync between
     them (each reads the row the step before appended), equal the same steps run
-    one at a time through RoPE append + attention."""
+    one at a time through RoPE append + attention (B = 2: the clustered pass;
+    B = 64: the RoPE split pass, against the persistent one)."""
     torch = need_cuda()
-    B, H, Hkv, S_max, pos0, steps = 2, 20, 5, 2048, 1020, 12
+    H, Hkv, S_max, pos0, steps = 20, 5, 2048, 1020, 12
     rng = np.random.default_rng(77)
     k = torch.from_numpy(rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16))
     v = torch.from_numpy(rng.standard_normal((B, S_max, Hkv, D)).astype(np.float16))
