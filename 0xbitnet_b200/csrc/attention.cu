@@ -806,6 +806,202 @@ __global__ __launch_bounds__(kAttnThreads, kPipeCtasPerSm) void k_attn_split_pip
   }
 }
 
+// ---- prefill attention: one 16-row query tile per CTA ------------------------
+// For chunks of many new tokens (n >= kFaMinRows) the split pass would read every
+// 128-key chunk once per query row. k_attn_prefill_fa gives a CTA 16 consecutive
+// query rows of one sequence and one KV head; warp w takes query head
+// kvh * G + w for those rows, so the G warps share every K / V block. Keys stream
+// in 64-key blocks (double-buffered 16-byte cp.async pieces); per block each
+// warp computes S = Q K^T (mma.sync m16n8k16, q split into binary16 hi + lo),
+// scales, masks the causal limit, updates its rows' running max and sum (online
+// softmax) and accumulates O += P V (P split into hi + lo). The outputs are
+// written once, divided by the sums: no partials, no combine. Numerically the
+// same function as the split + combine passes in another order (the oracle
+// tolerance, 1e-4 relative).
+constexpr int kFaRows = 16;      // query rows per CTA (the MMA's M)
+constexpr int kFaKeys = 64;      // keys per block
+constexpr int kFaMinRows = 16;   // query rows per sequence from which prefill uses it
+constexpr int kFaStride = kAttnHeadDim + 8;  // halves per smem K / V row
+
+template <int G>
+__global__ __launch_bounds__(32 * G) void k_attn_prefill_fa(
+    const float* __restrict__ q, const __half* __restrict__ k_cache,
+    const __half* __restrict__ v_cache, int n, int H, int Hkv, int S_max, int seq_len,
+    const int* __restrict__ pos_dev, float scale, float* __restrict__ out) {
+  constexpr int D = kAttnHeadDim;
+  constexpr int NT = 32 * G;  // threads
+  static_assert(D == 128 && G >= 1 && G <= 8, "tile shape");
+  extern __shared__ __align__(16) unsigned char smem[];
+  __half* sKV = reinterpret_cast<__half*>(smem);  // [2 stages][K, V][kFaKeys][kFaStride]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = lane >> 2, qd = lane & 3;
+  const int t0 = blockIdx.x * kFaRows, kvh = blockIdx.y;
+  const size_t b = blockIdx.z;
+  const int h = kvh * G + warp;  // this warp's query head
+  pdl_launch_dependents();
+  pdl_wait();
+  if (pos_dev) seq_len = min(*pos_dev + n, S_max);
+  if (t0 >= n) return;
+  const int t_last = min(t0 + kFaRows, n) - 1;
+  const int kmax = seq_len - n + t_last + 1;  // keys visible to the tile's last row
+  const int nkb = (kmax + kFaKeys - 1) / kFaKeys;
+  // q rows t0 + grp and t0 + grp + 8 as A fragments, split hi / lo (rows past n zero)
+  uint32_t qh[8][4], ql[8][4];
+  {
+    const int ta = t0 + grp, tb = t0 + grp + 8;
+    const float* qa = q + ((b * n + ta) * H + h) * static_cast<size_t>(D);
+    const float* qb = q + ((b * n + tb) * H + h) * static_cast<size_t>(D);
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const int d0 = 16 * ks + 2 * qd;
+      const float2 a0 = ta < n ? *reinterpret_cast<const float2*>(qa + d0) : make_float2(0.f, 0.f);
+      const float2 a1 = tb < n ? *reinterpret_cast<const float2*>(qb + d0) : make_float2(0.f, 0.f);
+      const float2 a2 =
+          ta < n ? *reinterpret_cast<const float2*>(qa + d0 + 8) : make_float2(0.f, 0.f);
+      const float2 a3 =
+          tb < n ? *reinterpret_cast<const float2*>(qb + d0 + 8) : make_float2(0.f, 0.f);
+      split_h2(a0.x, a0.y, &qh[ks][0], &ql[ks][0]);
+      split_h2(a1.x, a1.y, &qh[ks][1], &ql[ks][1]);
+      split_h2(a2.x, a2.y, &qh[ks][2], &ql[ks][2]);
+      split_h2(a3.x, a3.y, &qh[ks][3], &ql[ks][3]);
+    }
+  }
+  // K and V rows of block kb into stage kb & 1 (rows at or past kmax zero-filled)
+  auto load_block = [&](int kb) {
+    __half* sK = sKV + (kb & 1) * 2 * kFaKeys * kFaStride;
+    __half* sV = sK + kFaKeys * kFaStride;
+    const int key0 = kb * kFaKeys;
+    for (int i = tid; i < kFaKeys * (D / 8); i += NT) {
+      const int row = i >> 4, pc = i & 15, key = key0 + row;
+      const size_t g = key < kmax ? ((b * S_max + key) * Hkv + kvh) * D + pc * 8
+                                  : ((b * S_max) * Hkv + kvh) * D;
+      const uint32_t nbytes = key < kmax ? 16u : 0u;
+      cp_async16_zfill(sK + row * kFaStride + pc * 8, k_cache + g, nbytes);
+      cp_async16_zfill(sV + row * kFaStride + pc * 8, v_cache + g, nbytes);
+    }
+    cp_async_commit();
+  };
+  // running max / sum of rows grp (index 0) and grp + 8 (index 1); O accumulators
+  // oacc[dt]: dims 8 dt + 2 qd, + 1 of rows grp (0, 1) and grp + 8 (2, 3)
+  float m_run[2] = {-FLT_MAX, -FLT_MAX}, l_run[2] = {0.0f, 0.0f};
+  float oacc[16][4];
+#pragma unroll
+  for (int dt = 0; dt < 16; ++dt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) oacc[dt][i] = 0.0f;
+  const int lim0 = seq_len - n + t0 + grp;  // last key row grp may see (row grp + 8: + 8)
+  const bool row_ok[2] = {t0 + grp < n, t0 + grp + 8 < n};
+  if (nkb > 0) load_block(0);
+  for (int kb = 0; kb < nkb; ++kb) {
+    if (kb + 1 < nkb) {
+      load_block(kb + 1);
+      cp_async_wait_group<1>();  // block kb landed (this thread's pieces)
+    } else {
+      cp_async_wait_group<0>();
+    }
+    __syncthreads();  // every thread's pieces of block kb
+    const __half* sK = sKV + (kb & 1) * 2 * kFaKeys * kFaStride;
+    const __half* sV = sK + kFaKeys * kFaStride;
+    const int key0 = kb * kFaKeys;
+    // S = Q K^T: sacc[nt] holds keys key0 + 8 nt + 2 qd, + 1 of rows grp, grp + 8
+    float sacc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sacc[nt][i] = 0.0f;
+      // ldmatrix x4 of keys 8 nt .. + 7: matrices d 0-7, 8-15, 16-23, 24-31 of each 32-d step
+      const uint32_t kaddr =
+          smem_u32(sK + (8 * nt + (lane & 7)) * kFaStride + ((lane >> 3) << 3));
+#pragma unroll
+      for (int k2 = 0; k2 < 4; ++k2) {  // 32 dims per ldmatrix.x4 = two k-steps
+        uint32_t kb4[4];
+        ldsm_x4(kaddr + k2 * 64, kb4);
+        mma_16816(sacc[nt], qh[2 * k2], kb4[0], kb4[1]);
+        mma_16816(sacc[nt], ql[2 * k2], kb4[0], kb4[1]);
+        mma_16816(sacc[nt], qh[2 * k2 + 1], kb4[2], kb4[3]);
+        mma_16816(sacc[nt], ql[2 * k2 + 1], kb4[2], kb4[3]);
+      }
+    }
+    // scale, causal mask, block max per row
+    float bmax[2] = {-FLT_MAX, -FLT_MAX};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = i >> 1, key = key0 + 8 * nt + 2 * qd + (i & 1);
+        const bool ok = row_ok[r] && key <= lim0 + 8 * r;
+        sacc[nt][i] = ok ? __fmul_rn(sacc[nt][i], scale) : -FLT_MAX;
+        bmax[r] = fmaxf(bmax[r], sacc[nt][i]);
+      }
+    float alpha[2], mnew[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      bmax[r] = fmaxf(bmax[r], __shfl_xor_sync(0xffffffffu, bmax[r], 1));
+      bmax[r] = fmaxf(bmax[r], __shfl_xor_sync(0xffffffffu, bmax[r], 2));
+      mnew[r] = fmaxf(m_run[r], bmax[r]);
+      alpha[r] = expf(m_run[r] - mnew[r]);  // 1 while both are -FLT_MAX
+      m_run[r] = mnew[r];
+    }
+    // P = exp(S - max) (masked entries 0), the rows' sums, O rescaled
+    float psum[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = i >> 1;
+        const float p = sacc[nt][i] == -FLT_MAX ? 0.0f : expf(sacc[nt][i] - mnew[r]);
+        sacc[nt][i] = p;
+        psum[r] += p;
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      psum[r] += __shfl_xor_sync(0xffffffffu, psum[r], 1);
+      psum[r] += __shfl_xor_sync(0xffffffffu, psum[r], 2);
+      l_run[r] = fmaf(l_run[r], alpha[r], psum[r]);
+    }
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      oacc[dt][0] *= alpha[0];
+      oacc[dt][1] *= alpha[0];
+      oacc[dt][2] *= alpha[1];
+      oacc[dt][3] *= alpha[1];
+    }
+    // O += P V over the block's 4 key steps of 16
+    const int vkey = (lane & 7) + (((lane >> 3) & 1) << 3);
+    const int vdim = (lane >> 4) << 3;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      uint32_t ph[4], pl[4];
+      split_h2(sacc[2 * ks][0], sacc[2 * ks][1], &ph[0], &pl[0]);
+      split_h2(sacc[2 * ks][2], sacc[2 * ks][3], &ph[1], &pl[1]);
+      split_h2(sacc[2 * ks + 1][0], sacc[2 * ks + 1][1], &ph[2], &pl[2]);
+      split_h2(sacc[2 * ks + 1][2], sacc[2 * ks + 1][3], &ph[3], &pl[3]);
+#pragma unroll
+      for (int d2 = 0; d2 < 8; ++d2) {  // 16 dims per ldmatrix.x4.trans
+        uint32_t vb[4];
+        ldsm_x4_t(smem_u32(sV + (16 * ks + vkey) * kFaStride + 16 * d2 + vdim), vb);
+        mma_16816(oacc[2 * d2], ph, vb[0], vb[1]);
+        mma_16816(oacc[2 * d2], pl, vb[0], vb[1]);
+        mma_16816(oacc[2 * d2 + 1], ph, vb[2], vb[3]);
+        mma_16816(oacc[2 * d2 + 1], pl, vb[2], vb[3]);
+      }
+    }
+    __syncthreads();  // stage kb & 1 is read; the next load may overwrite it
+  }
+  // outputs: O / l for the tile's rows below n
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    if (!row_ok[r]) continue;
+    const int t = t0 + grp + 8 * r;
+    float* o = out + ((b * n + t) * H + h) * static_cast<size_t>(D);
+    const float inv_l = 1.0f / l_run[r];
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt)
+      *reinterpret_cast<float2*>(o + 8 * dt + 2 * qd) =
+          make_float2(oacc[dt][2 * r] * inv_l, oacc[dt][2 * r + 1] * inv_l);
+  }
+}
+
 // ---- clustered decode pass ---------------------------------------------------
 // One decode token per sequence (n = 1) with RoPE, the cache append, the split
 // pass and the combine in ONE launch: a cluster of CS CTAs per (sequence, KV
@@ -1217,6 +1413,39 @@ cudaError_t launch_split_pipe(const float* q, const __half* k_cache, const __hal
                             scale, nsplit, rows_total, pa, pm, pl);
 }
 
+// Prefill chunks of >= kFaMinRows query rows per sequence take the 16-row tile
+// pass; OBN_ATTN_FA=0 keeps them on split + combine. Read once per process.
+bool attn_fa_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("OBN_ATTN_FA");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+template <int G>
+cudaError_t launch_prefill_fa(const float* q, const __half* k_cache, const __half* v_cache, int B,
+                              int n, int H, int Hkv, int S_max, int seq_len,
+                              const int* pos_dev, float scale, float* out, cudaStream_t s) {
+  const size_t smem = static_cast<size_t>(2) * 2 * kFaKeys * kFaStride * 2;
+  auto kern = k_attn_prefill_fa<G>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((n + kFaRows - 1) / kFaRows), Hkv, B);
+  cfg.blockDim = dim3(32 * G);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, q, k_cache, v_cache, n, H, Hkv, S_max, seq_len, pos_dev,
+                            scale, out);
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl_attn(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s,
                             Args... args) {
@@ -1357,6 +1586,16 @@ cudaError_t attention_impl(const float* q, const __half* k_cache, const __half* 
 #undef OBN_CL
   }
   cudaError_t e;
+  // Prefill chunks: the 16-row tile pass, no combine.
+  if (!rope && n >= kFaMinRows && attn_fa_enabled()) {
+    switch (G) {
+      case 1: return launch_prefill_fa<1>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, out, s);
+      case 2: return launch_prefill_fa<2>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, out, s);
+      case 4: return launch_prefill_fa<4>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, out, s);
+      case 8: return launch_prefill_fa<8>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, out, s);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   const bool pipe = !rope && attn_pipe_enabled() &&
                     reinterpret_cast<uintptr_t>(q) % 16 == 0 &&
                     static_cast<long long>(B) * n * Hkv * nsplit >=

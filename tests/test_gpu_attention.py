@@ -58,7 +58,11 @@ def test_rope_kv_append(B, n, H, Hkv, pos):
                                          # causal prefill with empty items, G = 8 and G = 1)
                                          (64, 1, 20, 5, 2048), (8, 1, 20, 5, 1900),
                                          (1, 300, 20, 5, 600), (20, 1, 32, 4, 1100),
-                                         (3, 40, 8, 8, 2000)])
+                                         (3, 40, 8, 8, 2000),
+                                         # >= 16 new rows: the 16-row prefill tile pass, G = 1, 2,
+                                         # 4, 8, ragged last tiles, an empty cache (S = n)
+                                         (2, 33, 16, 8, 100), (1, 64, 32, 4, 64),
+                                         (2, 17, 20, 5, 17), (1, 512, 20, 5, 512)])
 def test_attention_matches_oracle(B, n, H, Hkv, S):
     torch = need_cuda()
     S_max = S + 3
