@@ -631,6 +631,14 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                 tmem_ld32(taddr + c * 32, v);
               else
                 tmem_ld16(taddr + c * 16, v);
+              const size_t o0 = static_cast<size_t>(tok0 + c * kCols) * M + m;
+              // y += val: every load of the chunk issues before its first store (a
+              // load after a store to y would wait for the one before it)
+              float yv[K_ == 2 ? kCols : 1];
+              if constexpr (K_ == 2) {
+#pragma unroll
+                for (int j = 0; j < kCols; ++j) yv[j] = y[o0 + static_cast<size_t>(j) * M];
+              }
               int qs_v[kCols];
               float sx_v[kCols];
 #pragma unroll
@@ -644,7 +652,6 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                 xr[k] = xr[k + 1];
               }
               tmem_ld_wait();
-              const size_t o0 = static_cast<size_t>(tok0 + c * kCols) * M + m;
 #pragma unroll
               for (int j = 0; j < kCols; ++j) {
                 const int d = static_cast<int>(v[j]) - qs_v[j];
@@ -656,7 +663,7 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm(const __grid_constant__ CU
                   const float val = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx_v[j])
                                                : __fmul_rn(fd, __fmul_rn(sw, sx_v[j]));
                   if constexpr (K_ == 2)
-                    y[o] = __fadd_rn(y[o], val);
+                    y[o] = __fadd_rn(yv[j], val);
                   else
                     y[o] = val;
                 }
@@ -1279,8 +1286,21 @@ __global__ __launch_bounds__(kThreads, 1) void k_gemm_sk(const __grid_constant__
             y[static_cast<size_t>(col) * Mh + (m >> 1)] = __fmul_rn(gate_act(K_ - 3, g), u);
         }
       } else if (j0 + 8 <= N) {
+        if constexpr (K_ == 2) {  // y += val: the 8 loads first, then the stores
+          float yv[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) put(c);
+          for (int c = 0; c < 8; ++c) yv[c] = y[static_cast<size_t>(j0 + c) * M + m];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const float fd = static_cast<float>(sum[c]);
+            const float val = gemv_order ? __fmul_rn(__fmul_rn(fd, sw), sx[c])
+                                         : __fmul_rn(fd, __fmul_rn(sw, sx[c]));
+            y[static_cast<size_t>(j0 + c) * M + m] = __fadd_rn(yv[c], val);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) put(c);
+        }
       } else {
         for (int c = 0; c < 8 && j0 + c < N; ++c) put(c);
       }
