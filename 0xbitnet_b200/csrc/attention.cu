@@ -103,6 +103,52 @@ __global__ __launch_bounds__(256) void k_rope_kv_append(const float* __restrict_
   }
 }
 
+// The same append, one CTA per token row: the row's d / 2 RoPE angles are
+// computed once (rope_angle, as above) and shared by all its q and k heads, so a
+// row of H + Hkv rotated heads costs d / 2 pow / sincos calls instead of
+// (H + Hkv) d / 2. Same values, same stores.
+constexpr int kRopeRowMaxHalf = 256;  // d <= 512
+
+__global__ __launch_bounds__(256) void k_rope_kv_append_row(
+    const float* __restrict__ qkv, int n, int H, int Hkv, int d, int pos,
+    const int* __restrict__ pos_dev, float theta_base, float* __restrict__ q_out,
+    __half* __restrict__ k_cache, __half* __restrict__ v_cache, int S_max) {
+  __shared__ float s_c[kRopeRowMaxHalf], s_s[kRopeRowMaxHalf];
+  // No early launch of dependents (as k_rope_kv_append).
+  pdl_wait();
+  const size_t r = blockIdx.x;  // token row b * n + t
+  const int t = static_cast<int>(r % n);
+  const size_t b = r / n;
+  const int half = d >> 1;
+  const int slots = H + 2 * Hkv;
+  const int p = (pos_dev ? *pos_dev : pos) + t;
+  if (p < 0 || p >= S_max) return;  // a device-side position past the cache writes nothing
+  for (int i = threadIdx.x; i < half; i += blockDim.x)
+    rope_angle(i, d, p, theta_base, &s_c[i], &s_s[i]);
+  __syncthreads();
+  const float* row = qkv + r * static_cast<size_t>(slots) * d;
+  for (int e = threadIdx.x; e < slots * half; e += blockDim.x) {
+    const int j = e / half, i = e - j * half;  // head slot: q heads, k heads, v heads
+    const float* src = row + static_cast<size_t>(j) * d + 2 * i;
+    const float x0 = src[0], x1 = src[1];
+    if (j >= H + Hkv) {  // v: stored as is
+      __half* dst = v_cache + ((b * S_max + p) * Hkv + (j - H - Hkv)) * d + 2 * i;
+      *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(x0, x1);
+      continue;
+    }
+    float y0, y1;
+    rope_rotate(x0, x1, s_c[i], s_s[i], &y0, &y1);
+    if (j < H) {
+      float* dst = q_out + (r * H + j) * d + 2 * i;
+      dst[0] = y0;
+      dst[1] = y1;
+    } else {
+      __half* dst = k_cache + ((b * S_max + p) * Hkv + (j - H)) * d + 2 * i;
+      *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(y0, y1);
+    }
+  }
+}
+
 // 16-byte global -> shared copy that does not hold a register (cp.async, L2 only).
 OBN_DEVINL void cp_async16(void* smem_dst, const void* gmem_src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
@@ -1537,6 +1583,12 @@ cudaError_t launch_decode_cl(const float* qkv, __half* k_cache, __half* v_cache,
 cudaError_t launch_rope_kv_append(const float* qkv, int B, int n, int H, int Hkv, int d, int pos,
                                   float theta_base, float* q_out, __half* k_cache,
                                   __half* v_cache, int S_max, cudaStream_t s, const int* pos_dev) {
+  // Many rows (prefill chunks): the per-row form. Fewer rows (decode batches) keep
+  // one thread per pair, whose short chains finish sooner than a row's loop.
+  if (d / 2 <= kRopeRowMaxHalf && B * n >= num_sms_cached())
+    return launch_pdl_attn(k_rope_kv_append_row, dim3(static_cast<unsigned>(B * n)), dim3(256), s,
+                           qkv, n, H, Hkv, d, pos, pos_dev, theta_base, q_out, k_cache, v_cache,
+                           S_max);
   const size_t total = static_cast<size_t>(B) * n * (H + 2 * Hkv) * (d / 2);
   const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
   return launch_pdl_attn(k_rope_kv_append, dim3(blocks), dim3(256), s, qkv, n, H, Hkv, d, pos,

@@ -25,7 +25,9 @@ def att():
 D = 128
 
 
-@pytest.mark.parametrize("B,n,H,Hkv,pos", [(2, 3, 20, 5, 100), (1, 1, 8, 8, 0), (3, 1, 16, 2, 2000)])
+@pytest.mark.parametrize("B,n,H,Hkv,pos", [(2, 3, 20, 5, 100), (1, 1, 8, 8, 0), (3, 1, 16, 2, 2000),
+                                            # >= one row per SM: one CTA per row, angles shared
+                                            (1, 300, 20, 5, 100), (2, 160, 16, 2, 1500)])
 def test_rope_kv_append(B, n, H, Hkv, pos):
     torch = need_cuda()
     S_max = pos + n + 5
@@ -36,7 +38,8 @@ def test_rope_kv_append(B, n, H, Hkv, pos):
     q = att().rope_kv_append(torch.from_numpy(qkv).cuda(), cache, H, n, 500000.0)
     q = q.cpu().numpy()
     kc, vc = cache.k.cpu().numpy(), cache.v.cpu().numpy()
-    tol = 1e-5 if pos < 200 else 1e-3  # theta = pos * base^(-2i/D): pow's last bit, scaled by pos
+    # theta = pos * base^(-2i/D): pow's last bit, scaled by the largest position
+    tol = 1e-5 if pos + n < 200 else 1e-3
     for b in range(B):
         rows = qkv[b * n:(b + 1) * n]
         qr = orc.rope(rows[:, :H * D], H, D, pos, 500000.0)
