@@ -869,21 +869,26 @@ constexpr int kFaKeys = 64;      // keys per block
 constexpr int kFaMinRows = 16;   // query rows per sequence from which prefill uses it
 constexpr int kFaStride = kAttnHeadDim + 8;  // halves per smem K / V row
 
-template <int G>
-__global__ __launch_bounds__(32 * G) void k_attn_prefill_fa(
+// KS = 2 (G <= 4): two warps per head, the first taking the even key blocks and
+// the second the odd ones, their running max / sum / O merged at the end, which
+// halves the chain of the tiles that see the most keys. Tiles are issued from
+// the last (longest) one down.
+template <int G, int KS>
+__global__ __launch_bounds__(32 * G * KS) void k_attn_prefill_fa(
     const float* __restrict__ q, const __half* __restrict__ k_cache,
     const __half* __restrict__ v_cache, int n, int H, int Hkv, int S_max, int seq_len,
     const int* __restrict__ pos_dev, float scale, float* __restrict__ out) {
   constexpr int D = kAttnHeadDim;
-  constexpr int NT = 32 * G;  // threads
-  static_assert(D == 128 && G >= 1 && G <= 8, "tile shape");
+  constexpr int NT = 32 * G * KS;  // threads
+  static_assert(D == 128 && G >= 1 && G <= 8 && (KS == 1 || KS == 2), "tile shape");
   extern __shared__ __align__(16) unsigned char smem[];
-  __half* sKV = reinterpret_cast<__half*>(smem);  // [2 stages][K, V][kFaKeys][kFaStride]
+  __half* sKV = reinterpret_cast<__half*>(smem);  // [2 stages][KS blocks][K, V][kFaKeys][kFaStride]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int grp = lane >> 2, qd = lane & 3;
-  const int t0 = blockIdx.x * kFaRows, kvh = blockIdx.y;
+  const int hw = warp % G, kp = warp / G;  // head within the group, key-block parity
+  const int t0 = (gridDim.x - 1 - blockIdx.x) * kFaRows, kvh = blockIdx.y;
   const size_t b = blockIdx.z;
-  const int h = kvh * G + warp;  // this warp's query head
+  const int h = kvh * G + hw;  // this warp's query head
   pdl_launch_dependents();
   pdl_wait();
   if (pos_dev) seq_len = min(*pos_dev + n, S_max);
@@ -912,13 +917,15 @@ __global__ __launch_bounds__(32 * G) void k_attn_prefill_fa(
       split_h2(a3.x, a3.y, &qh[ks][3], &ql[ks][3]);
     }
   }
-  // K and V rows of block kb into stage kb & 1 (rows at or past kmax zero-filled)
-  auto load_block = [&](int kb) {
-    __half* sK = sKV + (kb & 1) * 2 * kFaKeys * kFaStride;
-    __half* sV = sK + kFaKeys * kFaStride;
-    const int key0 = kb * kFaKeys;
-    for (int i = tid; i < kFaKeys * (D / 8); i += NT) {
-      const int row = i >> 4, pc = i & 15, key = key0 + row;
+  // K and V rows of blocks KS it .. KS it + KS - 1 into stage it & 1 (rows at or
+  // past kmax zero-filled)
+  auto load_block = [&](int it) {
+    __half* sK0 = sKV + (it & 1) * KS * 2 * kFaKeys * kFaStride;
+    for (int i = tid; i < KS * kFaKeys * (D / 8); i += NT) {
+      const int j = i / (kFaKeys * (D / 8)), ii = i - j * (kFaKeys * (D / 8));
+      __half* sK = sK0 + j * 2 * kFaKeys * kFaStride;
+      __half* sV = sK + kFaKeys * kFaStride;
+      const int row = ii >> 4, pc = ii & 15, key = (KS * it + j) * kFaKeys + row;
       const size_t g = key < kmax ? ((b * S_max + key) * Hkv + kvh) * D + pc * 8
                                   : ((b * S_max) * Hkv + kvh) * D;
       const uint32_t nbytes = key < kmax ? 16u : 0u;
@@ -937,16 +944,22 @@ __global__ __launch_bounds__(32 * G) void k_attn_prefill_fa(
     for (int i = 0; i < 4; ++i) oacc[dt][i] = 0.0f;
   const int lim0 = seq_len - n + t0 + grp;  // last key row grp may see (row grp + 8: + 8)
   const bool row_ok[2] = {t0 + grp < n, t0 + grp + 8 < n};
-  if (nkb > 0) load_block(0);
-  for (int kb = 0; kb < nkb; ++kb) {
-    if (kb + 1 < nkb) {
-      load_block(kb + 1);
-      cp_async_wait_group<1>();  // block kb landed (this thread's pieces)
+  const int nit = (nkb + KS - 1) / KS;
+  if (nit > 0) load_block(0);
+  for (int it = 0; it < nit; ++it) {
+    if (it + 1 < nit) {
+      load_block(it + 1);
+      cp_async_wait_group<1>();  // iteration it's blocks landed (this thread's pieces)
     } else {
       cp_async_wait_group<0>();
     }
-    __syncthreads();  // every thread's pieces of block kb
-    const __half* sK = sKV + (kb & 1) * 2 * kFaKeys * kFaStride;
+    __syncthreads();  // every thread's pieces of iteration it
+    const int kb = KS * it + kp;  // this warp's block
+    if (kb >= nkb) {
+      __syncthreads();
+      continue;
+    }
+    const __half* sK = sKV + ((it & 1) * KS + kp) * 2 * kFaKeys * kFaStride;
     const __half* sV = sK + kFaKeys * kFaStride;
     const int key0 = kb * kFaKeys;
     // S = Q K^T: sacc[nt] holds keys key0 + 8 nt + 2 qd, + 1 of rows grp, grp + 8
@@ -1032,7 +1045,37 @@ __global__ __launch_bounds__(32 * G) void k_attn_prefill_fa(
         mma_16816(oacc[2 * d2 + 1], pl, vb[2], vb[3]);
       }
     }
-    __syncthreads();  // stage kb & 1 is read; the next load may overwrite it
+    __syncthreads();  // stage it & 1 is read; the next load may overwrite it
+  }
+  if constexpr (KS == 2) {
+    // the odd-block warps hand their (max, sum, O) to the even-block warps of the
+    // same head through the (now idle) stage buffers; those merge them
+    float* xch = reinterpret_cast<float*>(smem) + (hw * 32 + lane) * 68;
+    if (kp == 1) {
+      xch[0] = m_run[0];
+      xch[1] = m_run[1];
+      xch[2] = l_run[0];
+      xch[3] = l_run[1];
+#pragma unroll
+      for (int dt = 0; dt < 16; ++dt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) xch[4 + 4 * dt + i] = oacc[dt][i];
+    }
+    __syncthreads();
+    if (kp == 1) return;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const float m1 = xch[r], l1 = xch[2 + r];
+      const float mm = fmaxf(m_run[r], m1);
+      const float a0 = expf(m_run[r] - mm), a1 = expf(m1 - mm);
+      l_run[r] = __fadd_rn(__fmul_rn(l_run[r], a0), __fmul_rn(l1, a1));
+#pragma unroll
+      for (int dt = 0; dt < 16; ++dt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          oacc[dt][2 * r + e] =
+              __fadd_rn(__fmul_rn(oacc[dt][2 * r + e], a0), __fmul_rn(xch[4 + 4 * dt + 2 * r + e], a1));
+    }
   }
   // outputs: O / l for the tile's rows below n
 #pragma unroll
@@ -1469,18 +1512,18 @@ bool attn_fa_enabled() {
   return on;
 }
 
-template <int G>
-cudaError_t launch_prefill_fa(const float* q, const __half* k_cache, const __half* v_cache, int B,
+template <int G, int KS>
+cudaError_t launch_prefill_fa_ks(const float* q, const __half* k_cache, const __half* v_cache, int B,
                               int n, int H, int Hkv, int S_max, int seq_len,
                               const int* pos_dev, float scale, float* out, cudaStream_t s) {
-  const size_t smem = static_cast<size_t>(2) * 2 * kFaKeys * kFaStride * 2;
-  auto kern = k_attn_prefill_fa<G>;
+  const size_t smem = static_cast<size_t>(2) * KS * 2 * kFaKeys * kFaStride * 2;
+  auto kern = k_attn_prefill_fa<G, KS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>((n + kFaRows - 1) / kFaRows), Hkv, B);
-  cfg.blockDim = dim3(32 * G);
+  cfg.blockDim = dim3(32 * G * KS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -1490,6 +1533,15 @@ cudaError_t launch_prefill_fa(const float* q, const __half* k_cache, const __hal
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, q, k_cache, v_cache, n, H, Hkv, S_max, seq_len, pos_dev,
                             scale, out);
+}
+
+// Two warps per head while the CTA's registers allow it (G <= 4).
+template <int G>
+cudaError_t launch_prefill_fa(const float* q, const __half* k_cache, const __half* v_cache, int B,
+                              int n, int H, int Hkv, int S_max, int seq_len,
+                              const int* pos_dev, float scale, float* out, cudaStream_t s) {
+  return launch_prefill_fa_ks<G, (G <= 4 ? 2 : 1)>(q, k_cache, v_cache, B, n, H, Hkv, S_max,
+                                                   seq_len, pos_dev, scale, out, s);
 }
 
 template <typename... KArgs, typename... Args>
