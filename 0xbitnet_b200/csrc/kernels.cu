@@ -316,7 +316,11 @@ __global__ __launch_bounds__(256) void k_rmsnorm_quant_reg(const float* __restri
 // PDL wait.
 constexpr int kTokThreads = 64;
 constexpr int kTokPerCta = 4;
-constexpr int kQuantFewTokens = 256;  // up to here one CTA per token
+// Up to here one CTA per token (measured on B200: rows of 2560 columns 2.9 / 3.8
+// against 3.6 / 4.1 us at 384 / 512 tokens, the 64-thread form ahead from 1024;
+// wide rows take the 128-thread form above 256 tokens at every count measured).
+constexpr int kQuantFewTokens = 640;
+constexpr int kQuantFewTokensWide = 256;  // rows of kWideMinCols columns or more
 
 OBN_DEVINL void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
@@ -1185,7 +1189,12 @@ cudaError_t launch_rmsnorm_quant(const float* x, const float* norm_w, float eps,
                                  int8_t* q, float* scales, int32_t* qsum, cudaStream_t s) {
   // Few tokens (decode): one 256-thread CTA per token keeps each token's chain short.
   const int ept = (d + 255) / 256;
-  if (n <= kQuantFewTokens) {
+  static const int few = [] {  // OBN_QUANT_FEW=<tokens> moves the switch (A/B measurements)
+    const char* e = std::getenv("OBN_QUANT_FEW");
+    const int v = e ? std::atoi(e) : 0;
+    return v;
+  }();
+  if (n <= (few > 0 ? few : d >= kWideMinCols ? kQuantFewTokensWide : kQuantFewTokens)) {
     if (ept <= 2) return rmsnorm_quant_ept<2>(x, norm_w, eps, n, d, q, scales, qsum, s);
     if (ept <= 4) return rmsnorm_quant_ept<4>(x, norm_w, eps, n, d, q, scales, qsum, s);
     if (ept <= 8) return rmsnorm_quant_ept<8>(x, norm_w, eps, n, d, q, scales, qsum, s);
