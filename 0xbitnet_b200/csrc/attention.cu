@@ -127,24 +127,40 @@ __global__ __launch_bounds__(256) void k_rope_kv_append_row(
     rope_angle(i, d, p, theta_base, &s_c[i], &s_s[i]);
   __syncthreads();
   const float* row = qkv + r * static_cast<size_t>(slots) * d;
-  for (int e = threadIdx.x; e < slots * half; e += blockDim.x) {
-    const int j = e / half, i = e - j * half;  // head slot: q heads, k heads, v heads
-    const float* src = row + static_cast<size_t>(j) * d + 2 * i;
-    const float x0 = src[0], x1 = src[1];
-    if (j >= H + Hkv) {  // v: stored as is
-      __half* dst = v_cache + ((b * S_max + p) * Hkv + (j - H - Hkv)) * d + 2 * i;
-      *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(x0, x1);
-      continue;
+  const int items = slots * half;
+  // eight of this thread's pairs per pass, their loads issued together
+  for (int e0 = threadIdx.x; e0 < items; e0 += 8 * blockDim.x) {
+    float2 xv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e < items) {
+        const int j = e / half, i = e - j * half;
+        const float* src = row + static_cast<size_t>(j) * d + 2 * i;
+        xv[u] = make_float2(src[0], src[1]);
+      }
     }
-    float y0, y1;
-    rope_rotate(x0, x1, s_c[i], s_s[i], &y0, &y1);
-    if (j < H) {
-      float* dst = q_out + (r * H + j) * d + 2 * i;
-      dst[0] = y0;
-      dst[1] = y1;
-    } else {
-      __half* dst = k_cache + ((b * S_max + p) * Hkv + (j - H)) * d + 2 * i;
-      *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(y0, y1);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e >= items) break;
+      const int j = e / half, i = e - j * half;  // head slot: q heads, k heads, v heads
+      const float x0 = xv[u].x, x1 = xv[u].y;
+      if (j >= H + Hkv) {  // v: stored as is
+        __half* dst = v_cache + ((b * S_max + p) * Hkv + (j - H - Hkv)) * d + 2 * i;
+        *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(x0, x1);
+        continue;
+      }
+      float y0, y1;
+      rope_rotate(x0, x1, s_c[i], s_s[i], &y0, &y1);
+      if (j < H) {
+        float* dst = q_out + (r * H + j) * d + 2 * i;
+        dst[0] = y0;
+        dst[1] = y1;
+      } else {
+        __half* dst = k_cache + ((b * S_max + p) * Hkv + (j - H)) * d + 2 * i;
+        *reinterpret_cast<__half2*>(dst) = __floats2half2_rn(y0, y1);
+      }
     }
   }
 }
