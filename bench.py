@@ -1162,6 +1162,17 @@ def run_case(spec: str):
         torch.cuda.synchronize()
         print(f"case attn B={B}: ok")
         return
+    if name == "attnpf":  # prefill attention: one sequence, B new rows on an empty cache, 3 runs
+        att = importlib.import_module("0xbitnet_b200.attention")
+        cache = att.KVCache(1, B, 5, 128)
+        cache.k.normal_()
+        cache.v.normal_()
+        q = torch.randn(B, 20 * 128, device="cuda")
+        for _ in range(3):
+            att.attention(q, cache, 20, B, B)
+        torch.cuda.synchronize()
+        print(f"case attnpf n={B}: ok")
+        return
     if name == "gateup":  # merged 6912 x 2560 gate|up layer, ReLU^2 x up in the matmul epilogue
         M, K = synth.SHAPES_2B["gate"]
         layers = []
