@@ -872,7 +872,8 @@ __global__ __launch_bounds__(kAttnThreads, kPipeCtasPerSm) void k_attn_split_pip
 // For chunks of many new tokens (n >= kFaMinRows) the split pass would read every
 // 128-key chunk once per query row. k_attn_prefill_fa gives a CTA 16 consecutive
 // query rows of one sequence and one KV head; warp w takes query head
-// kvh * G + w for those rows, so the G warps share every K / V block. Keys stream
+// kvh * G + w % G for those rows (and, with KS = 2, the key blocks of parity
+// w / G), so all warps share every K / V block. Keys stream
 // in 64-key blocks (double-buffered 16-byte cp.async pieces); per block each
 // warp computes S = Q K^T (mma.sync m16n8k16, q split into binary16 hi + lo),
 // scales, masks the causal limit, updates its rows' running max and sum (online
