@@ -1707,8 +1707,10 @@ cudaError_t attention_impl(const float* q, const __half* k_cache, const __half* 
 #undef OBN_CL
   }
   cudaError_t e;
-  // Prefill chunks: the 16-row tile pass, no combine.
-  if (!rope && n >= kFaMinRows && attn_fa_enabled()) {
+  // Prefill chunks: the 16-row tile pass, no combine (its q loads and output stores are
+  // 8-byte pairs; other alignments run split + combine).
+  if (!rope && n >= kFaMinRows && attn_fa_enabled() &&
+      ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) % 8) == 0) {
     switch (G) {
       case 1: return launch_prefill_fa<1>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, out, s);
       case 2: return launch_prefill_fa<2>(q, k_cache, v_cache, B, n, H, Hkv, S_max, seq_len, pos_dev, scale, out, s);
