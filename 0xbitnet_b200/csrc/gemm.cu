@@ -42,7 +42,9 @@
 // from L2 once per 128 rows, and at 8192 tokens that L2 -> SM stream
 // (~10 TB/s) is what held the MMA back. The odd CTA announces its codes and its
 // drained accumulators with relaxed remote arrivals; the even CTA's commits
-// reach both CTAs' barriers (multicast to the pair, no TMA multicast).
+// reach both CTAs' barriers (multicast to the pair, no TMA multicast). Tiles of
+// the last partial wave (or all of them, when their halves fit at once) run as
+// two 128-token units each (tile_unit below).
 #include <cuda.h>
 
 #include <cstdlib>
