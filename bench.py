@@ -64,7 +64,8 @@ def parse_args():
                    help="config-4 tensor-parallel prefill tokens when run on N > 1 GPUs (0 skips)")
     p.add_argument("--case", type=str, default=None,
                    help="SHAPE:B — run a few forwards of one 2B shape (or of 'all' five in "
-                        "turn; or 'lmhead' / 'attn' / 'gateup' / 'quant' / 'mmarate') at B tokens and exit (a "
+                        "turn; or 'lmhead' / 'attn' / 'attnpf' / 'attndec' / 'decoder' / 'prefill' / "
+                        "'prefilltrace' / 'gateup' / 'quant' / 'mmarate') at B and exit (a "
                         "small, self-contained workload for ncu captures)")
     return p.parse_args()
 
@@ -1161,6 +1162,48 @@ def run_case(spec: str):
             att.attention(q, cache, 20, 1, 2048)
         torch.cuda.synchronize()
         print(f"case attn B={B}: ok")
+        return
+    if name == "prefilltrace":  # kernel timeline (CUPTI) of one B-token prompt through the model ABI
+        import re
+        import shutil
+        import tempfile
+
+        import numpy as np
+        from torch.profiler import ProfilerActivity, profile
+        W = importlib.import_module("0xbitnet_b200.gguf_writer")
+        ox = importlib.import_module("0xbitnet_b200.oxbitnet")
+        tmp = tempfile.mkdtemp(prefix="obn_gguf_")
+        try:
+            path = os.path.join(tmp, "bitnet2b.gguf")
+            toks, merges, bos, eos = W.synthetic_vocab(128256)
+            W.write_bitnet_model(path, W.BitNetShape(), toks, merges, bos, eos, seed=0, fast=True)
+            m = ox.BitNet.load_sync(path)
+            rng = np.random.default_rng(0)
+            prompt = [bos] + [int(x) for x in rng.integers(0, 128000, B - 1)]
+            m.forward(prompt, reset=True)
+            torch.cuda.synchronize()
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                m.forward(prompt, reset=True)
+                torch.cuda.synchronize()
+            ev = sorted((e for e in prof.events() if e.device_type.name == "CUDA"),
+                        key=lambda e: e.time_range.start)
+            kinds = {}
+            for i, e in enumerate(ev):
+                mt = re.search(r"(k_\w+)", e.name)
+                k = mt.group(1) if mt else e.name[:40]
+                end_prev = ev[i - 1].time_range.end if i else e.time_range.start
+                a = kinds.setdefault(k, [0, 0.0])
+                a[0] += 1
+                a[1] += e.time_range.end - end_prev  # end-to-end increment, us
+            span = (ev[-1].time_range.end - ev[0].time_range.start) if ev else 0
+            print(json.dumps({"prefilltrace": {
+                "tokens": B, "gpu_span_us": span,
+                "kernels": {k: {"launches": n, "end_increment_us": round(t, 1)}
+                            for k, (n, t) in sorted(kinds.items(), key=lambda x: -x[1][1])}}}),
+                flush=True)
+            del m
+        finally:
+            shutil.rmtree(tmp, ignore_errors=True)
         return
     if name == "attnpf":  # prefill attention: one sequence, B new rows on an empty cache, 3 runs
         att = importlib.import_module("0xbitnet_b200.attention")
